@@ -1,0 +1,360 @@
+"""Training-throughput benchmark: Mimir2 dense ~1.3B (24 x 2048, 16 Q / 4 KV heads of 128,
+SwiGLU 5632, vocab 65536), seq 4096, 4 sequences per GPU, prefix-LM mask with prompt length
+uniform in [0, 2048], FSDP2 bf16 compute / fp32 master weights, AdamATan2 (+EMA).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 run under ``torch.distributed.run`` (one rank per GPU).  Rank 0 prints one JSON
+line.  ``value`` is device-timed (CUDA events around exactly K steps, barrier + synchronize
+on both sides, max over ranks) with the step's inputs already on the device; ``e2e`` times
+the same K-step loop through the public training-step API including, every step, the
+pinned host->device copy of the batch and the device->host read of the loss.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+SEQ_LEN, SEQS_PER_GPU, VOCAB = 4096, 4, 65536
+MODEL = dict(n_layers=24, hidden_size=2048, num_heads=16, num_key_value_heads=4, expansion=4.125)
+METRIC = "train tokens/sec (box, device-timed, max over ranks) at 1/2/4/8 B200; MFU"
+BASELINE_VALUE = None  # the reference publishes no throughput number
+
+
+def arch_dict(kv_heads=4):
+    return dict(name="mimir2", max_seq_len=SEQ_LEN, n_layers=MODEL["n_layers"], hidden_size=MODEL["hidden_size"],
+                num_heads=MODEL["num_heads"], num_key_value_heads=kv_heads, expansion=MODEL["expansion"],
+                init_type="lecun_normal", norm_type="pre", norm_eps=1e-6, pos_emb_type="rope", rope_theta=10000.0,
+                recurrence_mode="looped", half_layers=False, H_override={"n_layers": 0}, H_cycles=1, L_cycles=1,
+                bp_min_steps=2, bp_max_steps=2, bp_warmup_ratio=0.0, fwd_bwd_dtype="bfloat16", vocab_size=VOCAB)
+
+
+# ---------------------------------------------------------------------------------------- batch
+def synthetic_batch(rank: int, step: int):
+    """Host batch in the corpus format: packed inputs/labels/positions + prefix-LM metadata."""
+    rng = np.random.default_rng(1_000_003 * rank + step)
+    T = SEQ_LEN * SEQS_PER_GPU
+    prefix = rng.integers(0, 2049, size=SEQS_PER_GPU).astype(np.int32)
+    inputs = rng.integers(0, VOCAB, size=T).astype(np.int32)
+    labels = rng.integers(0, VOCAB, size=T).astype(np.int32)
+    for s in range(SEQS_PER_GPU):
+        labels[s * SEQ_LEN: s * SEQ_LEN + max(int(prefix[s]) - 1, 0)] = -100  # supervise the answer only
+    positions = np.tile(np.arange(SEQ_LEN, dtype=np.int32), SEQS_PER_GPU)
+    causal = (SEQ_LEN - prefix).astype(np.int32)
+    pad = lambda a: np.pad(a, (0, T - a.shape[0]))
+    cu = np.pad(np.cumsum(np.full(SEQS_PER_GPU, SEQ_LEN, np.int32)), (1, T - SEQS_PER_GPU - 1)).astype(np.int32)
+    tensors = dict(inputs=inputs, labels=labels, position_ids=positions, prefix_lens=pad(prefix),
+                   causal_lens=pad(causal), cu_seqlens=cu)
+    scalars = dict(total_seqlen=T, numseqs=SEQS_PER_GPU, max_seqlen_prefix=int(prefix.max()),
+                   max_seqlen_causal=int(causal.max()), max_seqlen_all=SEQ_LEN)
+    host = {k: torch.from_numpy(v).pin_memory() if torch.cuda.is_available() else torch.from_numpy(v)
+            for k, v in tensors.items()}
+    return host, scalars
+
+
+def attention_pairs(host) -> int:
+    """Visible (query, key) pairs of the prefix-LM mask in one local batch."""
+    total = 0
+    for s in range(SEQS_PER_GPU):
+        p = int(host["prefix_lens"][s])
+        L = SEQ_LEN
+        total += p * p + sum(r + 1 for r in range(p, L)) if p < L else p * p
+    return total
+
+
+def model_flops_per_step(host, kv_heads) -> float:
+    d, H, hd, F = MODEL["hidden_size"], MODEL["num_heads"], 128, 5632
+    per_layer = d * (2 * H + 2 * kv_heads) * hd + H * hd * d + d * 2 * F + F * d
+    matmul_params = MODEL["n_layers"] * per_layer + d * VOCAB
+    T = SEQ_LEN * SEQS_PER_GPU
+    dense = 6.0 * matmul_params * T
+    attn_fwd = 4.0 * hd * H * attention_pairs(host) * MODEL["n_layers"]
+    return dense + 3.0 * attn_fwd
+
+
+# ---------------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        self.path = os.path.join("/tmp", f"mimir_clocks_{os.getpid()}.csv")
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(gpu_index)], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------------------------------- distributed
+def init_distributed(gpus: int):
+    if "RANK" not in os.environ:
+        if gpus != 1:
+            raise SystemExit("--gpus N > 1 must be launched with torch.distributed.run")
+        os.environ.update(RANK="0", WORLD_SIZE="1", LOCAL_RANK="0", MASTER_ADDR="127.0.0.1",
+                          MASTER_PORT=str(29500 + os.getpid() % 1000))
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    from datetime import timedelta
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=600))
+    return rank, world, local
+
+
+def device_batch(host, scalars, device, wrap):
+    batch = {k: v.to(device, non_blocking=True) for k, v in host.items()}
+    batch.update({k: wrap(torch.tensor(v)) for k, v in scalars.items()})
+    return batch
+
+
+def max_over_ranks(x: float) -> float:
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed_loop(run_step, batches, steps: int):
+    """CUDA-event time of exactly `steps` calls (inputs already on device), max over ranks."""
+    dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        run_step(batches[i % len(batches)])
+    end.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    return max_over_ranks(start.elapsed_time(end) / 1000.0)
+
+
+# ---------------------------------------------------------------------------------------- our arm
+def run_ours(args, rank, world, local):
+    sys.path.insert(0, ROOT)
+    from mimir_b200.config.schema import PretrainConfig
+    from mimir_b200.models.common import wrap_tensor
+    from mimir_b200.ops._ext import ext, launch_count
+    from mimir_b200.optim.schedules import update_lr
+    from mimir_b200.train.setup import create_model_and_optimizer, make_train_state
+    from mimir_b200.train.steps import train_accumulated_batches
+
+    ext()  # fail loudly if the extension is missing
+    device = torch.device("cuda", local)
+    arch = arch_dict(kv_heads=MODEL["num_key_value_heads"])
+    vocab = arch.pop("vocab_size")
+    config = PretrainConfig(arch=arch, data=dict(path="synthetic"), global_batch_size=SEQ_LEN * SEQS_PER_GPU * world,
+                            epochs=1, lr=3e-4, lr_warmup_steps=0, lr_min_ratio=1.0, weight_decay=0.1, beta1=0.9,
+                            beta2=0.95, ema=0.9999, distributed_strategy="fsdp", lr_auto=False)
+    torch.manual_seed(0)
+    model, carry, optim = create_model_and_optimizer(config, {"vocab_size": vocab, "max_seq_len": SEQ_LEN}, device)
+    state = make_train_state(config, model, carry, optim, total_steps=10_000, device=device)
+    hosts = [synthetic_batch(rank, i) for i in range(2)]
+    dev_batches = [device_batch(h, s, device, wrap_tensor) for h, s in hosts]
+
+    def step(batch):
+        state.step += 1
+        update_lr(config, state)
+        metrics, _ = train_accumulated_batches(config, rank, state, [batch])
+        return metrics
+
+    for i in range(args.warmup):
+        step(dev_batches[i % 2])
+    torch.cuda.synchronize()
+    launches0 = launch_count()
+    clocks = ClockSampler(local)
+    seconds = timed_loop(step, dev_batches, args.steps)
+    clock_info = clocks.stop()
+    launches = (launch_count() - launches0) // max(args.steps, 1) * args.steps
+
+    # End to end through the public step API: H2D of each step's batch + D2H of its loss.
+    h2d = sum(t.numel() * t.element_size() for t in hosts[0][0].values())
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    losses = []
+    for i in range(args.steps):
+        host, scalars = hosts[i % 2]
+        metrics = step(device_batch(host, scalars, device, wrap_tensor))
+        losses.append((metrics["loss"][0] / metrics["loss"][1]).item())
+    torch.cuda.synchronize()
+    e2e_seconds = max_over_ranks(time.perf_counter() - t0)
+    flops = model_flops_per_step(hosts[0][0], MODEL["num_key_value_heads"])
+    return emit(args, world, seconds, e2e_seconds, h2d, 4, flops, clock_info, launches, impl="ours",
+                extra={"final_loss": losses[-1]})
+
+
+# ---------------------------------------------------------------------------------------- reference arm
+def run_reference(args, rank, world, local):
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "mimir")):
+        print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
+        return
+    sys.path.insert(0, ref)
+    from mimir.model import Mimir2 as RefMimir2
+    from mimir.model.accelerator import set_accelerator_type
+    from mimir.model.adam_atan2 import AdamATan2 as RefAdam
+    from mimir.model.common import wrap_tensor
+    from mimir.model.lm_head import LMHead as RefHead
+    from mimir.training.config import PretrainConfig as RefConfig
+    from mimir.training.distributed import apply_fsdp, fsdp_wrap_modules
+    from mimir.training.schedules import update_lr
+    from mimir.training.state import TrainState
+    from mimir.training.steps import train_accumulated_batches
+
+    # FlashAttention-4 (flash_attn.cute) is not installable offline, so the reference's own
+    # dense prefix-LM attention backend (accelerator "none") is the path that can run.
+    set_accelerator_type("none")
+    device = torch.device("cuda", local)
+    arch = arch_dict(kv_heads=None)  # the reference ties KV heads to Q heads
+    arch.pop("num_key_value_heads")
+    vocab = arch.pop("vocab_size")
+    compiled = os.environ.get("MIMIR_REF_COMPILE", "1") == "1"
+    config = RefConfig(arch=arch, data=dict(path="synthetic"), global_batch_size=SEQ_LEN * SEQS_PER_GPU * world,
+                       epochs=1, lr=3e-4, lr_warmup_steps=0, lr_min_ratio=1.0, weight_decay=0.1, beta1=0.9, beta2=0.95,
+                       ema=0.9999, distributed_strategy="fsdp", accelerator_type="sm100", lr_auto=False,
+                       compile_train_batch=compiled)
+    model_cfg = config.arch.model_dump() | {"vocab_size": vocab, "max_seq_len": SEQ_LEN} | config.data.model_dump() | {
+        "fwd_bwd_dtype": "bfloat16", "activation_checkpointing": "none"}
+    torch.manual_seed(0)
+    with torch.device(device):
+        model = RefHead(RefMimir2(model_cfg), model_cfg)
+    for buf in model.buffers():
+        dist.broadcast(buf, src=0)
+    for module in fsdp_wrap_modules(model, "transformer_block"):
+        apply_fsdp(module, torch.bfloat16)
+    apply_fsdp(model, torch.bfloat16)
+    optim = RefAdam(model.parameters(), lr=0.0, betas=(0.9, 0.95), weight_decay=0.1, ema=0.9999)
+    state = TrainState(model=model, carry=None, optim=optim, step=0, total_steps=10_000, fwd_bwd_dtype=torch.bfloat16,
+                       use_cuda_autocast=False)
+    hosts = [synthetic_batch(rank, i) for i in range(2)]
+    dev_batches = [device_batch(h, s, device, wrap_tensor) for h, s in hosts]
+
+    def step(batch):
+        state.step += 1
+        update_lr(config, state)
+        metrics, _ = train_accumulated_batches(config, rank, state, [batch], config.compile_train_batch,
+                                               bp_steps=2)
+        return metrics
+
+    for i in range(args.warmup):
+        step(dev_batches[i % 2])
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    seconds = timed_loop(step, dev_batches, args.steps)
+    clock_info = clocks.stop()
+    h2d = sum(t.numel() * t.element_size() for t in hosts[0][0].values())
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        host, scalars = hosts[i % 2]
+        metrics = step(device_batch(host, scalars, device, wrap_tensor))
+        (metrics["loss"][0] / metrics["loss"][1]).item()
+    torch.cuda.synchronize()
+    e2e_seconds = max_over_ranks(time.perf_counter() - t0)
+    flops = model_flops_per_step(hosts[0][0], MODEL["num_heads"])
+    extra = {"attention_backend": "reference dense prefix-LM SDPA (FA4 unavailable offline)",
+             "num_key_value_heads": MODEL["num_heads"], "torch_compile": compiled}
+    return emit(args, world, seconds, e2e_seconds, h2d, 4, flops, clock_info, None, impl="reference", extra=extra)
+
+
+# ---------------------------------------------------------------------------------------- output
+def emit(args, world, seconds, e2e_seconds, h2d_bytes, d2h_bytes, flops_per_step_per_rank, clocks, launches, impl,
+         extra=None):
+    tokens = SEQ_LEN * SEQS_PER_GPU * world * args.steps
+    value = tokens / seconds
+    e2e = tokens / e2e_seconds
+    ms = seconds / args.steps * 1000.0
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    achieved = flops_per_step_per_rank / (seconds / args.steps)
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": (value / BASELINE_VALUE) if BASELINE_VALUE else None, "dtype": "bf16",
+        "data": "synthetic uniform token ids, random-init weights",
+        "config": {"model": "Mimir2 dense ~1.3B (24x2048, 16Q/4KV heads x128, SwiGLU 5632, vocab 65536)",
+                   "global_batch": SEQ_LEN * SEQS_PER_GPU * world, "seq_len": SEQ_LEN, "micro_batch": SEQS_PER_GPU,
+                   "parallelism": f"fsdp{world}", "mask": "prefix-LM, prompt length uniform [0,2048]",
+                   "optimizer": "AdamATan2 + EMA", "l2": "inputs larger than L2 (weights+activations >> 126 MB)"},
+        "mfu": round(achieved / 2.25e15, 4),
+        "frac_of_measured_bf16": round(achieved / (peaks.get("bf16_tflops_sustained", 1422.4) * 1e12), 4),
+        "clocks": clocks,
+        "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d_bytes,
+                "d2h_bytes_per_step": d2h_bytes},
+        "impl": impl,
+    }
+    if launches is not None:
+        out["gpu_launches"] = launches
+    if extra:
+        out.update(extra)
+    if dist.get_rank() == 0:
+        print(json.dumps(out), flush=True)
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference" and not os.path.isdir(os.path.join(ROOT, "baseline", "_ref", "mimir")):
+        print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
+        return
+    rank, world, local = init_distributed(args.gpus)
+    try:
+        (run_reference if args.impl == "reference" else run_ours)(args, rank, world, local)
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

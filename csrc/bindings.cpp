@@ -1,0 +1,54 @@
+// Python bindings for the mimir_b200 sm_100a kernels (module mimir_b200._C).
+#include <torch/extension.h>
+
+// elementwise.cu
+std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, double eps);
+at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor rstd);
+at::Tensor swiglu_fwd(at::Tensor gu);
+at::Tensor swiglu_bwd(at::Tensor dp, at::Tensor gu);
+at::Tensor rope_qk(at::Tensor gqkv, at::Tensor cos_t, at::Tensor sin_t, at::Tensor pos, int64_t H, int64_t KV);
+void rope_qk_bwd(at::Tensor dq, at::Tensor dk, at::Tensor dv, at::Tensor cos_t, at::Tensor sin_t, at::Tensor pos,
+                 at::Tensor dgqkv, int64_t H, int64_t KV);
+std::vector<at::Tensor> attn_gate_bwd(at::Tensor dy, at::Tensor o, at::Tensor gqkv, at::Tensor dgqkv, int64_t H);
+at::Tensor attn_delta(at::Tensor d_o, at::Tensor o, int64_t H);
+// loss.cu
+std::vector<at::Tensor> ce_fwd(at::Tensor logits, at::Tensor labels);
+void ce_bwd_inplace(at::Tensor logits, at::Tensor lse, at::Tensor labels, at::Tensor gscale);
+// optim.cu
+void adam_atan2_multi(std::vector<at::Tensor> params, std::vector<at::Tensor> grads,
+                      c10::optional<std::vector<at::Tensor>> exp_avgs, std::vector<at::Tensor> exp_avg_sqs,
+                      c10::optional<std::vector<at::Tensor>> emas, std::vector<double> lrs, std::vector<double> bc1,
+                      std::vector<double> bc2_sqrt, double beta1, double beta2, double weight_decay, double ema_decay);
+// ngram.cu
+at::Tensor ngram_fwd(at::Tensor ids, at::Tensor pos, std::vector<at::Tensor> tables, std::vector<int64_t> orders,
+                     int64_t heads, int64_t buckets, at::ScalarType dtype);
+void ngram_bwd(at::Tensor dout, at::Tensor ids, at::Tensor pos, std::vector<at::Tensor> grads,
+               std::vector<int64_t> orders, int64_t heads, int64_t buckets);
+// fmha_fwd.cu
+std::vector<at::Tensor> fmha_plan(at::Tensor cu_seqlens, at::Tensor prefix_lens, int64_t numseqs, int64_t total_tokens,
+                                  bool is_causal);
+std::vector<at::Tensor> fmha_fwd(at::Tensor q_src, int64_t q_col, at::Tensor k_src, int64_t k_col, at::Tensor v_src,
+                                 int64_t v_col, c10::optional<at::Tensor> gate_src, int64_t gate_col, int64_t H,
+                                 int64_t KV, bool is_causal, at::Tensor cu_seqlens, at::Tensor prefix_lens,
+                                 int64_t numseqs, at::Tensor tiles, at::Tensor ntiles);
+int64_t fmha_status(at::Device dev);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "mimir_b200 hand-written sm_100a kernels";
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("rope_qk", &rope_qk);
+  m.def("rope_qk_bwd", &rope_qk_bwd);
+  m.def("attn_gate_bwd", &attn_gate_bwd);
+  m.def("attn_delta", &attn_delta);
+  m.def("ce_fwd", &ce_fwd);
+  m.def("ce_bwd_inplace", &ce_bwd_inplace);
+  m.def("adam_atan2_multi", &adam_atan2_multi);
+  m.def("ngram_fwd", &ngram_fwd);
+  m.def("ngram_bwd", &ngram_bwd);
+  m.def("fmha_plan", &fmha_plan);
+  m.def("fmha_fwd", &fmha_fwd);
+  m.def("fmha_status", &fmha_status);
+}

@@ -1,0 +1,207 @@
+"""Token-level MLP expert mixtures (MoE), their router, and dense->MoE upcycling.
+
+Reference behaviour: ``src/mimir/model/expert_mixtures.py`` (router ``:11-66``, dense
+and sparse mixture ``:69-104``, upcycling ``:107-165``) and
+``src/mimir/model/routed_block.py:7-22``.
+
+* The router keeps one parameter row and one bias per expert (so freezing expert 0 is
+  real), computes fp32 scores, breaks ties by a stable descending sort, and returns
+  softmax-over-top-k weights, or sigmoid affinities renormalised over the top-k when
+  aux-loss-free balancing is on (the per-expert ``selection_bias`` only steers selection).
+* For top-1 with several experts a straight-through surrogate gives the router a gradient.
+* The sparse path runs each expert only on its tokens and still calls every expert (even
+  with zero tokens) so all ranks issue identical collectives.  On CUDA the token
+  permutation is done by the fused kernels in :mod:`mimir_b200.ops.moe`.
+"""
+from __future__ import annotations
+
+import copy
+import re
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from mimir_b200 import ops
+from mimir_b200.models.transformer import TransformerBlock
+
+
+class TopKRouter(nn.Module):
+    def __init__(self, hidden_size, n, k, *, freeze_base=False, top1_straight_through=True,
+                 balance_enabled=False, balance_update_rate=0.001):
+        super().__init__()
+        if not 1 <= k <= n:
+            raise ValueError("Routing requires 1 <= k <= n")
+        self.n, self.k = n, k
+        self.balance_enabled = balance_enabled
+        self.balance_update_rate = balance_update_rate
+        if balance_enabled:
+            self.register_buffer("selection_bias", torch.zeros(n, dtype=torch.float32))
+        self.top1_straight_through = top1_straight_through
+        self.rows = nn.ParameterList([nn.Parameter(torch.zeros(hidden_size), requires_grad=not (freeze_base and i == 0))
+                                      for i in range(n)])
+        self.biases = nn.ParameterList([nn.Parameter(torch.zeros(1), requires_grad=not (freeze_base and i == 0))
+                                        for i in range(n)])
+        self.register_buffer("logit_bias", torch.zeros(n))
+
+    def _apply(self, fn, recurse=True):
+        # The balancing bias is a counter-driven fp32 quantity: keep it fp32 through .to(dtype).
+        before = getattr(self, "selection_bias", None)
+        out = super()._apply(fn, recurse=recurse)
+        if self.balance_enabled:
+            self.selection_bias = (self.selection_bias.float() if before.is_meta
+                                   else before.to(device=self.selection_bias.device, dtype=torch.float32))
+        return out
+
+    def scores(self, x, logit_bias=None):
+        weight = torch.stack(list(self.rows)).float()
+        bias = torch.cat(list(self.biases)).float()
+        s = F.linear(x.float(), weight, bias) + self.logit_bias.float()
+        if logit_bias is not None:
+            s = s + logit_bias.float()
+        return s
+
+    def forward(self, x, logit_bias=None):
+        scores = self.scores(x, logit_bias)
+        tiny = torch.finfo(torch.float32).tiny
+        if self.balance_enabled:
+            affinity = scores.sigmoid()
+            selection = affinity + self.selection_bias.float()
+        else:
+            affinity = selection = scores
+        chosen = selection.argsort(dim=-1, descending=True, stable=True)[..., :self.k]
+        mask = torch.zeros_like(scores, dtype=torch.bool).scatter(-1, chosen, True)
+        if self.balance_enabled:
+            from mimir_b200.optim.routing_balance import record_load
+            record_load(self, mask)
+            weights = affinity * mask
+            weights = weights / weights.sum(-1, keepdim=True).clamp_min(tiny)
+        else:
+            weights = scores.masked_fill(~mask, -torch.inf).softmax(-1)
+        if self.k == 1 and self.n > 1 and self.top1_straight_through:
+            probs = (affinity / affinity.sum(-1, keepdim=True).clamp_min(tiny)) if self.balance_enabled \
+                else scores.softmax(-1)
+            surrogate = probs * mask
+            weights = weights + (surrogate - surrogate.detach())
+        return weights
+
+
+class MLPMixture(nn.Module):
+    def __init__(self, mlp, hidden_size, n, k, *, freeze_base=False, top1_straight_through=True, sparse=False,
+                 balance_enabled=False, balance_update_rate=0.001):
+        super().__init__()
+        self.experts = nn.ModuleList([mlp] + [copy.deepcopy(mlp) for _ in range(n - 1)])
+        self.router = TopKRouter(hidden_size, n, k, freeze_base=freeze_base,
+                                 top1_straight_through=top1_straight_through, balance_enabled=balance_enabled,
+                                 balance_update_rate=balance_update_rate)
+        self.sparse = sparse
+        if freeze_base:
+            self.experts[0].requires_grad_(False)
+
+    def forward(self, x, stability_diagnostics=None, stability_scope=None, routing_bias=None):
+        weights = self.router(x, routing_bias)
+        if self.sparse:
+            return self._dispatch(x, weights, stability_diagnostics, stability_scope)
+        out = torch.zeros_like(x)
+        for i, expert in enumerate(self.experts):
+            y = expert(x, stability_diagnostics=stability_diagnostics,
+                       stability_scope=f"{stability_scope}/expert_{i}" if stability_scope else None)
+            out = out + weights[..., i:i + 1].to(y.dtype) * y
+        return out
+
+    @torch.compiler.disable
+    def _dispatch(self, x, weights, diagnostics, scope):
+        flat = x.reshape(-1, x.shape[-1])
+        w = weights.reshape(-1, len(self.experts))
+        plan = ops.moe_plan(w)  # per-expert token lists (one device sort; no per-expert nonzero)
+        out = torch.zeros_like(flat)
+        for i, expert in enumerate(self.experts):
+            idx = plan.indices(i)
+            y = expert(flat.index_select(0, idx), stability_diagnostics=diagnostics if idx.numel() else None,
+                       stability_scope=f"{scope}/expert_{i}" if scope else None)
+            out = out.index_add(0, idx, y * w[idx, i, None].to(y.dtype))
+        return out.reshape_as(x)
+
+
+def install_mlp_mixtures(core, hidden_size, n, k, **kwargs):
+    if n > 1:
+        for layer in core.layers:
+            layer.mlp = MLPMixture(layer.mlp, hidden_size, n, k, **kwargs)
+
+
+class RoutedBlock(TransformerBlock):
+    """A block whose MLP mixture also receives a per-token routing (metadata) bias."""
+
+    def __init__(self, original, norm_type):
+        nn.Module.__init__(self)
+        self.attn, self.mlp, self.norm = original.attn, original.mlp, original.norm
+        self.norm_type = norm_type
+
+    def forward(self, x, routing_bias=None, stability_diagnostics=None, stability_scope=None, **seq_info):
+        attn_kw = dict(stability_diagnostics=stability_diagnostics,
+                       stability_scope=f"{stability_scope}/attention" if stability_scope else None)
+        mlp_kw = dict(routing_bias=routing_bias, stability_diagnostics=stability_diagnostics,
+                      stability_scope=f"{stability_scope}/mlp" if stability_scope else None)
+        if self.norm_type == "pre":
+            x = x + self.attn(self.norm(x), **seq_info, **attn_kw)
+            return x + self.mlp(self.norm(x), **mlp_kw)
+        x = self.norm(x + self.attn(x, **seq_info, **attn_kw))
+        return self.norm(x + self.mlp(x, **mlp_kw))
+
+
+# ----------------------------------------------------------------------------------------
+# Dense -> MoE/MoS upcycling
+# ----------------------------------------------------------------------------------------
+NEW_V2_COMPONENTS = {
+    "router", "stack_router", "invocation_gates", "gate_alpha", "attn_residual", "mlp_residual", "residual_alpha",
+    "residual_readout", "memory", "ngram", "routing_bias_scale", "l_branch_mixer",
+}
+
+
+def dense_source_key(key: str) -> str:
+    """Map an expert key (``...mlp.experts.3.x`` / ``...stack_experts.1.x``) to its dense origin."""
+    key = re.sub(r"\.stack_experts\.\d+\.", ".core.", key)
+    return re.sub(r"\.mlp\.experts\.\d+\.", ".mlp.", key)
+
+
+def is_new_v2_key(key: str) -> bool:
+    return bool(set(key.split(".")) & NEW_V2_COMPONENTS)
+
+
+def upcycle_dense_weights(destination, source_state):
+    """Copy a dense state dict into an expert model; every expert starts as the dense MLP/stack.
+
+    Missing backbone keys, shape mismatches and unused source keys are errors.
+    """
+    state = destination.state_dict()
+    used = set()
+    for key, value in state.items():
+        src = dense_source_key(key)
+        if src not in source_state:
+            if is_new_v2_key(key):
+                continue
+            raise ValueError(f"Missing dense backbone key: {src}")
+        if source_state[src].shape != value.shape:
+            raise ValueError(f"Shape mismatch for {key}: {source_state[src].shape} != {value.shape}")
+        state[key] = source_state[src].detach().clone()
+        used.add(src)
+    if set(source_state) != used:
+        raise ValueError(f"Unexpected dense source keys: {set(source_state) - used}")
+    destination.load_state_dict(state, strict=True)
+
+
+def upcycle_training_state(destination, optimizer, source_model, source_optimizer):
+    """Upcycle weights and clone every optimizer slot (moments, EMA) of the dense source."""
+    if type(optimizer) is not type(source_optimizer):
+        raise ValueError("Upcycling must retain the optimizer type")
+    upcycle_dense_weights(destination, source_model.state_dict())
+    src_params = dict(source_model.named_parameters())
+    for name, p in destination.named_parameters():
+        src = dense_source_key(name)
+        if src in src_params:
+            state = source_optimizer.state[src_params[src]]
+            if set(state) != set(optimizer.state[p]):
+                raise ValueError(f"Optimizer slot mismatch for {name}")
+            optimizer.state[p] = copy.deepcopy(state)
+        elif not is_new_v2_key(name):
+            raise ValueError(f"Missing optimizer source for {name}")

@@ -1,0 +1,77 @@
+"""Loader for the compiled sm_100a extension ``mimir_b200._C``.
+
+On a CUDA tensor every op in :mod:`mimir_b200.ops` runs its hand-written kernel; if the
+extension is missing there, the op raises instead of silently falling back to PyTorch.
+``MIMIR_DISABLE_KERNELS=1`` forces the PyTorch formulation (used as the oracle in tests).
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+_EXT = None
+_LOAD_ERROR: Exception | None = None
+
+# Kernel launches issued by one call of each binding (for launch accounting in benchmarks).
+_LAUNCHES_PER_CALL = {"fmha_status": 0, "fmha_plan": 1}
+
+
+class _CountingModule:
+    """Thin proxy over the compiled module that counts the kernels each binding launches."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self.launches = 0
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+        per_call = _LAUNCHES_PER_CALL.get(name, 1)
+
+        def counted(*args, **kwargs):
+            self.launches += per_call
+            return fn(*args, **kwargs)
+        counted.__name__ = name
+        return counted
+
+
+def ext():
+    """Return the compiled extension module, raising a clear error if it was not built."""
+    global _EXT, _LOAD_ERROR
+    if _EXT is None:
+        if _LOAD_ERROR is not None:
+            raise RuntimeError(_missing_message()) from _LOAD_ERROR
+        try:
+            from mimir_b200 import _C  # type: ignore[attr-defined]
+        except ImportError as exc:  # pragma: no cover - depends on the build
+            _LOAD_ERROR = exc
+            raise RuntimeError(_missing_message()) from exc
+        _EXT = _CountingModule(_C)
+    return _EXT
+
+
+def launch_count() -> int:
+    """Number of mimir_b200 kernels launched so far in this process."""
+    return _EXT.launches if _EXT is not None else 0
+
+
+def _missing_message() -> str:
+    return ("mimir_b200._C (the sm_100a CUDA extension) is not built. Run "
+            "`python setup.py build_ext --inplace` (or __graft_entry__.build()).")
+
+
+def available() -> bool:
+    try:
+        ext()
+        return True
+    except RuntimeError:
+        return False
+
+
+def kernels_enabled(t: torch.Tensor | None = None) -> bool:
+    """True when ``t`` lives on a CUDA device and kernels are not disabled by the environment."""
+    if os.environ.get("MIMIR_DISABLE_KERNELS", "0") == "1":
+        return False
+    return t is not None and t.is_cuda

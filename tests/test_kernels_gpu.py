@@ -1,0 +1,150 @@
+"""Numerics of the sm_100a kernels against plain PyTorch fp32 references."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from mimir_b200 import ops
+from mimir_b200.data.prefixlm import compute_aux_seq_tensors_scalars
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(a, b, atol, rtol=0.0, name=""):
+    err = (a.float() - b.float()).abs()
+    bound = atol + rtol * b.float().abs()
+    assert bool((err <= bound).all()), f"{name}: max abs err {err.max().item():.3e}"
+
+
+@pytest.mark.parametrize("d", [256, 2048, 1536])
+def test_rmsnorm(d):
+    x = torch.randn(300, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    y = ops.rms_norm(x, 1e-6)
+    xr = x.detach().float().requires_grad_(True)
+    yr = F.rms_norm(xr, (d,), eps=1e-6)
+    _close(y, yr, 2e-2, 1e-2, "rmsnorm fwd")
+    g = torch.randn_like(y)
+    y.backward(g)
+    yr.backward(g.float())
+    _close(x.grad, xr.grad, 3e-2, 2e-2, "rmsnorm bwd")
+
+
+def test_swiglu():
+    gu = torch.randn(257, 2 * 5632, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    out = ops.swiglu(gu)
+    ref_in = gu.detach().float().requires_grad_(True)
+    ref = ops.swiglu_reference(ref_in)
+    _close(out, ref, 2e-2, 1e-2, "swiglu fwd")
+    g = torch.randn_like(out)
+    out.backward(g)
+    ref.backward(g.float())
+    _close(gu.grad, ref_in.grad, 3e-2, 2e-2, "swiglu bwd")
+
+
+def test_cross_entropy():
+    torch.manual_seed(0)
+    h = torch.randn(200, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(4096, 256, device="cuda") * 0.05).to(torch.bfloat16).requires_grad_(True)
+    labels = torch.randint(0, 4096, (200,), device="cuda")
+    labels[:17] = -100
+    loss, correct = ops.linear_cross_entropy(h, w, labels)
+    hr, wr = h.detach().float().requires_grad_(True), w.detach().float().requires_grad_(True)
+    logits = (hr.bfloat16() @ wr.bfloat16().t()).float()
+    ref = F.cross_entropy(logits, labels, ignore_index=-100, reduction="sum")
+    assert abs(loss.item() - ref.item()) <= 1e-3 * abs(ref.item()) + 1e-2
+    assert torch.equal(correct, logits.argmax(-1) == labels)
+    (loss * 0.5).backward()
+    (ref * 0.5).backward()
+    _close(h.grad, hr.grad, 2e-2, 2e-2, "ce dh")
+    _close(w.grad, wr.grad, 2e-2, 2e-2, "ce dw")
+
+
+def test_adam_atan2_fused_matches_reference():
+    from mimir_b200.optim.adam_atan2 import AdamATan2
+    torch.manual_seed(0)
+    ps = [torch.randn(s, device="cuda", requires_grad=True) for s in [(100, 37), (5000,), (3, 3)]]
+    ref = [p.detach().clone().requires_grad_(True) for p in ps]
+    o1 = AdamATan2(ps, lr=1e-2, ema=0.99)
+    o2 = AdamATan2(ref, lr=1e-2, ema=0.99, fused=False)
+    for _ in range(3):
+        for a, b in zip(ps, ref):
+            g = torch.randn_like(a)
+            a.grad, b.grad = g.clone(), g.clone()
+        o1.step()
+        o2.step()
+    for a, b in zip(ps, ref):
+        _close(a, b, 1e-5, 1e-5, "param")
+        _close(o1.state[a]["param_ema"], o2.state[b]["param_ema"], 1e-5, 1e-5, "ema")
+        _close(o1.state[a]["exp_avg_sq"], o2.state[b]["exp_avg_sq"], 1e-7, 1e-5, "v")
+
+
+def test_ngram_kernel_matches_torch():
+    from mimir_b200.models.ngram import NGramMemory
+    torch.manual_seed(0)
+    mem = NGramMemory(256, (2, 3), 1021, heads=2).cuda()
+    for t in mem.tables:
+        torch.nn.init.normal_(t)
+    ids = torch.randint(0, 500, (1, 777), device="cuda")
+    pos = torch.cat([torch.arange(300), torch.arange(477)]).cuda()[None]
+    out = mem.lookup(ids, pos, torch.float32)
+    import os
+    os.environ["MIMIR_DISABLE_KERNELS"] = "1"
+    try:
+        ref = mem.lookup(ids, pos, torch.float32)
+    finally:
+        os.environ.pop("MIMIR_DISABLE_KERNELS")
+    _close(out, ref, 1e-5, 1e-5, "ngram")
+
+
+def _packed(lengths, prefixes, heads, kv_heads, seed=0, pad=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    T = sum(lengths) + pad
+    q = torch.randn(T, heads, 128, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(T, kv_heads, 128, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(T, kv_heads, 128, device="cuda", generator=g).to(torch.bfloat16)
+    p = torch.tensor(prefixes, dtype=torch.int32)
+    c = torch.tensor(lengths, dtype=torch.int32) - p
+    tensors, scalars = compute_aux_seq_tensors_scalars(p.numpy(), c.numpy(), T)
+    meta = {k2: torch.from_numpy(v2).cuda() for k2, v2 in tensors.items()} | scalars
+    return q, k, v, meta
+
+
+CASES = [
+    ([4096, 4096], [1000, 0], 16, 4),
+    ([130, 1, 257, 513], [5, 1, 256, 0], 2, 2),
+    ([128, 256], [128, 129], 4, 1),
+    ([300], [299], 2, 1),
+]
+
+
+@pytest.mark.parametrize("lengths,prefixes,H,KV", CASES)
+@pytest.mark.parametrize("causal", [False, True])
+def test_fmha_forward(lengths, prefixes, H, KV, causal):
+    q, k, v, meta = _packed(lengths, prefixes, H, KV, pad=37)
+    out = ops.prefixlm_attention(q, k, v, causal, **meta)
+    ref = ops.dense_prefixlm_attention(q.float(), k.float(), v.float(), causal, **meta)
+    total = sum(lengths)
+    assert ops.ext().fmha_status(q.device) == 0
+    _close(out[:total], ref[:total], 2e-2, 2e-2, "fmha fwd")
+
+
+def test_gated_attention_block_matches_composite():
+    from mimir_b200.models.layers import RotaryEmbedding
+    torch.manual_seed(0)
+    H, KV, hd = 4, 2, 128
+    lengths, prefixes = [200, 333], [50, 1]
+    _, _, _, meta = _packed(lengths, prefixes, H, KV)
+    T = sum(lengths)
+    gqkv = (torch.randn(T, (2 * H + 2 * KV) * hd, device="cuda")).to(torch.bfloat16).requires_grad_(True)
+    rope = RotaryEmbedding(hd, 4096, 10000.0).cuda()
+    pos = torch.cat([torch.arange(n) for n in lengths]).cuda()
+    tables = (rope.cos_cached, rope.sin_cached)
+    y = ops.gated_prefixlm_attention(gqkv, tables, pos, H, KV, hd, False, meta)
+    g32 = gqkv.detach().float().requires_grad_(True)
+    ref = ops.gated_attention_composite(g32, tables, pos, H, KV, hd, False, meta)
+    _close(y, ref, 3e-2, 3e-2, "gated fwd")
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    ref.backward(dy.float())
+    _close(gqkv.grad, g32.grad, 6e-2, 5e-2, "gated bwd")
