@@ -224,12 +224,38 @@ def run_ours(args, rank, world, local):
 
 
 # ---------------------------------------------------------------------------------------- reference arm
+def _stub_missing_reference_deps():
+    """The offline wheelhouse lacks `coolname` and `omegaconf`, which the reference's
+    training/runtime.py imports at module level for run naming and Hydra config handling.
+    Neither is used on the training-step path; empty stand-ins let the unmodified module import."""
+    import types
+    for name in ("coolname", "omegaconf"):
+        try:
+            __import__(name)
+            continue
+        except ImportError:
+            pass
+        mod = types.ModuleType(name)
+        if name == "coolname":
+            mod.generate_slug = lambda n=2: "bench-run"
+        else:
+            mod.DictConfig = dict
+
+            class OmegaConf:  # noqa: D401 - placeholder
+                @staticmethod
+                def to_container(cfg, **_):
+                    return dict(cfg)
+            mod.OmegaConf = OmegaConf
+        sys.modules[name] = mod
+
+
 def run_reference(args, rank, world, local):
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "mimir")):
         print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
         return
     sys.path.insert(0, ref)
+    _stub_missing_reference_deps()
     from mimir.model import Mimir2 as RefMimir2
     from mimir.model.accelerator import set_accelerator_type
     from mimir.model.adam_atan2 import AdamATan2 as RefAdam

@@ -183,9 +183,10 @@ __global__ void swiglu_bwd_kernel(const T* __restrict__ dp, const T* __restrict_
 // ------------------------------------------------------------------ RoPE on packed Q|K
 // gqkv row layout: [gate H | q H | k KV | v KV] x 128.  Output qk row: [q H | k KV] x 128.
 // One thread per (token, head, 8-wide chunk of the lower half).
+template <typename TT>
 __global__ void rope_qk_fwd_kernel(const __nv_bfloat16* __restrict__ gqkv, int64_t ld_in,
-                                   __nv_bfloat16* __restrict__ qk, int64_t ld_out, const float* __restrict__ cos_t,
-                                   const float* __restrict__ sin_t, const int* __restrict__ pos, int64_t T,
+                                   __nv_bfloat16* __restrict__ qk, int64_t ld_out, const TT* __restrict__ cos_t,
+                                   const TT* __restrict__ sin_t, const int* __restrict__ pos, int64_t T,
                                    int H, int heads /* H + KV */) {
   const int64_t total = T * heads * 8;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -197,15 +198,15 @@ __global__ void rope_qk_fwd_kernel(const __nv_bfloat16* __restrict__ gqkv, int64
     const __nv_bfloat16* src = gqkv + t * ld_in + (int64_t)(H + h) * 128;
     __nv_bfloat16* dst = qk + t * ld_out + (int64_t)h * 128;
     const int64_t p = pos[t];
-    const float* c = cos_t + p * 128;
-    const float* s = sin_t + p * 128;
+    const TT* c = cos_t + p * 128;
+    const TT* s = sin_t + p * 128;
     float lo[8], hi[8], olo[8], ohi[8];
     Vec<__nv_bfloat16>::load(src + d0, lo);
     Vec<__nv_bfloat16>::load(src + 64 + d0, hi);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      olo[j] = lo[j] * c[d0 + j] - hi[j] * s[d0 + j];
-      ohi[j] = hi[j] * c[64 + d0 + j] + lo[j] * s[64 + d0 + j];
+      olo[j] = lo[j] * to_f(c[d0 + j]) - hi[j] * to_f(s[d0 + j]);
+      ohi[j] = hi[j] * to_f(c[64 + d0 + j]) + lo[j] * to_f(s[64 + d0 + j]);
     }
     Vec<__nv_bfloat16>::store(dst + d0, olo);
     Vec<__nv_bfloat16>::store(dst + 64 + d0, ohi);
@@ -213,9 +214,9 @@ __global__ void rope_qk_fwd_kernel(const __nv_bfloat16* __restrict__ gqkv, int64
 }
 
 // Adjoint of the rotation: writes un-rotated dq/dk and copies dv into the packed gradient.
-template <typename TQ, typename TK, typename TV>
+template <typename TQ, typename TK, typename TV, typename TT>
 __global__ void rope_qk_bwd_kernel(const TQ* __restrict__ dq, const TK* __restrict__ dk, const TV* __restrict__ dv,
-                                   const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                   const TT* __restrict__ cos_t, const TT* __restrict__ sin_t,
                                    const int* __restrict__ pos, __nv_bfloat16* __restrict__ dgqkv, int64_t ld, int64_t T,
                                    int H, int KV) {
   const int heads = H + 2 * KV;  // q heads, k heads, v heads
@@ -239,13 +240,13 @@ __global__ void rope_qk_bwd_kernel(const TQ* __restrict__ dq, const TK* __restri
         for (int j = 0; j < 8; ++j) lo[j] = to_f(src[d0 + j]), hi[j] = to_f(src[64 + d0 + j]);
       }
       const int64_t p = pos[t];
-      const float* c = cos_t + p * 128;
-      const float* s = sin_t + p * 128;
+      const TT* c = cos_t + p * 128;
+      const TT* s = sin_t + p * 128;
       float olo[8], ohi[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        olo[j] = lo[j] * c[d0 + j] + hi[j] * s[64 + d0 + j];
-        ohi[j] = hi[j] * c[64 + d0 + j] - lo[j] * s[d0 + j];
+        olo[j] = lo[j] * to_f(c[d0 + j]) + hi[j] * to_f(s[64 + d0 + j]);
+        ohi[j] = hi[j] * to_f(c[64 + d0 + j]) - lo[j] * to_f(s[d0 + j]);
       }
       Vec<__nv_bfloat16>::store(dst + d0, olo);
       Vec<__nv_bfloat16>::store(dst + 64 + d0, ohi);
@@ -432,7 +433,9 @@ at::Tensor swiglu_bwd(at::Tensor dp, at::Tensor gu) {
 at::Tensor rope_qk(at::Tensor gqkv, at::Tensor cos_t, at::Tensor sin_t, at::Tensor pos, int64_t H, int64_t KV) {
   check_cuda_contig(gqkv, "gqkv");
   TORCH_CHECK(gqkv.scalar_type() == at::kBFloat16 && gqkv.dim() == 2);
-  TORCH_CHECK(cos_t.scalar_type() == at::kFloat && cos_t.size(-1) == 128 && cos_t.is_contiguous());
+  TORCH_CHECK((cos_t.scalar_type() == at::kFloat || cos_t.scalar_type() == at::kBFloat16) && cos_t.size(-1) == 128 &&
+              cos_t.is_contiguous() && sin_t.is_contiguous() && sin_t.scalar_type() == cos_t.scalar_type(),
+              "rope tables must be contiguous fp32/bf16 [max_seq, 128]");
   TORCH_CHECK(pos.scalar_type() == at::kInt && pos.is_contiguous());
   c10::cuda::CUDAGuard guard(gqkv.device());
   const int64_t T = gqkv.size(0);
@@ -441,10 +444,13 @@ at::Tensor rope_qk(at::Tensor gqkv, at::Tensor cos_t, at::Tensor sin_t, at::Tens
   auto st = at::cuda::getCurrentCUDAStream();
   if (T == 0) return qk;
   const int heads = (int)(H + KV);
-  rope_qk_fwd_kernel<<<grid_for(T * heads * 8, 256), 256, 0, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(gqkv.data_ptr()), gqkv.size(1),
-      reinterpret_cast<__nv_bfloat16*>(qk.data_ptr()), qk.size(1), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
-      pos.data_ptr<int>(), T, (int)H, heads);
+  auto launch = [&](auto* c, auto* s) {
+    rope_qk_fwd_kernel<<<grid_for(T * heads * 8, 256), 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(gqkv.data_ptr()), gqkv.size(1),
+        reinterpret_cast<__nv_bfloat16*>(qk.data_ptr()), qk.size(1), c, s, pos.data_ptr<int>(), T, (int)H, heads);
+  };
+  if (cos_t.scalar_type() == at::kFloat) launch(cos_t.data_ptr<float>(), sin_t.data_ptr<float>());
+  else launch(reinterpret_cast<const __nv_bfloat16*>(cos_t.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(sin_t.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return qk;
 }
@@ -460,11 +466,17 @@ void rope_qk_bwd(at::Tensor dq, at::Tensor dk, at::Tensor dv, at::Tensor cos_t, 
   auto st = at::cuda::getCurrentCUDAStream();
   if (T == 0) return;
   const int64_t work = T * (H + 2 * KV) * 8;
+  const bool tf = cos_t.scalar_type() == at::kFloat;
   auto args = [&](auto* q, auto* k, auto* v) {
-    rope_qk_bwd_kernel<<<grid_for(work, 256), 256, 0, st>>>(q, k, v, cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
-                                                            pos.data_ptr<int>(),
-                                                            reinterpret_cast<__nv_bfloat16*>(dgqkv.data_ptr()),
-                                                            dgqkv.size(1), T, (int)H, (int)KV);
+    auto* out = reinterpret_cast<__nv_bfloat16*>(dgqkv.data_ptr());
+    if (tf)
+      rope_qk_bwd_kernel<<<grid_for(work, 256), 256, 0, st>>>(q, k, v, cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+                                                              pos.data_ptr<int>(), out, dgqkv.size(1), T, (int)H, (int)KV);
+    else
+      rope_qk_bwd_kernel<<<grid_for(work, 256), 256, 0, st>>>(
+          q, k, v, reinterpret_cast<const __nv_bfloat16*>(cos_t.data_ptr()),
+          reinterpret_cast<const __nv_bfloat16*>(sin_t.data_ptr()), pos.data_ptr<int>(), out, dgqkv.size(1), T, (int)H,
+          (int)KV);
   };
   using bf = __nv_bfloat16;
   const bool qf = dq.scalar_type() == at::kFloat, kf = dk.scalar_type() == at::kFloat, vf = dv.scalar_type() == at::kFloat;
