@@ -32,6 +32,13 @@ std::vector<at::Tensor> fmha_fwd(at::Tensor q_src, int64_t q_col, at::Tensor k_s
                                  int64_t KV, bool is_causal, at::Tensor cu_seqlens, at::Tensor prefix_lens,
                                  int64_t numseqs, at::Tensor tiles, at::Tensor ntiles);
 int64_t fmha_status(at::Device dev);
+// fmha_bwd.cu
+std::vector<at::Tensor> fmha_bwd_plan(at::Tensor cu_seqlens, at::Tensor prefix_lens, int64_t numseqs,
+                                      int64_t total_tokens, bool is_causal);
+std::vector<at::Tensor> fmha_bwd(at::Tensor q_src, int64_t q_col, at::Tensor k_src, int64_t k_col, at::Tensor v_src,
+                                 int64_t v_col, at::Tensor d_o, at::Tensor lse, at::Tensor delta, int64_t H,
+                                 int64_t KV, bool is_causal, at::Tensor cu_seqlens, at::Tensor prefix_lens,
+                                 int64_t numseqs, at::Tensor kv_tiles, at::Tensor kv_ntiles);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mimir_b200 hand-written sm_100a kernels";
@@ -51,4 +58,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fmha_plan", &fmha_plan);
   m.def("fmha_fwd", &fmha_fwd);
   m.def("fmha_status", &fmha_status);
+  m.def("fmha_bwd_plan", &fmha_bwd_plan);
+  m.def("fmha_bwd", &fmha_bwd);
 }

@@ -421,6 +421,8 @@ int* status_word(const at::Device& dev) {
 
 }  // namespace
 
+int* fmha_status_ptr(const at::Device& dev) { return status_word(dev); }
+
 // Returns (tiles, ntiles) for a packed batch; reused across layers of one forward.
 std::vector<at::Tensor> fmha_plan(at::Tensor cu_seqlens, at::Tensor prefix_lens, int64_t numseqs, int64_t total_tokens,
                                   bool is_causal) {

@@ -76,13 +76,14 @@ def _fmha_bwd_ready() -> bool:
 
 
 def attention_plan(cu_seqlens: torch.Tensor, prefix_lens: torch.Tensor, numseqs: int, total_tokens: int,
-                   is_causal: bool):
+                   is_causal: bool, backward: bool = False):
     """Device tile schedule ``(tiles, ntiles)`` for a packed batch, cached on the metadata tensor.
 
     Every attention layer of a forward (and its backward) sees the same packed layout, so the
     schedule is built once per batch; the cache is invalidated if ``cu_seqlens`` is modified.
     """
-    key = (bool(is_causal), int(numseqs), int(total_tokens), prefix_lens.data_ptr(), prefix_lens._version)
+    key = (bool(backward), bool(is_causal), int(numseqs), int(total_tokens), prefix_lens.data_ptr(),
+           prefix_lens._version)
     cache = getattr(cu_seqlens, "_mimir_fmha_plans", None)
     if cache is None or cache[0] != cu_seqlens._version:
         cache = (cu_seqlens._version, {})
@@ -92,7 +93,8 @@ def attention_plan(cu_seqlens: torch.Tensor, prefix_lens: torch.Tensor, numseqs:
             pass
     plan = cache[1].get(key)
     if plan is None:
-        plan = ext().fmha_plan(cu_seqlens, prefix_lens, int(numseqs), int(total_tokens), bool(is_causal))
+        build = ext().fmha_bwd_plan if backward else ext().fmha_plan
+        plan = build(cu_seqlens, prefix_lens, int(numseqs), int(total_tokens), bool(is_causal))
         cache[1][key] = plan
     return plan
 
@@ -121,7 +123,9 @@ class _PrefixLMAttentionFn(torch.autograd.Function):
         if not _fmha_bwd_ready():
             raise RuntimeError("fmha_bwd kernel missing from mimir_b200._C")
         delta = ext().attn_delta(do, out, H)
-        dq, dk, dv = ext().fmha_bwd(q2, 0, k2, 0, v2, 0, do, lse, delta, H, KV, is_causal, cu, pl, numseqs)
+        kv_tiles, kv_ntiles = attention_plan(cu, pl, numseqs, T, is_causal, backward=True)
+        dq, dk, dv = ext().fmha_bwd(q2, 0, k2, 0, v2, 0, do, lse, delta, H, KV, is_causal, cu, pl, numseqs,
+                                    kv_tiles, kv_ntiles)
         return dq.view(T, H, -1).to(q2.dtype), dk.view(T, KV, -1).to(q2.dtype), dv.view(T, KV, -1).to(q2.dtype), \
             None, None, None, None
 
@@ -170,8 +174,9 @@ class _GatedAttentionFn(torch.autograd.Function):
         dgqkv = torch.empty_like(gqkv)
         # dO = dy * sigmoid(g); dgate -> dgqkv[:, :H*hd]; delta = rowsum(dO * O) per (head, token).
         do, delta = C.attn_gate_bwd(dy.contiguous(), o, gqkv, dgqkv, H)
+        kv_tiles, kv_ntiles = attention_plan(cu, pl, numseqs, gqkv.shape[0], is_causal, backward=True)
         dq, dk, dv = C.fmha_bwd(qk, 0, qk, H * hd, gqkv, (2 * H + KV) * hd, do, lse, delta, H, KV, is_causal,
-                                cu, pl, numseqs, tiles, ntiles)
+                                cu, pl, numseqs, kv_tiles, kv_ntiles)
         C.rope_qk_bwd(dq, dk, dv, cos, sin, positions, dgqkv, H, KV)  # un-rotate into the packed gradient
         return dgqkv, None, None, None, None, None, None, None, None, None, None
 
