@@ -160,8 +160,10 @@ def timed_loop(run_step, batches, steps: int):
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
+    torch.cuda.nvtx.range_push("timed")
     for i in range(steps):
         run_step(batches[i % len(batches)])
+    torch.cuda.nvtx.range_pop()
     end.record()
     torch.cuda.synchronize()
     dist.barrier()

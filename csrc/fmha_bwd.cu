@@ -7,13 +7,15 @@
 //   P^T  = exp2(S^T * scale*log2e - LSE2[q]) (masked), dS^T = P^T * (dP^T - Delta[q])  (softmax warps)
 //   dV  += P^T dO       (M=128 keys, N=128, K=64)            TMEM accumulator
 //   dK  += dS^T Q       (M=128 keys, N=128, K=64)            TMEM accumulator
-//   dQ^T = K^T dS^T     (M=128 head dims, N=64 queries, K=128 keys) -> TMEM, then added to a
-//          global fp32 dQ with coalesced reductions by the dQ warps.
+//   dQ^T = K^T dS^T     (M=128 head dims, N=64 queries, K=128 keys) -> TMEM; the dQ warps
+//          transpose it into a [64 x 128] fp32 smem tile that one TMA reduce-add folds into
+//          the global dQ (L2-side line reductions instead of per-element atomics).
 // dK/dV are written once per CTA (bf16, no atomics) because the CTA covers all query heads
 // that share its KV head.  TMEM: S^T 64 + dP^T 64 + dQ^T 64 + dV 128 + dK 128 = 448 columns.
 //
-// Warp roles (320 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
-// warps 2..5 softmax (thread = key row), warps 6..9 dQ drain (thread = head dim).
+// Warp roles (448 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
+// warps 2..9 softmax (thread = key row; warps w and w+4 split the 64 query columns, so each
+// SM sub-partition runs two softmax warps), warps 10..13 dQ drain (thread = head dim).
 // All waits are bounded (common.cuh) and the teardown drains async work before freeing TMEM.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -29,12 +31,13 @@ namespace {
 constexpr int kKeys = 128;     // keys per CTA
 constexpr int kQRows = 64;     // query rows per block
 constexpr int kHeadDim = 128;
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;  // 14 warps
 constexpr uint32_t kKVBytes = kKeys * kHeadDim * 2;        // 32 KB
 constexpr uint32_t kKVChunk = kKVBytes / 2;                // [128 keys][64 dims] = 16 KB
 constexpr uint32_t kQBytes = kQRows * kHeadDim * 2;        // 16 KB
 constexpr uint32_t kQChunk = kQBytes / 2;                  // [64 rows][64 dims] = 8 KB
 constexpr uint32_t kPBytes = kKeys * kQRows * 2;           // 16 KB
+constexpr int kStages = 3;                                  // Q/dO ring depth
 
 struct BwdParams {
   float* dq;                   // [T, H*128] fp32, pre-zeroed; receives scale * dS K
@@ -53,32 +56,45 @@ struct BwdParams {
   float scale_log2;            // log2(e) / sqrt(128)
   float scale;                 // 1 / sqrt(128)
   int* status;
+  unsigned long long* trace;   // optional event timestamps of CTA (0, trace_tile) for profiling
+  int trace_tile;
+  int mode;                    // profiling experiments only: bit0 no shuffles, bit1 no mask, bit2 no exp
+};
+
+// Event slots per iteration in the optional trace buffer.
+enum TraceEvent : int {
+  kEvMmaSdpIssued = 0, kEvMmaDsReady = 1, kEvMmaAccIssued = 2, kEvSmSdpFull = 3, kEvSmLoaded = 4,
+  kEvSmPdsFree = 5, kEvSmDsReady = 6, kEvDqFull = 7, kEvDqStaged = 8, kEvDqReduced = 9, kEvProdIssued = 10,
+  kEvCount = 16
 };
 
 struct __align__(8) Barriers {
   uint64_t kv_full;
-  uint64_t qdo_full[2];
-  uint64_t qdo_empty[2];
+  uint64_t qdo_full[3];
+  uint64_t qdo_empty[3];
   uint64_t sdp_full;
   uint64_t s_free;
   uint64_t ds_ready;
   uint64_t pds_free;
-  uint64_t dq_full;
-  uint64_t dq_free;
+  uint64_t dq_full[2];     // per TMEM dQ^T buffer
+  uint64_t dq_free[2];
   uint64_t acc_full;
   uint64_t mma_done;
+  uint64_t dqs_full[2];    // 4 dQ warps wrote staging tile b
+  uint64_t dqs_free[2];    // the TMA reduce finished reading staging tile b
   uint32_t tmem_base;
   int pad;
-  float lse[4][kQRows];    // per softmax warp copy (no cross-warp barrier needed)
-  float delta[4][kQRows];
 };
 
 constexpr uint32_t kSmemK = 0;
 constexpr uint32_t kSmemV = kKVBytes;
 constexpr uint32_t kSmemQ0 = 2 * kKVBytes;                       // Q stage s at kSmemQ0 + s * 2 * kQBytes
-constexpr uint32_t kSmemP = kSmemQ0 + 4 * kQBytes;
+constexpr uint32_t kSmemP = kSmemQ0 + 2 * kStages * kQBytes;
 constexpr uint32_t kSmemDS = kSmemP + kPBytes;
-constexpr uint32_t kSmemBar = kSmemDS + kPBytes;
+constexpr uint32_t kSmemDQ = kSmemDS + kPBytes;                  // 2 x [32 rows][128] fp32 staging tiles
+constexpr int kDqRows = 32;                                         // rows per TMA reduce
+constexpr uint32_t kDqTileBytes = kDqRows * kHeadDim * 4;           // 16 KB
+constexpr uint32_t kSmemBar = kSmemDQ + 2 * kDqTileBytes;
 constexpr uint32_t kSmemBytes = kSmemBar + sizeof(Barriers) + 1024;
 
 __device__ __forceinline__ uint8_t* q_stage(uint8_t* b, int s) { return b + kSmemQ0 + s * 2 * kQBytes; }
@@ -93,17 +109,13 @@ __device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint3
       : "memory");
 }
 
-__device__ __forceinline__ void red_add_f32(float* addr, float v) {
-  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
-}
-
 // tcgen05.ld of 32 columns for the 32 lanes of this warp's quarter (ld + wait fused).
 __device__ __forceinline__ void ld32(uint32_t taddr, float (&v)[32]) { tmem_ld32(taddr, v); }
 
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_do,
-                    const BwdParams p) {
+                    const __grid_constant__ CUtensorMap map_dq, const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers* bar = reinterpret_cast<Barriers*>(smem + kSmemBar);
@@ -126,19 +138,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  unsigned long long* trace = (p.trace != nullptr && blockIdx.x == 0 && tile == p.trace_tile) ? p.trace : nullptr;
+  // Per-warp event marks (lane 0 of each warp): trace[(iteration * 14 + warp) * 4 + event].
+  auto wmark = [&](int it, int ev) {
+    if (trace != nullptr && it < 64 && lane == 0) trace[(it * 14 + warp) * 4 + ev] = global_timer_ns();
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&bar->qdo_full[s], 1);
       mbar_init(&bar->qdo_empty[s], 1);
     }
     mbar_init(&bar->sdp_full, 1);
-    mbar_init(&bar->s_free, 4);
-    mbar_init(&bar->ds_ready, 4);
+    mbar_init(&bar->s_free, 8);
+    mbar_init(&bar->ds_ready, 8);
     mbar_init(&bar->pds_free, 1);
-    mbar_init(&bar->dq_full, 1);
-    mbar_init(&bar->dq_free, 4);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar->dq_full[b], 1);
+      mbar_init(&bar->dq_free[b], 4);
+      mbar_init(&bar->dqs_full[b], 4);
+      mbar_init(&bar->dqs_free[b], 1);
+    }
     mbar_init(&bar->acc_full, 1);
     mbar_init(&bar->mma_done, 1);
     fence_mbarrier_init();
@@ -157,7 +178,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
-  const uint32_t tS = tmem, tdP = tmem + 64, tdQ = tmem + 128, tdV = tmem + 192, tdK = tmem + 320;
+  // TMEM columns: S^T 0-63, dP^T 64-127, dQ^T buffers 128-191 and 448-511, dV 192-319, dK 320-447.
+  const uint32_t tS = tmem, tdP = tmem + 64, tdV = tmem + 192, tdK = tmem + 320;
+  auto tdQb = [tmem](int b) -> uint32_t { return b ? tmem + 448 : tmem + 128; };
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -170,8 +193,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_load_2d(smem + kSmemV + kKVChunk, &map_v, &bar->kv_full, vx + 64, start + k0);
       int issued = 0;
       for (int i = 0; i < n; ++i) {
-        const int s = i & 1;
-        if (i >= 2 && !mbar_wait(&bar->qdo_empty[s], ((i >> 1) - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+        const int s = i % kStages;
+        if (i >= kStages && !mbar_wait(&bar->qdo_empty[s], ((i / kStages) - 1) & 1, p.status, kStatusTimeoutEmpty))
+          break;
+        wmark(i, 0);
         const int hq = kvh * group + i / nqb;
         const int row = start + (qfirst_block + i % nqb) * kQRows;
         const int qx = p.q_col + hq * kHeadDim, dox = hq * kHeadDim;
@@ -183,8 +208,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued = i + 1;
       }
       mbar_wait(&bar->kv_full, 0, p.status, kStatusTimeoutKV);
-      for (int i = max(0, issued - 2); i < issued; ++i)
-        mbar_wait(&bar->qdo_full[i & 1], (i >> 1) & 1, p.status, kStatusTimeoutQ);
+      for (int i = max(0, issued - kStages); i < issued; ++i)
+        mbar_wait(&bar->qdo_full[i % kStages], (i / kStages) & 1, p.status, kStatusTimeoutQ);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -195,10 +220,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t sk = smem_u32(smem + kSmemK), sv = smem_u32(smem + kSmemV);
       const uint32_t sp = smem_u32(smem + kSmemP), sds = smem_u32(smem + kSmemDS);
       bool ok = mbar_wait(&bar->kv_full, 0, p.status, kStatusTimeoutKV);
-      for (int i = 0; ok && i < n; ++i) {
-        const int s = i & 1;
-        if (!mbar_wait(&bar->qdo_full[s], (i >> 1) & 1, p.status, kStatusTimeoutQ)) { ok = false; break; }
-        if (i > 0 && !mbar_wait(&bar->s_free, (i - 1) & 1, p.status, kStatusTimeoutS)) { ok = false; break; }
+      // S^T/dP^T of block i+1 are issued before dV/dK/dQ of block i, so the softmax warps work
+      // on block i+1 while the tensor core runs block i's accumulations.
+      auto issue_sdp = [&](int i) -> bool {
+        const int s = i % kStages;
+        if (!mbar_wait(&bar->qdo_full[s], (i / kStages) & 1, p.status, kStatusTimeoutQ)) return false;
+        if (i > 0 && !mbar_wait(&bar->s_free, (i - 1) & 1, p.status, kStatusTimeoutS)) return false;
         tc_fence_after();
         const uint32_t sq = smem_u32(q_stage(smem, s)), sdo = smem_u32(do_stage(smem, s));
 #pragma unroll
@@ -211,9 +238,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                  k > 0);
         }
         mma_commit(&bar->sdp_full);
+        return true;
+      };
+      if (ok && n > 0) ok = issue_sdp(0);
+      for (int i = 0; ok && i < n; ++i) {
+        const int s = i % kStages;
+        if (i + 1 < n && !issue_sdp(i + 1)) { ok = false; break; }
+        wmark(i, 0);
         if (!mbar_wait(&bar->ds_ready, i & 1, p.status, kStatusTimeoutP)) { ok = false; break; }
-        if (i > 0 && !mbar_wait(&bar->dq_free, (i - 1) & 1, p.status, kStatusTimeoutO)) { ok = false; break; }
+        wmark(i, 1);
+        if (i >= 2 && !mbar_wait(&bar->dq_free[i & 1], ((i >> 1) - 1) & 1, p.status, kStatusTimeoutO)) { ok = false; break; }
+        wmark(i, 2);
         tc_fence_after();
+        const uint32_t sq = smem_u32(q_stage(smem, s)), sdo = smem_u32(do_stage(smem, s));
 #pragma unroll
         for (int k = 0; k < 4; ++k) {  // K-dim = 64 queries
           const uint64_t a_p = smem_desc(sp + k * 32, 16, 1024, kLayoutSW128);
@@ -227,90 +264,98 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < 8; ++k) {  // K-dim = 128 keys
           const uint64_t a_kt = smem_desc(sk + k * 2048, kKVChunk, 1024, kLayoutSW128);
           const uint64_t b_ds = smem_desc(sds + k * 2048, kPBytes, 1024, kLayoutSW128);
-          mma_ss(tdQ, a_kt, b_ds, id_dq, k > 0);
+          mma_ss(tdQb(i & 1), a_kt, b_ds, id_dq, k > 0);
         }
-        mma_commit(&bar->dq_full);
+        mma_commit(&bar->dq_full[i & 1]);
         mma_commit(&bar->pds_free);
         mma_commit(&bar->qdo_empty[s]);
+        wmark(i, 3);
       }
       mma_commit(&bar->acc_full);
       mma_commit(&bar->mma_done);
       mbar_wait(&bar->mma_done, 0, p.status, kStatusTimeoutOther);
     }
-  } else if (warp < 6) {
+  } else if (warp < 10) {
     // ------------------------------------------------------------ softmax / dS (thread = key row)
     const int wq = warp & 3;
+    const int half = (warp - 2) >> 2;        // which 32 query columns this warp owns
     const int r = wq * 32 + lane;
     const int key = k0 + r;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-    float* w_lse = bar->lse[wq];
-    float* w_delta = bar->delta[wq];
-    uint8_t* sP = smem + kSmemP;
-    uint8_t* sDS = smem + kSmemDS;
-    bool ok = true;
-    for (int i = 0; i < n; ++i) {
+    const uint32_t col_off = half * 32;
+    const uint32_t sP = smem_u32(smem + kSmemP);
+    const uint32_t sDS = smem_u32(smem + kSmemDS);
+    // LSE / Delta of this warp's 32 queries live in registers (lane l holds query 32*half + l)
+    // and are fetched one iteration ahead to hide the global latency.
+    auto fetch = [&](int i, float& lse2, float& dl) {
       const int hq = kvh * group + i / nqb;
       const int q0 = (qfirst_block + i % nqb) * kQRows;
-      __syncwarp();  // this warp's previous LSE/Delta copy fully consumed
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const int q = q0 + lane + 32 * h2;
-        const int64_t idx = (int64_t)hq * p.lse_ld + start + min(q, L - 1);
-        w_lse[lane + 32 * h2] = p.lse[idx];
-        w_delta[lane + 32 * h2] = p.delta[idx];
-      }
-      __syncwarp();
-      if (!mbar_wait(&bar->sdp_full, i & 1, p.status, kStatusTimeoutS)) { ok = false; break; }
+      const int64_t idx = (int64_t)hq * p.lse_ld + start + min(q0 + (int)col_off + lane, L - 1);
+      lse2 = p.lse[idx];
+      dl = p.delta[idx];
+    };
+    float cur_lse = 0.f, cur_dl = 0.f, nxt_lse = 0.f, nxt_dl = 0.f;
+    if (n > 0) fetch(0, cur_lse, cur_dl);
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+      const int q0 = (qfirst_block + i % nqb) * kQRows;
+      if (i + 1 < n) fetch(i + 1, nxt_lse, nxt_dl);
+      if (!warp_wait(&bar->sdp_full, i & 1, p.status, kStatusTimeoutS)) { ok = false; break; }
+      wmark(i, 0);
       tc_fence_after();
-      float sv[64], dpv[64];
-      {
-        float a[32], b[32];
-        ld32(tS + lane_off, a);
-        ld32(tdP + lane_off, b);
-#pragma unroll
-        for (int c = 0; c < 32; ++c) sv[c] = a[c], dpv[c] = b[c];
-        ld32(tS + lane_off + 32, a);
-        ld32(tdP + lane_off + 32, b);
-#pragma unroll
-        for (int c = 0; c < 32; ++c) sv[32 + c] = a[c], dpv[32 + c] = b[c];
-      }
+      float sv[32], dpv[32];
+      ld32(tS + lane_off + col_off, sv);
+      ld32(tdP + lane_off + col_off, dpv);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->s_free);
-      uint32_t pk[32], dk[32];
+      wmark(i, 1);
+      uint32_t pk[16], dk[16];
+      // Branch-free element loop: masked entries get an exponent argument of -inf (exp2 -> 0), so
+      // the compiler keeps one basic block and interleaves the 32 independent element chains.
       const bool full = (q0 + kQRows <= L) && (k0 + kKeys - 1 <= (q0 < P ? P - 1 : q0));
+      const int qbase = q0 + (int)col_off;
 #pragma unroll
-      for (int c = 0; c < 64; c += 2) {
+      for (int c = 0; c < 32; c += 2) {
         float pe[2], de[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int q = q0 + c + e;
+          const int col = c + e;
+          const float lse_c = __shfl_sync(0xffffffffu, cur_lse, col);
+          const float dl_c = __shfl_sync(0xffffffffu, cur_dl, col);
+          const int q = qbase + col;
           const int lim = q < P ? P - 1 : q;
-          const bool vis = full || (q < L && key <= lim);
-          const float pv = vis ? fast_exp2(fmaf(sv[c + e], p.scale_log2, -w_lse[c + e])) : 0.f;
+          const bool vis = full | ((q < L) & (key <= lim));
+          const float arg = vis ? fmaf(sv[col], p.scale_log2, -lse_c) : -INFINITY;
+          const float pv = fast_exp2(arg);
           pe[e] = pv;
-          de[e] = vis ? pv * (dpv[c + e] - w_delta[c + e]) : 0.f;
+          de[e] = pv * (dpv[col] - dl_c);
         }
         pk[c >> 1] = pack_bf16x2(pe[0], pe[1]);
         dk[c >> 1] = pack_bf16x2(de[0], de[1]);
       }
-      if (i > 0 && !mbar_wait(&bar->pds_free, (i - 1) & 1, p.status, kStatusTimeoutP)) { ok = false; break; }
+      wmark(i, 2);
+      if (i > 0 && !warp_wait(&bar->pds_free, (i - 1) & 1, p.status, kStatusTimeoutP)) { ok = false; break; }
+      wmark(i, 3);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u4 = 0; u4 < 4; ++u4) {
+        const int u = half * 4 + u4;  // 16-byte unit of the 128-byte row
         const uint32_t off = r * 128 + ((u ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(sP + off) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-        *reinterpret_cast<uint4*>(sDS + off) = make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+        st_shared_v4(sP + off, pk[4 * u4], pk[4 * u4 + 1], pk[4 * u4 + 2], pk[4 * u4 + 3]);
+        st_shared_v4(sDS + off, dk[4 * u4], dk[4 * u4 + 1], dk[4 * u4 + 2], dk[4 * u4 + 3]);
       }
       fence_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->ds_ready);
+      cur_lse = nxt_lse, cur_dl = nxt_dl;
     }
     // Epilogue: dK (scaled) and dV rows of this key block.
-    if (ok && mbar_wait(&bar->acc_full, 0, p.status, kStatusTimeoutO)) {
+    if (ok && warp_wait(&bar->acc_full, 0, p.status, kStatusTimeoutO)) {
       tc_fence_after();
       const bool valid = key < L;
       const int64_t row = (int64_t)start + key;
-      for (int which = 0; which < 2; ++which) {
+      {
+        const int which = half;  // half-0 warps write dK, half-1 warps write dV
         const uint32_t tacc = which == 0 ? tdK : tdV;
         __nv_bfloat16* out = which == 0 ? p.dk : p.dv;
         const float mul = which == 0 ? p.scale : 1.f;
@@ -339,26 +384,62 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int wq = warp & 3;
     const int d = wq * 32 + lane;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    const uint32_t sdq_addr = smem_u32(smem + kSmemDQ);
+    const bool issuer = (warp == 10 && lane == 0);
+    bool pending = false;
     for (int i = 0; i < n; ++i) {
       const int hq = kvh * group + i / nqb;
       const int q0 = (qfirst_block + i % nqb) * kQRows;
-      if (!mbar_wait(&bar->dq_full, i & 1, p.status, kStatusTimeoutO)) break;
+      const int b = i & 1;
+      if (!warp_wait(&bar->dq_full[b], (i >> 1) & 1, p.status, kStatusTimeoutO)) break;
+      wmark(i, 0);
       tc_fence_after();
-      float a[32], b[32];
-      ld32(tdQ + lane_off, a);
-      ld32(tdQ + lane_off + 32, b);
+      float a[32], c2[32];
+      ld32(tdQb(b) + lane_off, a);
+      ld32(tdQb(b) + lane_off + 32, c2);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->dq_free);
-      float* base = p.dq + ((int64_t)start + q0) * (int64_t)p.H * kHeadDim + (int64_t)hq * kHeadDim + d;
-      const int64_t ld = (int64_t)p.H * kHeadDim;
+      if (lane == 0) mbar_arrive(&bar->dq_free[b]);
+      wmark(i, 1);
+      // Two 32-row halves, alternating between two 16 KB staging tiles: transpose a half into
+      // [query][dim] and fold it into global dQ with one TMA reduce-add; the reduce of the
+      // previous half overlaps the staging of this one.
+      bool issued_ok = true;
 #pragma unroll
-      for (int c = 0; c < 32; ++c)
-        if (q0 + c < L) red_add_f32(base + c * ld, a[c] * p.scale);
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int ph = 2 * i + h2;   // staging phase
+        const int sb = ph & 1;       // staging tile
+        if (ph >= 2 && !warp_wait(&bar->dqs_free[sb], ((ph >> 1) - 1) & 1, p.status, kStatusTimeoutOther)) {
+          issued_ok = false;
+          break;
+        }
+        const uint32_t tile = sdq_addr + sb * kDqTileBytes;
+        const float* src = h2 == 0 ? a : c2;
 #pragma unroll
-      for (int c = 0; c < 32; ++c)
-        if (q0 + 32 + c < L) red_add_f32(base + (32 + c) * ld, b[c] * p.scale);
+        for (int c = 0; c < 32; ++c)
+          st_shared_f32(tile + (c * kHeadDim + d) * 4, (q0 + 32 * h2 + c < L) ? src[c] * p.scale : 0.f);
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->dqs_full[sb]);
+        bool ok2 = true;
+        if (issuer) {
+          ok2 = mbar_wait(&bar->dqs_full[sb], (ph >> 1) & 1, p.status, kStatusTimeoutOther);
+          if (ok2) {
+            tma_reduce_add_2d(&map_dq, smem + kSmemDQ + sb * kDqTileBytes, hq * kHeadDim, start + q0 + 32 * h2);
+            bulk_commit_group();
+            pending = true;
+            if (ph >= 1) {
+              bulk_wait_group_read1();          // the previous phase's reduce has read its tile
+              mbar_arrive(&bar->dqs_free[sb ^ 1]);
+            }
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, ok2 ? 1 : 0, 0)) { issued_ok = false; break; }
+      }
+      if (!issued_ok) break;
+      wmark(i, 3);
     }
+    if (issuer && pending) bulk_wait_group0();
   }
 
   tc_fence_before();
@@ -440,7 +521,8 @@ std::vector<at::Tensor> fmha_bwd_plan(at::Tensor cu_seqlens, at::Tensor prefix_l
 std::vector<at::Tensor> fmha_bwd(at::Tensor q_src, int64_t q_col, at::Tensor k_src, int64_t k_col, at::Tensor v_src,
                                  int64_t v_col, at::Tensor d_o, at::Tensor lse, at::Tensor delta, int64_t H,
                                  int64_t KV, bool is_causal, at::Tensor cu_seqlens, at::Tensor prefix_lens,
-                                 int64_t numseqs, at::Tensor kv_tiles, at::Tensor kv_ntiles) {
+                                 int64_t numseqs, at::Tensor kv_tiles, at::Tensor kv_ntiles,
+                                 c10::optional<at::Tensor> trace, int64_t trace_tile, int64_t mode) {
   for (const at::Tensor* t : {&q_src, &k_src, &v_src, &d_o}) {
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->stride(1) == 1,
                 "fmha_bwd: q/k/v/dO must be 2-D bf16 row-major CUDA tensors");
@@ -461,6 +543,7 @@ std::vector<at::Tensor> fmha_bwd(at::Tensor q_src, int64_t q_col, at::Tensor k_s
   CUtensorMap mk = make_tmap_bf16_2d(k_src.data_ptr(), T, k_src.size(1), k_src.stride(0), 64, kKeys);
   CUtensorMap mv = make_tmap_bf16_2d(v_src.data_ptr(), T, v_src.size(1), v_src.stride(0), 64, kKeys);
   CUtensorMap mdo = make_tmap_bf16_2d(d_o.data_ptr(), T, d_o.size(1), d_o.stride(0), 64, kQRows);
+  CUtensorMap mdq = make_tmap_f32_2d(dq.data_ptr(), T, dq.size(1), dq.size(1), kHeadDim, kDqRows);
   BwdParams prm{};
   prm.dq = dq.data_ptr<float>();
   prm.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
@@ -481,13 +564,19 @@ std::vector<at::Tensor> fmha_bwd(at::Tensor q_src, int64_t q_col, at::Tensor k_s
   prm.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
   prm.scale = 1.f / sqrtf((float)kHeadDim);
   prm.status = fmha_status_ptr(q_src.device());
+  if (trace.has_value()) {
+    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->numel() >= 64 * 14 * 4 && trace->is_cuda());
+    prm.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+    prm.trace_tile = (int)trace_tile;
+  }
+  prm.mode = (int)mode;
   static bool attr_set[16] = {false};
   if (!attr_set[q_src.device().index()]) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(fmha_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
     attr_set[q_src.device().index()] = true;
   }
   dim3 grid((unsigned)KV, (unsigned)kv_tiles.size(0));
-  fmha_bwd_kernel<<<grid, kThreads, kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(mq, mk, mv, mdo, prm);
+  fmha_bwd_kernel<<<grid, kThreads, kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(mq, mk, mv, mdo, mdq, prm);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {dq, dk, dv};
 }

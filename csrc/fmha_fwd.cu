@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
-  const uint32_t tS[2] = {tmem, tmem + 128};
+  auto tS = [tmem](int s) -> uint32_t { return s ? tmem + 128 : tmem; };
   const uint32_t tO = tmem + 256;
 
   if (warp == 0) {
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t off = (k >> 2) * kChunkBytes + (k & 3) * 32;
-          mma_ss(tS[s], smem_desc(sq + off, 16, 1024, kLayoutSW128), smem_desc(sk + off, 16, 1024, kLayoutSW128),
+          mma_ss(tS(s), smem_desc(sq + off, 16, 1024, kLayoutSW128), smem_desc(sk + off, 16, 1024, kLayoutSW128),
                  idesc_qk, k > 0 ? 1u : 0u);
         }
         mma_commit(&bar->s_full[s]);
@@ -233,17 +233,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lim = qpos < P ? P - 1 : qpos;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     float m_i = -INFINITY, l_i = 0.f;
-    uint8_t* sP = smem + kSmemP;
+    const uint32_t sP_addr = smem_u32(smem + kSmemP);
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int s = j & 1;
-      if (!mbar_wait(&bar->s_full[s], (j >> 1) & 1, p.status, kStatusTimeoutS)) { ok = false; break; }
+      if (!warp_wait(&bar->s_full[s], (j >> 1) & 1, p.status, kStatusTimeoutS)) { ok = false; break; }
       tc_fence_after();
       float sv[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float part[32];
-        tmem_ld32(tS[s] + lane_off + c * 32, part);
+        tmem_ld32(tS(s) + lane_off + c * 32, part);
 #pragma unroll
         for (int i = 0; i < 32; ++i) sv[c * 32 + i] = part[i];
       }
@@ -257,9 +257,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 128; ++c) sv[c] = c > rel ? -INFINITY : sv[c];
       }
-      float mx = sv[0];
+      float mxp[8];
 #pragma unroll
-      for (int c = 1; c < 128; ++c) mx = fmaxf(mx, sv[c]);
+      for (int e = 0; e < 8; ++e) mxp[e] = sv[e];
+#pragma unroll
+      for (int c = 8; c < 128; c += 8) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mxp[e] = fmaxf(mxp[e], sv[c + e]);
+      }
+      float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                       fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       mx *= p.scale_log2;
       float m_use = m_i, alpha = 1.f;
       bool rescale = false;
@@ -270,20 +277,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         alpha = fast_exp2(m_i - mx);
         rescale = true;
       }
-      float rowsum = 0.f;
+      float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint32_t pk[64];
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
         const float a = fast_exp2(fmaf(sv[2 * c], p.scale_log2, -m_use));
         const float b = fast_exp2(fmaf(sv[2 * c + 1], p.scale_log2, -m_use));
-        rowsum += a + b;
+        sums[c & 7] += a + b;
         pk[c] = pack_bf16x2(a, b);
       }
+      const float rowsum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
       l_i = l_i * alpha + rowsum;
       m_i = m_use;
 
       if (j > 0) {
-        if (!mbar_wait(&bar->o_done, (j - 1) & 1, p.status, kStatusTimeoutO)) { ok = false; break; }
+        if (!warp_wait(&bar->o_done, (j - 1) & 1, p.status, kStatusTimeoutO)) { ok = false; break; }
         tc_fence_after();
         if (__any_sync(0xffffffff, rescale)) {
 #pragma unroll
@@ -301,15 +309,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int u = 0; u < 16; ++u) {
         const int chunk = u >> 3, unit = u & 7;
-        uint8_t* dst = sP + chunk * kChunkBytes + r * 128 + ((unit ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        st_shared_v4(sP_addr + chunk * kChunkBytes + r * 128 + ((unit ^ (r & 7)) << 4), pk[4 * u], pk[4 * u + 1],
+                     pk[4 * u + 2], pk[4 * u + 3]);
       }
       fence_async_shared();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->p_full);
     }
-    if (ok && mbar_wait(&bar->o_done, (nkv - 1) & 1, p.status, kStatusTimeoutO)) {
+    if (ok && warp_wait(&bar->o_done, (nkv - 1) & 1, p.status, kStatusTimeoutO)) {
       tc_fence_after();
       const bool valid = qpos < L;
       const int64_t grow = (int64_t)start + qpos;

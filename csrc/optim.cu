@@ -11,13 +11,39 @@
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kChunk = kThreads * 16;  // elements per CTA
+constexpr int kChunk = kThreads * 4 * 8;  // elements per CTA (8 iterations of 4-wide vectors)
 
 struct TensorEntry {
   uint64_t p, g, m, v, e;
   int64_t n;
   int64_t block_start;
-  float lr, bc1, bc2_sqrt, pad;
+  float lr, bc1, bc2_sqrt;
+  int vec;  // all slot pointers 16-byte aligned: use 4-wide vector accesses
+};
+
+template <typename T>
+struct V4;
+template <>
+struct V4<float> {
+  __device__ static void load(const float* p, float (&f)[4]) {
+    const float4 u = *reinterpret_cast<const float4*>(p);
+    f[0] = u.x, f[1] = u.y, f[2] = u.z, f[3] = u.w;
+  }
+  __device__ static void store(float* p, const float (&f)[4]) {
+    *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+  }
+};
+template <>
+struct V4<__nv_bfloat16> {
+  __device__ static void load(const __nv_bfloat16* p, float (&f)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+    f[0] = a.x, f[1] = a.y, f[2] = b.x, f[3] = b.y;
+  }
+  __device__ static void store(__nv_bfloat16* p, const float (&f)[4]) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(mimir::pack_bf16x2(f[0], f[1]), mimir::pack_bf16x2(f[2], f[3]));
+  }
 };
 
 template <typename T>
@@ -58,6 +84,40 @@ __global__ void __launch_bounds__(kThreads) adam_atan2_kernel(const TensorEntry*
   const int64_t end = min(start + (int64_t)kChunk, t.n);
   const float decay = 1.f - t.lr * wd;
   const float step_size = t.lr / t.bc1;
+  if (t.vec) {
+    // 4-wide path: same arithmetic as the scalar loop below, one 16-byte (fp32) access per slot.
+    for (int64_t i = start + 4 * threadIdx.x; i + 3 < end; i += 4 * kThreads) {
+      float gi[4], pi[4], vi[4], mi[4], ei[4];
+      V4<P>::load(g + i, gi);
+      V4<P>::load(p + i, pi);
+      V4<P>::load(v + i, vi);
+      if (m != nullptr) V4<P>::load(m + i, mi);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (wd != 0.f) pi[k] = pi[k] * decay;
+        vi[k] = b2 * vi[k] + (1.f - b2) * gi[k] * gi[k];
+        const float denom = sqrtf(vi[k]) / t.bc2_sqrt;
+        if (m != nullptr) {
+          mi[k] = mi[k] + (1.f - b1) * (gi[k] - mi[k]);
+          pi[k] = pi[k] - step_size * atan2f(mi[k], denom);
+        } else {
+          pi[k] = pi[k] - t.lr * atan2f(gi[k], denom);
+        }
+      }
+      V4<P>::store(v + i, vi);
+      V4<P>::store(p + i, pi);
+      if (m != nullptr) V4<P>::store(m + i, mi);
+      if (e != nullptr) {
+        float stored[4];
+        V4<P>::load(p + i, stored);  // EMA follows the stored (rounded) parameter
+        V4<E>::load(e + i, ei);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ei[k] = ei[k] + (1.f - ema_decay) * (stored[k] - ei[k]);
+        V4<E>::store(e + i, ei);
+      }
+    }
+    return;  // vec tensors have n % 4 == 0, so the chunk is fully covered
+  }
   for (int64_t i = start + threadIdx.x; i < end; i += kThreads) {
     const float gi = ld(g + i);
     float pi = ld(p + i);
@@ -126,6 +186,9 @@ void adam_atan2_multi(std::vector<at::Tensor> params, std::vector<at::Tensor> gr
     tab[i].lr = (float)lrs[i];
     tab[i].bc1 = (float)bc1[i];
     tab[i].bc2_sqrt = (float)bc2_sqrt[i];
+    auto al = [](uint64_t ptr) { return ptr % 16 == 0; };
+    tab[i].vec = (p.numel() % 4 == 0) && al(tab[i].p) && al(tab[i].g) && al(tab[i].v) && (tab[i].m == 0 || al(tab[i].m)) &&
+                 (tab[i].e == 0 || al(tab[i].e));
     blocks += (p.numel() + kChunk - 1) / kChunk;
   }
   if (blocks == 0) return;

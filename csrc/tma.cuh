@@ -40,4 +40,22 @@ inline CUtensorMap make_tmap_bf16_2d(const void* base, int64_t rows, int64_t col
   return map;
 }
 
+// Row-major fp32 matrix [rows, cols] (leading dimension `ld` elements), no swizzle; used as
+// the destination of TMA reduce-add stores.
+inline CUtensorMap make_tmap_f32_2d(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_cols,
+                                    int box_rows) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((ld * 4) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
+                                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (f32) failed with code ", (int)r);
+  return map;
+}
+
 }  // namespace mimir
