@@ -26,6 +26,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "fmha_noalloc.h"
 #include "tma.cuh"
 
 using namespace mimir;
@@ -517,4 +518,97 @@ int64_t fmha_status(at::Device dev) {
   C10_CUDA_CHECK(cudaMemcpy(&host, w, sizeof(int), cudaMemcpyDeviceToHost));
   if (host != 0) C10_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
   return host;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free entry point (declared in fmha_noalloc.h; no counterpart in the reference).
+// Scratch lives in file-scope device arrays; host code only ever passes the addresses that
+// cudaGetSymbolAddress returns for the current device.
+namespace {
+static __device__ __align__(256) int2 g_noalloc_tiles[MIMIR_FMHA_NOALLOC_MAX_TILES];
+static __device__ __align__(256) int g_noalloc_words[64];  // [0] tile count, [1] kernel status
+
+struct NoAllocScratch {
+  int2* tiles = nullptr;
+  int* words = nullptr;
+  bool ready = false;
+};
+NoAllocScratch g_scratch[64];
+
+int noalloc_setup(int device) {
+  if (device < 0 || device >= 64) return MIMIR_NOALLOC_ERR_ARGS;
+  NoAllocScratch& s = g_scratch[device];
+  if (s.ready) return MIMIR_NOALLOC_OK;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.tiles), g_noalloc_tiles) != cudaSuccess)
+    return MIMIR_NOALLOC_ERR_CUDA;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.words), g_noalloc_words) != cudaSuccess)
+    return MIMIR_NOALLOC_ERR_CUDA;
+  if (cudaFuncSetAttribute(fmha_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+    return MIMIR_NOALLOC_ERR_CUDA;
+  s.ready = true;
+  return MIMIR_NOALLOC_OK;
+}
+
+bool make_tmap_noexcept(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0 || (ld * 2) % 16 != 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)kTile};
+  cuuint32_t estr[2] = {1, 1};
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || fn == nullptr)
+    return false;
+  auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
+extern "C" int mimir_fmha_fwd_noalloc(const void* q, int64_t q_ld, const void* k, int64_t k_ld, const void* v,
+                                      int64_t v_ld, void* out, float* lse, int64_t lse_ld, const int* cu_seqlens,
+                                      const int* prefix_lens, int numseqs, int64_t total_tokens, int num_heads,
+                                      int num_kv_heads, int is_causal, cudaStream_t stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || lse == nullptr || cu_seqlens == nullptr ||
+      (prefix_lens == nullptr && !is_causal) || numseqs < 0 || total_tokens < 0 || num_heads <= 0 ||
+      num_kv_heads <= 0 || num_heads % num_kv_heads != 0 || lse_ld < total_tokens ||
+      q_ld < (int64_t)num_heads * kHeadDim || k_ld < (int64_t)num_kv_heads * kHeadDim ||
+      v_ld < (int64_t)num_kv_heads * kHeadDim)
+    return MIMIR_NOALLOC_ERR_ARGS;
+  if (total_tokens == 0 || numseqs == 0) return MIMIR_NOALLOC_OK;
+  const int64_t max_tiles = (total_tokens + kTile - 1) / kTile + numseqs;
+  if (max_tiles > MIMIR_FMHA_NOALLOC_MAX_TILES || max_tiles > 65535) return MIMIR_NOALLOC_ERR_TOO_LARGE;
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess) return MIMIR_NOALLOC_ERR_CUDA;
+  const int rc = noalloc_setup(device);
+  if (rc != MIMIR_NOALLOC_OK) return rc;
+  NoAllocScratch& s = g_scratch[device];
+  CUtensorMap mq, mk, mv;
+  if (!make_tmap_noexcept(&mq, q, total_tokens, q_ld, q_ld) || !make_tmap_noexcept(&mk, k, total_tokens, k_ld, k_ld) ||
+      !make_tmap_noexcept(&mv, v, total_tokens, v_ld, v_ld))
+    return MIMIR_NOALLOC_ERR_ARGS;
+  // The status word must start at zero; the tile count is rewritten by the schedule kernel.
+  if (cudaMemsetAsync(s.words + 1, 0, sizeof(int), stream) != cudaSuccess) return MIMIR_NOALLOC_ERR_CUDA;
+  // A causal call never reads prefix_lens; the schedule kernel gets the cu_seqlens pointer as a
+  // harmless stand-in so it never dereferences a null pointer.
+  const int* prefix = is_causal ? cu_seqlens : prefix_lens;
+  build_tiles_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, prefix, numseqs, is_causal ? 1 : 0, s.tiles, s.words,
+                                             (int)max_tiles);
+  FwdParams prm{};
+  prm.y = reinterpret_cast<__nv_bfloat16*>(out);
+  prm.lse = lse;
+  prm.lse_ld = lse_ld;
+  prm.cu_seqlens = cu_seqlens;
+  prm.prefix_lens = prefix;
+  prm.tiles = s.tiles;
+  prm.ntiles = s.words;
+  prm.H = num_heads;
+  prm.KV = num_kv_heads;
+  prm.is_causal = is_causal ? 1 : 0;
+  prm.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
+  prm.status = s.words + 1;
+  dim3 grid((unsigned)num_heads, (unsigned)max_tiles);
+  fmha_fwd_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, prm);
+  return cudaGetLastError() == cudaSuccess ? MIMIR_NOALLOC_OK : MIMIR_NOALLOC_ERR_CUDA;
 }
