@@ -3,7 +3,7 @@ import glob
 import os
 
 from setuptools import find_packages, setup
-from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
 
 os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -13,6 +13,7 @@ if os.environ.get("MIMIR_PTXAS_VERBOSE") == "1":
     NVCC_FLAGS += ["-Xptxas", "-v"]
 
 sources = sorted(glob.glob(os.path.join("csrc", "*.cu"))) + ["csrc/bindings.cpp"]
+host_sources = sorted(glob.glob(os.path.join("csrc", "host", "*.cpp")))
 
 setup(
     name="mimir_b200",
@@ -21,7 +22,9 @@ setup(
     package_data={"mimir_b200": ["conf/**/*.yaml", "evaluation/suites/*.json"]},
     ext_modules=[CUDAExtension("mimir_b200._C", sources=sources,
                                include_dirs=[os.path.join(HERE, "csrc")],
-                               extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS})],
+                               extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS}),
+                 CppExtension("mimir_b200._host", sources=host_sources,
+                              extra_compile_args={"cxx": ["-O3", "-std=c++17"]})],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
     entry_points={"console_scripts": ["mimir=mimir_b200.cli:main"]},
 )
