@@ -1,0 +1,156 @@
+"""Command line: ``python -m mimir_b200 <command>``.
+
+Commands mirror the reference CLI (``src/mimir/cli.py:11-98``): ``train`` (Hydra-style
+overrides passed through unchanged, ``--suspendable``), ``checkpoint import``, ``export``,
+``serve``, ``eval``, ``schedule``, ``monitor`` and ``doctor``.  Built on argparse.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+from pathlib import Path
+
+
+def _train(args, rest):
+    from mimir_b200.train.entry import run
+    run(rest, suspendable=args.suspendable)
+
+
+def _import(args, _rest):
+    from mimir_b200.ckpt.importer import import_legacy
+    import_legacy(args.source, args.output, tag=args.tag, mode=args.mode)
+
+
+def _export(args, _rest):
+    from mimir_b200.export.convert import export
+    export(args.checkpoint, args.output, args.tokenizer, ema=args.ema)
+
+
+def _serve(args, _rest):
+    from mimir_b200.serving.server import serve
+    serve(args.model, args.port, args.gpus, eager=args.eager)
+
+
+def _eval(args, _rest):
+    from mimir_b200.evaluation.clients import evaluate
+    print(json.dumps(evaluate(str(args.suite), args.model, str(args.output), args.base_url)))
+
+
+def _schedule(args, _rest):
+    from mimir_b200.scheduling.store import Store
+    store = Store(args.database)
+    if args.hold_job:
+        store.hold(args.hold_job, True)
+    if args.release_job:
+        store.hold(args.release_job, False)
+    if args.backup:
+        store.backup(args.backup)
+    if args.edit_job:
+        if args.config_file is None:
+            raise SystemExit("--edit-job requires --config-file")
+        store.edit(args.edit_job, json.loads(args.config_file.read_text()))
+    if args.plan:
+        for row in json.loads(args.plan.read_text())["jobs"]:
+            store.add(row["id"], row["kind"], row["config"],
+                      [(d["id"], d.get("policy", "success")) for d in row.get("depends", [])],
+                      row.get("max_attempts", 3), held=row.get("held", False))
+    if args.run:
+        from mimir_b200.scheduling.worker import recover_abandoned, run_one
+        from mimir_b200.serving.server import ServerPool
+        from mimir_b200.train.suspension.protocol import exclusive
+        with exclusive(args.database.with_suffix(".runner.lock")):
+            pool = ServerPool(args.database.parent / "servers")
+            try:
+                recover_abandoned(store, args.database.parent / "attempts")
+                while run_one(store, args.database.parent / "attempts", pool):
+                    pass
+            finally:
+                pool.close()
+    print(json.dumps(store.rows(), indent=2))
+
+
+def _monitor(args, _rest):
+    from mimir_b200.scheduling.monitor import monitor
+    from mimir_b200.scheduling.store import Store
+    monitor(Store(args.database), args.watch)
+
+
+def _doctor(_args, _rest):
+    """Read-only dependency and capability report; never allocates a GPU."""
+    from importlib.metadata import PackageNotFoundError, version
+    out = {}
+    for name in ("torch", "transformers", "vllm", "numpy", "pydantic"):
+        try:
+            out[name] = version(name)
+        except PackageNotFoundError:
+            out[name] = "not installed"
+    from mimir_b200.ops import _ext
+    out["mimir_b200._C"] = "built" if _ext.available() else "missing"
+    try:
+        from mimir_b200 import _host  # noqa: F401
+        out["mimir_b200._host"] = "built"
+    except ImportError:
+        out["mimir_b200._host"] = "missing"
+    print(json.dumps(out, indent=2))
+
+
+def parser() -> argparse.ArgumentParser:
+    p = argparse.ArgumentParser(prog="mimir_b200")
+    sub = p.add_subparsers(dest="command", required=True)
+    t = sub.add_parser("train", help="train with config overrides, e.g. size@arch=XXS")
+    t.add_argument("--suspendable", action="store_true")
+    t.set_defaults(fn=_train)
+    ck = sub.add_parser("checkpoint").add_subparsers(dest="action", required=True)
+    im = ck.add_parser("import", help="explicit one-way legacy checkpoint import")
+    im.add_argument("source", type=Path)
+    im.add_argument("output", type=Path)
+    im.add_argument("--mode", required=True, choices=("exact", "weights"))
+    im.add_argument("--tag", required=True)
+    im.set_defaults(fn=_import)
+    ex = sub.add_parser("export", help="convert a checkpoint to a Hugging Face directory")
+    ex.add_argument("checkpoint", type=Path)
+    ex.add_argument("output", type=Path)
+    ex.add_argument("--tokenizer", type=Path, required=True)
+    ex.add_argument("--ema", action=argparse.BooleanOptionalAction, default=True)
+    ex.set_defaults(fn=_export)
+    sv = sub.add_parser("serve")
+    sv.add_argument("model", type=Path)
+    sv.add_argument("--port", type=int, default=8000)
+    sv.add_argument("--gpus", required=True)
+    sv.add_argument("--eager", action="store_true")
+    sv.set_defaults(fn=_serve)
+    ev = sub.add_parser("eval")
+    ev.add_argument("suite", type=Path)
+    ev.add_argument("model")
+    ev.add_argument("output", type=Path)
+    ev.add_argument("--base-url", default="http://127.0.0.1:8000/v1")
+    ev.set_defaults(fn=_eval)
+    sc = sub.add_parser("schedule")
+    sc.add_argument("database", type=Path)
+    sc.add_argument("--plan", type=Path)
+    sc.add_argument("--run", action="store_true")
+    sc.add_argument("--hold-job")
+    sc.add_argument("--release-job")
+    sc.add_argument("--backup", type=Path)
+    sc.add_argument("--edit-job")
+    sc.add_argument("--config-file", type=Path)
+    sc.set_defaults(fn=_schedule)
+    mo = sub.add_parser("monitor")
+    mo.add_argument("database", type=Path)
+    mo.add_argument("--watch", action="store_true")
+    mo.set_defaults(fn=_monitor)
+    sub.add_parser("doctor").set_defaults(fn=_doctor)
+    return p
+
+
+def main(argv=None) -> None:
+    argv = sys.argv[1:] if argv is None else list(argv)
+    args, rest = parser().parse_known_args(argv)
+    if rest and args.command != "train":
+        parser().error(f"unrecognized arguments: {' '.join(rest)}")
+    args.fn(args, rest)
+
+
+if __name__ == "__main__":
+    main()
