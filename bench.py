@@ -186,7 +186,7 @@ def run_ours(args, rank, world, local):
     vocab = arch.pop("vocab_size")
     config = PretrainConfig(arch=arch, data=dict(path="synthetic"), global_batch_size=SEQ_LEN * SEQS_PER_GPU * world,
                             epochs=1, lr=3e-4, lr_warmup_steps=0, lr_min_ratio=1.0, weight_decay=0.1, beta1=0.9,
-                            beta2=0.95, ema=0.9999, distributed_strategy="fsdp", lr_auto=False)
+                            beta2=0.95, ema=0.9999, distributed_strategy=args.dp, lr_auto=False)
     torch.manual_seed(0)
     model, carry, optim = create_model_and_optimizer(config, {"vocab_size": vocab, "max_seq_len": SEQ_LEN}, device)
     state = make_train_state(config, model, carry, optim, total_steps=10_000, device=device)
@@ -221,8 +221,10 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     e2e_seconds = max_over_ranks(time.perf_counter() - t0)
     flops = model_flops_per_step(hosts[0][0], MODEL["num_key_value_heads"])
+    label = (f"dp{world}: replicated bf16 weights, fp32 master+AdamATan2 state sharded like FSDP2, one fused "
+             "NVLink reduce-scatter+update+all-gather kernel per step" if args.dp == "replicated" else f"fsdp{world}")
     return emit(args, world, seconds, e2e_seconds, h2d, 4, flops, clock_info, launches, impl="ours",
-                extra={"final_loss": losses[-1]})
+                extra={"final_loss": losses[-1], "parallelism": label})
 
 
 # ---------------------------------------------------------------------------------------- reference arm
@@ -346,7 +348,8 @@ def emit(args, world, seconds, e2e_seconds, h2d_bytes, d2h_bytes, flops_per_step
         "data": "synthetic uniform token ids, random-init weights",
         "config": {"model": "Mimir2 dense ~1.3B (24x2048, 16Q/4KV heads x128, SwiGLU 5632, vocab 65536)",
                    "global_batch": SEQ_LEN * SEQS_PER_GPU * world, "seq_len": SEQ_LEN, "micro_batch": SEQS_PER_GPU,
-                   "parallelism": f"fsdp{world}", "mask": "prefix-LM, prompt length uniform [0,2048]",
+                   "parallelism": (extra or {}).pop("parallelism", f"fsdp{world}"),
+                   "mask": "prefix-LM, prompt length uniform [0,2048]",
                    "optimizer": "AdamATan2 + EMA", "l2": "inputs larger than L2 (weights+activations >> 126 MB)"},
         "mfu": round(achieved / 2.25e15, 4),
         "frac_of_measured_bf16": round(achieved / (peaks.get("bf16_tflops_sustained", 1422.4) * 1e12), 4),
@@ -370,6 +373,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--dp", choices=["replicated", "fsdp"], default="replicated",
+                    help="data-parallel engine of our arm (the reference arm always uses its FSDP2)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

@@ -41,6 +41,20 @@ std::vector<at::Tensor> fmha_bwd(at::Tensor q_src, int64_t q_col, at::Tensor k_s
                                  int64_t numseqs, at::Tensor kv_tiles, at::Tensor kv_ntiles,
                                  c10::optional<at::Tensor> trace, int64_t trace_tile, int64_t mode);
 
+// dp_fused.cu
+int64_t dp_segment_bytes();
+int64_t dp_chunk_elements();
+void dp_step(std::vector<int64_t> peer_grads, std::vector<int64_t> peer_weights, at::Tensor segs, int64_t nblocks,
+             at::Tensor master, c10::optional<at::Tensor> exp_avg, at::Tensor exp_avg_sq, c10::optional<at::Tensor> ema,
+             c10::optional<at::Tensor> reduced, c10::optional<at::Tensor> grad_scale, double b1, double b2,
+             double ema_decay);
+void dp_reduce(std::vector<int64_t> peer_grads, at::Tensor segs, int64_t nblocks, at::Tensor reduced_out,
+               at::Tensor sumsq_out);
+std::vector<at::Tensor> ipc_alloc(int64_t nbytes, int64_t device);
+int64_t ipc_open(at::Tensor handle_bytes, int64_t device);
+void ipc_close(int64_t ptr, int64_t device);
+bool peer_access_possible(int64_t device, int64_t peer);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mimir_b200 hand-written sm_100a kernels";
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
@@ -60,6 +74,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fmha_fwd", &fmha_fwd);
   m.def("fmha_status", &fmha_status);
   m.def("fmha_bwd_plan", &fmha_bwd_plan);
+  m.def("dp_segment_bytes", &dp_segment_bytes);
+  m.def("dp_chunk_elements", &dp_chunk_elements);
+  m.def("dp_step", &dp_step);
+  m.def("dp_reduce", &dp_reduce);
+  m.def("ipc_alloc", &ipc_alloc);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("peer_access_possible", &peer_access_possible);
   m.def("fmha_bwd", &fmha_bwd, py::arg("q_src"), py::arg("q_col"), py::arg("k_src"), py::arg("k_col"),
         py::arg("v_src"), py::arg("v_col"), py::arg("d_o"), py::arg("lse"), py::arg("delta"), py::arg("H"),
         py::arg("KV"), py::arg("is_causal"), py::arg("cu_seqlens"), py::arg("prefix_lens"), py::arg("numseqs"),

@@ -1,0 +1,336 @@
+// Replicated-weight data parallelism over NVLink peer memory: one kernel per optimizer step
+// reduce-scatters the ranks' bf16 gradients, applies AdamATan2 to this rank's fp32 master shard
+// and all-gathers the new bf16 weights, all through direct loads/stores to the peers' buffers.
+//
+// Layout.  Every rank holds the full model twice in bf16 (weights and gradients), in one flat
+// buffer each, allocated with cudaMalloc and exported with CUDA IPC so every peer can map it.
+// Parameter p occupies [flat_p, flat_p + numel_p); rank r owns rows [r*c, min(R, (r+1)*c)) of p
+// (c = ceil(R / world), the same split FSDP2 uses, so the fp32 shards checkpoint identically).
+// The owned ranges of all parameters are the rank's "segments"; its fp32 master weights and
+// moments are stored back to back in segment order.
+//
+// Kernel (one CTA per 8192-element chunk of a segment):
+//   g   = sum_k grad_k[flat + i]   (peer loads, fixed rank order, fp32)
+//   g  *= grad_scale               (global clipping coefficient or 1)
+//   w   = w * (1 - lr*wd);  v = b2 v + (1-b2) g^2;  m += (1-b1)(g - m)
+//   w  -= lr/bc1 * atan2(m, sqrt(v)/bc2_sqrt)     (or lr * atan2(g, .) without first moment)
+//   ema += (1-d)(w - ema)
+//   param_k[flat + i] = bf16(w) for every rank k  (peer stores)
+// A reduce-only variant writes the fp32 reduced gradient shard and per-CTA sums of squares for
+// global-norm clipping; the update variant can then read that shard instead of the peers.
+//
+// The caller orders the step with the other ranks (a collective before: every rank's backward
+// is complete; and after: every rank's stores have landed).  Nothing here waits on a peer.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kVec = 8;                              // bf16 elements per 16-byte access
+constexpr int kIters = 4;
+constexpr int kChunk = kThreads * kVec * kIters;     // 8192 elements per CTA
+constexpr int kMaxRanks = 8;
+
+struct Segment {
+  int64_t flat;         // element offset in the flat bf16 weight/grad buffers
+  int64_t shard;        // element offset in the fp32 shard buffers
+  int64_t n;            // elements
+  int64_t block_start;  // first chunk index
+  float lr, wd, bc1, bc2_sqrt;
+  int32_t vec;          // flat % 8 == 0, shard % 8 == 0, n % 8 == 0
+  int32_t pad;
+};
+
+struct Peers {
+  uint64_t grad[kMaxRanks];
+  uint64_t weight[kMaxRanks];
+};
+
+struct StepArgs {
+  const Segment* segs;
+  int nsegs;
+  int world;
+  float* master;
+  float* exp_avg;        // nullptr without a first moment
+  float* exp_avg_sq;
+  float* ema;            // nullptr without EMA
+  const float* reduced;  // update variant: read gradients from here instead of the peers
+  float* reduced_out;    // reduce variant: write the reduced gradient shard here
+  float* sumsq_out;      // reduce variant: one partial sum of squares per CTA
+  const float* grad_scale;  // device scalar (clip coefficient) or nullptr for 1
+  float b1, b2, ema_decay;
+};
+
+__device__ __forceinline__ int find_segment(const Segment* segs, int n, int64_t b) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (segs[mid].block_start <= b) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 t = __bfloat1622float2(h[k]);
+    f[2 * k] = t.x;
+    f[2 * k + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  return make_uint4(mimir::pack_bf16x2(f[0], f[1]), mimir::pack_bf16x2(f[2], f[3]), mimir::pack_bf16x2(f[4], f[5]),
+                    mimir::pack_bf16x2(f[6], f[7]));
+}
+
+__device__ __forceinline__ void ld8(const float* p, float (&f)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  f[0] = a.x, f[1] = a.y, f[2] = a.z, f[3] = a.w, f[4] = b.x, f[5] = b.y, f[6] = b.z, f[7] = b.w;
+}
+
+__device__ __forceinline__ void st8(float* p, const float (&f)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(f[4], f[5], f[6], f[7]);
+}
+
+// Gradient of 8 consecutive elements summed over the ranks (fixed order 0..world-1).
+__device__ __forceinline__ void reduce8(const Peers& peers, int world, int64_t flat, float (&g)[8]) {
+  uint4 raw[kMaxRanks];
+#pragma unroll
+  for (int k = 0; k < kMaxRanks; ++k)
+    if (k < world) raw[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peers.grad[k]) + flat);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) g[e] = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxRanks; ++k) {
+    if (k < world) {
+      float f[8];
+      unpack8(raw[k], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) g[e] += f[e];
+    }
+  }
+}
+
+__device__ __forceinline__ float reduce1(const Peers& peers, int world, int64_t flat) {
+  float g = 0.f;
+  for (int k = 0; k < world; ++k) g += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(peers.grad[k])[flat]);
+  return g;
+}
+
+__device__ __forceinline__ float adam1(float g, float& w, float* m, float& v, float* e, const Segment& s,
+                                       const StepArgs& a) {
+  if (s.wd != 0.f) w = w * (1.f - s.lr * s.wd);
+  v = a.b2 * v + (1.f - a.b2) * g * g;
+  const float denom = sqrtf(v) / s.bc2_sqrt;
+  if (m != nullptr) {
+    *m = *m + (1.f - a.b1) * (g - *m);
+    w = w - (s.lr / s.bc1) * atan2f(*m, denom);
+  } else {
+    w = w - s.lr * atan2f(g, denom);
+  }
+  if (e != nullptr) *e = *e + (1.f - a.ema_decay) * (w - *e);
+  return w;
+}
+
+template <bool kFromPeers>
+__global__ void __launch_bounds__(kThreads) dp_update_kernel(const __grid_constant__ Peers peers, const StepArgs a) {
+  const Segment s = a.segs[find_segment(a.segs, a.nsegs, blockIdx.x)];
+  const int64_t start = (int64_t(blockIdx.x) - s.block_start) * kChunk;
+  const int64_t end = min(start + int64_t(kChunk), s.n);
+  const float scale = a.grad_scale != nullptr ? *a.grad_scale : 1.f;
+  if (s.vec) {
+    for (int64_t i = start + int64_t(threadIdx.x) * kVec; i < end; i += int64_t(kThreads) * kVec) {
+      const int64_t sh = s.shard + i;
+      float g[8], w[8], v[8], m[8], e[8];
+      if (kFromPeers) reduce8(peers, a.world, s.flat + i, g);
+      else ld8(a.reduced + sh, g);
+      ld8(a.master + sh, w);
+      ld8(a.exp_avg_sq + sh, v);
+      if (a.exp_avg != nullptr) ld8(a.exp_avg + sh, m);
+      if (a.ema != nullptr) ld8(a.ema + sh, e);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        adam1(g[k] * scale, w[k], a.exp_avg != nullptr ? &m[k] : nullptr, v[k], a.ema != nullptr ? &e[k] : nullptr, s, a);
+      st8(a.master + sh, w);
+      st8(a.exp_avg_sq + sh, v);
+      if (a.exp_avg != nullptr) st8(a.exp_avg + sh, m);
+      if (a.ema != nullptr) st8(a.ema + sh, e);
+      const uint4 packed = pack8(w);
+#pragma unroll
+      for (int k = 0; k < kMaxRanks; ++k)
+        if (k < a.world) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers.weight[k]) + s.flat + i) = packed;
+    }
+  } else {
+    for (int64_t i = start + threadIdx.x; i < end; i += kThreads) {
+      const int64_t sh = s.shard + i;
+      const float g = (kFromPeers ? reduce1(peers, a.world, s.flat + i) : a.reduced[sh]) * scale;
+      float w = a.master[sh], v = a.exp_avg_sq[sh];
+      w = adam1(g, w, a.exp_avg != nullptr ? a.exp_avg + sh : nullptr, v, a.ema != nullptr ? a.ema + sh : nullptr, s, a);
+      a.master[sh] = w;
+      a.exp_avg_sq[sh] = v;
+      const __nv_bfloat16 b = __float2bfloat16(w);
+      for (int k = 0; k < a.world; ++k) reinterpret_cast<__nv_bfloat16*>(peers.weight[k])[s.flat + i] = b;
+    }
+  }
+  __threadfence_system();  // peer stores are visible before the caller's closing collective
+}
+
+__global__ void __launch_bounds__(kThreads) dp_reduce_kernel(const __grid_constant__ Peers peers, const StepArgs a) {
+  const Segment s = a.segs[find_segment(a.segs, a.nsegs, blockIdx.x)];
+  const int64_t start = (int64_t(blockIdx.x) - s.block_start) * kChunk;
+  const int64_t end = min(start + int64_t(kChunk), s.n);
+  float sq = 0.f;
+  if (s.vec) {
+    for (int64_t i = start + int64_t(threadIdx.x) * kVec; i < end; i += int64_t(kThreads) * kVec) {
+      float g[8];
+      reduce8(peers, a.world, s.flat + i, g);
+      st8(a.reduced_out + s.shard + i, g);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sq += g[k] * g[k];
+    }
+  } else {
+    for (int64_t i = start + threadIdx.x; i < end; i += kThreads) {
+      const float g = reduce1(peers, a.world, s.flat + i);
+      a.reduced_out[s.shard + i] = g;
+      sq += g * g;
+    }
+  }
+  // deterministic block sum: warp shuffles, then warp 0 over the warp partials
+  __shared__ float part[kThreads / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < kThreads / 32 ? part[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) a.sumsq_out[blockIdx.x] = t;
+  }
+}
+
+Peers make_peers(const std::vector<int64_t>& grads, const std::vector<int64_t>& weights) {
+  TORCH_CHECK(grads.size() == weights.size() && grads.size() >= 1 && grads.size() <= kMaxRanks,
+              "dp step supports 1..", kMaxRanks, " ranks");
+  Peers p{};
+  for (size_t k = 0; k < grads.size(); ++k) {
+    TORCH_CHECK(grads[k] % 16 == 0 && weights[k] % 16 == 0, "peer buffers must be 16-byte aligned");
+    p.grad[k] = static_cast<uint64_t>(grads[k]);
+    p.weight[k] = static_cast<uint64_t>(weights[k]);
+  }
+  return p;
+}
+
+StepArgs make_args(at::Tensor segs, int64_t world, at::Tensor master, c10::optional<at::Tensor> exp_avg,
+                   at::Tensor exp_avg_sq, c10::optional<at::Tensor> ema, c10::optional<at::Tensor> grad_scale,
+                   double b1, double b2, double ema_decay) {
+  TORCH_CHECK(segs.is_cuda() && segs.dtype() == at::kByte && segs.numel() % sizeof(Segment) == 0, "bad segment table");
+  for (const at::Tensor* t : {&master, &exp_avg_sq})
+    TORCH_CHECK(t->is_cuda() && t->dtype() == at::kFloat && t->is_contiguous(), "fp32 contiguous shard buffers");
+  StepArgs a{};
+  a.segs = reinterpret_cast<const Segment*>(segs.data_ptr());
+  a.nsegs = static_cast<int>(segs.numel() / sizeof(Segment));
+  a.world = static_cast<int>(world);
+  a.master = master.data_ptr<float>();
+  a.exp_avg = exp_avg ? exp_avg->data_ptr<float>() : nullptr;
+  a.exp_avg_sq = exp_avg_sq.data_ptr<float>();
+  a.ema = ema ? ema->data_ptr<float>() : nullptr;
+  a.grad_scale = grad_scale ? grad_scale->data_ptr<float>() : nullptr;
+  a.b1 = static_cast<float>(b1);
+  a.b2 = static_cast<float>(b2);
+  a.ema_decay = static_cast<float>(ema_decay);
+  return a;
+}
+
+}  // namespace
+
+// Segment table entry size (bytes), for the host-side packer.
+int64_t dp_segment_bytes() { return sizeof(Segment); }
+
+int64_t dp_chunk_elements() { return kChunk; }
+
+void dp_step(std::vector<int64_t> peer_grads, std::vector<int64_t> peer_weights, at::Tensor segs, int64_t nblocks,
+             at::Tensor master, c10::optional<at::Tensor> exp_avg, at::Tensor exp_avg_sq, c10::optional<at::Tensor> ema,
+             c10::optional<at::Tensor> reduced, c10::optional<at::Tensor> grad_scale, double b1, double b2,
+             double ema_decay) {
+  const c10::cuda::CUDAGuard guard(master.device());
+  const Peers peers = make_peers(peer_grads, peer_weights);
+  StepArgs a = make_args(segs, peer_grads.size(), master, exp_avg, exp_avg_sq, ema, grad_scale, b1, b2, ema_decay);
+  if (nblocks == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (reduced) {
+    a.reduced = reduced->data_ptr<float>();
+    dp_update_kernel<false><<<static_cast<unsigned>(nblocks), kThreads, 0, stream>>>(peers, a);
+  } else {
+    dp_update_kernel<true><<<static_cast<unsigned>(nblocks), kThreads, 0, stream>>>(peers, a);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dp_reduce(std::vector<int64_t> peer_grads, at::Tensor segs, int64_t nblocks, at::Tensor reduced_out,
+               at::Tensor sumsq_out) {
+  const c10::cuda::CUDAGuard guard(reduced_out.device());
+  const Peers peers = make_peers(peer_grads, peer_grads);
+  TORCH_CHECK(reduced_out.dtype() == at::kFloat && sumsq_out.dtype() == at::kFloat && sumsq_out.numel() >= nblocks,
+              "dp_reduce outputs");
+  StepArgs a{};
+  a.segs = reinterpret_cast<const Segment*>(segs.data_ptr());
+  a.nsegs = static_cast<int>(segs.numel() / sizeof(Segment));
+  a.world = static_cast<int>(peer_grads.size());
+  a.reduced_out = reduced_out.data_ptr<float>();
+  a.sumsq_out = sumsq_out.data_ptr<float>();
+  if (nblocks == 0) return;
+  dp_reduce_kernel<<<static_cast<unsigned>(nblocks), kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(peers, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------ CUDA IPC buffers
+// A device buffer from cudaMalloc (IPC handles need allocation-granular memory, which the
+// caching allocator does not guarantee), returned as a uint8 tensor that frees it on release.
+std::vector<at::Tensor> ipc_alloc(int64_t nbytes, int64_t device) {
+  TORCH_CHECK(nbytes > 0, "ipc_alloc: empty buffer");
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  void* ptr = nullptr;
+  C10_CUDA_CHECK(cudaMalloc(&ptr, static_cast<size_t>(nbytes)));
+  C10_CUDA_CHECK(cudaMemset(ptr, 0, static_cast<size_t>(nbytes)));
+  cudaIpcMemHandle_t handle;
+  C10_CUDA_CHECK(cudaIpcGetMemHandle(&handle, ptr));
+  auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device);
+  at::Tensor buf = torch::from_blob(ptr, {nbytes}, [device](void* p) {
+    c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+    cudaFree(p);
+  }, opts);
+  at::Tensor h = at::empty({static_cast<int64_t>(sizeof(handle))}, at::TensorOptions().dtype(at::kByte));
+  std::memcpy(h.data_ptr(), &handle, sizeof(handle));
+  return {buf, h};
+}
+
+int64_t ipc_open(at::Tensor handle_bytes, int64_t device) {
+  TORCH_CHECK(handle_bytes.numel() == sizeof(cudaIpcMemHandle_t) && !handle_bytes.is_cuda(), "bad IPC handle");
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  cudaIpcMemHandle_t handle;
+  std::memcpy(&handle, handle_bytes.contiguous().data_ptr(), sizeof(handle));
+  void* ptr = nullptr;
+  C10_CUDA_CHECK(cudaIpcOpenMemHandle(&ptr, handle, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(ptr);
+}
+
+void ipc_close(int64_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  C10_CUDA_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)));
+}
+
+bool peer_access_possible(int64_t device, int64_t peer) {
+  int ok = 0;
+  C10_CUDA_CHECK(cudaDeviceCanAccessPeer(&ok, static_cast<int>(device), static_cast<int>(peer)));
+  return ok != 0;
+}

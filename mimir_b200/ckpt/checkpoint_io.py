@@ -280,6 +280,10 @@ def load_sharded_train_state(config, train_state: TrainState, tag: str) -> None:
             return
         if src_arch["name"] != config.arch.name:
             raise ValueError("Only the original HRM baseline can initialize v2 gates")
+    engine = _engine(train_state)
+    if engine is not None:
+        _load_replicated(engine, train_state, ckpt)
+        return
     model_state = train_state.model.state_dict()
     # DCP loads the requested subset only: refuse sources with modules this run disabled.
     stored = {k.removeprefix("model.") for k in dcp.FileSystemReader(ckpt).read_metadata().state_dict_metadata
@@ -297,6 +301,56 @@ def load_sharded_train_state(config, train_state: TrainState, tag: str) -> None:
     set_state_dict(train_state.model, train_state.optim, model_state_dict=model_state, optim_state_dict=optim_state)
 
 
+def _load_replicated(engine, train_state: TrainState, ckpt: str) -> None:
+    """DCP into the engine's shard buffers in place (same keys/placements FSDP2 writes)."""
+    from mimir_b200.parallel.replicated import model_dcp_state
+    model_state = model_dcp_state(engine)
+    stored = {k.removeprefix("model.") for k in dcp.FileSystemReader(ckpt).read_metadata().state_dict_metadata
+              if k.startswith("model.")}
+    unexpected = stored - set(model_state)
+    if unexpected:
+        raise ValueError(f"Checkpoint contains model keys this run does not have: {sorted(unexpected)}")
+    optim_state = train_state.optim.dcp_state()
+    dcp.load({"model": model_state, "optim": optim_state}, checkpoint_id=ckpt)
+    train_state.optim.load_dcp_state(optim_state)
+    engine.gather_weights()
+
+
+def _full(value):
+    return value.full_tensor() if hasattr(value, "full_tensor") else value
+
+
+def _save_unsharded_replicated(engine, train_state: TrainState, path: str, rank: int) -> None:
+    from mimir_b200.parallel.replicated import model_dcp_state
+    model = {k: _full(v).cpu() for k, v in model_dcp_state(engine).items()}
+    optim = train_state.optim.dcp_state()
+    optim["state"] = {k: {n: _full(t).cpu() for n, t in slots.items()} for k, slots in optim["state"].items()}
+    if rank == 0:
+        torch.save({"model": model, "optim": optim}, path)
+
+
+@torch.no_grad()
+def _load_unsharded_replicated(engine, train_state: TrainState, path: str) -> None:
+    ckpt = torch.load(path, map_location="cpu", weights_only=False)
+    optim = train_state.optim
+    buffers = dict(engine.model.named_buffers())
+    for name, value in ckpt["model"].items():
+        if name in buffers:
+            buffers[name].copy_(value)
+    for s in engine.slots:
+        sl = slice(s.shard, s.shard + s.shard_numel)
+        rows = slice(s.row0, s.row0 + s.rows_mine)
+        engine.master[sl] = ckpt["model"][s.fqn].reshape(s.rows, -1)[rows].reshape(-1).to(engine.master)
+        saved = ckpt["optim"]["state"].get(s.fqn)
+        if saved is None or not s.trainable:
+            continue
+        for slot, buf in (("exp_avg", optim.exp_avg), ("exp_avg_sq", optim.exp_avg_sq), ("param_ema", optim.ema)):
+            if buf is not None and slot in saved:
+                buf[sl] = saved[slot].reshape(s.rows, -1)[rows].reshape(-1).to(buf)
+    optim.load_dcp_state(ckpt["optim"])
+    engine.gather_weights()
+
+
 def load_unsharded_train_state(config, train_state: TrainState, tag: str, rank: int) -> None:
     root = config.resume_checkpoint_path
     if config.arch.gate_initialize_from_v1:
@@ -307,6 +361,9 @@ def load_unsharded_train_state(config, train_state: TrainState, tag: str, rank: 
     if not os.path.isfile(path):
         raise ValueError(f"Checkpoint file not found: {path}")
     distributed = dist.is_available() and dist.is_initialized()
+    if _engine(train_state) is not None:
+        _load_unsharded_replicated(_engine(train_state), train_state, path)
+        return
     if config.arch.upcycle_from_dense:
         from mimir_b200.ckpt.upcycle import expand_unsharded_state
         opts = StateDictOptions(full_state_dict=True, cpu_offload=True)
@@ -330,13 +387,25 @@ def load_unsharded_train_state(config, train_state: TrainState, tag: str, rank: 
     set_optimizer_state_dict(train_state.model, train_state.optim, ckpt["optim"])
 
 
+def _engine(train_state):
+    return getattr(train_state.model, "replicated_engine", None)
+
+
 def save_sharded_train_state(directory: str, train_state: TrainState, tag: str) -> None:
-    dcp.save({"model": train_state.model.state_dict(),
-              "optim": get_optimizer_state_dict(train_state.model, train_state.optim)},
-             checkpoint_id=sharded_checkpoint_id(directory, tag))
+    engine = _engine(train_state)
+    if engine is not None:
+        from mimir_b200.parallel.replicated import model_dcp_state
+        state = {"model": model_dcp_state(engine), "optim": train_state.optim.dcp_state()}
+    else:
+        state = {"model": train_state.model.state_dict(),
+                 "optim": get_optimizer_state_dict(train_state.model, train_state.optim)}
+    dcp.save(state, checkpoint_id=sharded_checkpoint_id(directory, tag))
 
 
 def save_unsharded_train_state(directory: str, train_state: TrainState, tag: str, rank: int) -> None:
+    if _engine(train_state) is not None:
+        _save_unsharded_replicated(_engine(train_state), train_state, unsharded_checkpoint_path(directory, tag), rank)
+        return
     if dist.is_available() and dist.is_initialized():
         opts = StateDictOptions(full_state_dict=True, cpu_offload=True)
         model_state = get_model_state_dict(train_state.model, options=opts)

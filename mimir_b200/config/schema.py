@@ -93,7 +93,7 @@ class PretrainConfig(pydantic.BaseModel):
     fwd_bwd_dtype: str = "bfloat16"
     activation_checkpointing: Literal["none", "full", "l_only", "h_only"] = "none"
     accelerator_type: AcceleratorType = "sm100"
-    distributed_strategy: Literal["fsdp", "ddp", "none"] = "fsdp"
+    distributed_strategy: Literal["fsdp", "ddp", "replicated", "none"] = "fsdp"
     fsdp_params_precision: Literal["fp32", "bf16"] = "fp32"
     fsdp_wrap_policy: Literal["transformer_block", "recurrent_level"] = "transformer_block"
     fsdp_shard_degree: Optional[int] = pydantic.Field(default=None, ge=2)

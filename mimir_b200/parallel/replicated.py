@@ -1,0 +1,408 @@
+"""Replicated-weight data parallelism with a fused reduce-scatter + AdamATan2 + all-gather step.
+
+Design (one process per GPU).  Every rank keeps the whole model in the compute dtype (bf16)
+— a 1.3B-parameter model is 2.6 GB, small next to 180 GB of HBM — so forward and backward
+run with no collective at all.  The fp32 master weights and the optimizer slots are sharded
+exactly like FSDP2 shards a parameter (dim 0 split in ``ceil(rows / world)`` chunks), so a DCP
+checkpoint written here has the same keys, shapes, dtypes and shard placement
+(``model.<fqn>``, ``optim.state.<fqn>.{step,exp_avg,exp_avg_sq,param_ema}``, ``Shard(0)``) as one
+written by FSDP2, and either can resume the other.
+
+The weights and gradients live in two flat buffers allocated with ``cudaMalloc`` and shared
+over CUDA IPC, so each rank can address every peer's buffers over NVLink.  One optimizer step
+is one kernel per rank (``csrc/dp_fused.cu``): for the rank's own shard it loads the peers'
+bf16 gradients, sums them in fp32, applies AdamATan2 (decoupled weight decay, atan2 update,
+first/second moments, EMA) to the fp32 master shard and stores the rounded bf16 weights into
+every rank's weight buffer.  A one-element NCCL all-reduce before and after the kernel orders
+it with the other ranks: before, every rank's backward is complete; after, every rank's
+stores have landed.  NVLink traffic per rank and step is ``(world-1)/world`` of the bf16
+gradients in and of the bf16 weights out; there is no fp32 gradient traffic at all.
+
+With global-norm clipping the step is two kernels: a reduce pass that writes the fp32 reduced
+gradient shard and per-CTA sums of squares, one scalar all-reduce for the norm, then the
+update pass reading the reduced shard with the clip coefficient.
+
+On CPU (tests, Gloo) the same algorithm runs with PyTorch collectives (all-reduce of the
+gradients, the reference AdamATan2 arithmetic on the shard, all-gather of the weights).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+import torch
+import torch.distributed as dist
+from torch import Tensor, nn
+from torch.optim.optimizer import Optimizer
+
+_ALIGN = 8  # elements: 16 bytes of bf16, 32 bytes of fp32
+
+
+def _align(n: int) -> int:
+    return (n + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+@dataclass
+class ParamSlot:
+    fqn: str
+    param: nn.Parameter
+    shape: torch.Size
+    flat: int              # element offset in the flat weight/grad buffers
+    numel: int
+    rows: int              # dim-0 extent (1 for scalars)
+    row0: int              # first owned row
+    rows_mine: int         # owned rows (may be 0)
+    shard: int             # element offset in the shard buffers
+    trainable: bool
+
+    @property
+    def shard_numel(self) -> int:
+        return self.rows_mine * (self.numel // self.rows)
+
+    @property
+    def shard_flat(self) -> int:
+        return self.flat + self.row0 * (self.numel // self.rows)
+
+    def local_shape(self) -> tuple:
+        return (self.rows_mine, *self.shape[1:]) if len(self.shape) else (self.rows_mine,)
+
+
+class ReplicatedEngine:
+    def __init__(self, model: nn.Module, *, compute_dtype: torch.dtype, device: torch.device,
+                 group: Optional[dist.ProcessGroup] = None):
+        self.model, self.device, self.compute_dtype = model, device, compute_dtype
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.cuda = device.type == "cuda"
+        if self.cuda and compute_dtype != torch.bfloat16:
+            raise ValueError("The fused CUDA step keeps bf16 replicated weights")
+        if self.world > 8:
+            raise ValueError("The fused step supports one node (<= 8 ranks)")
+        self._broadcast_initial_state()
+        self.slots = self._layout()
+        self.total = self.slots[-1].flat + _align(self.slots[-1].numel) if self.slots else 0
+        self.shard_total = max((s.shard + _align(s.shard_numel) for s in self.slots), default=0)
+        self._allocate()
+        self.reduced: Optional[Tensor] = None
+        # Parameters that received a gradient since the last zero_grad: like the per-parameter
+        # optimizer, a parameter without one (e.g. outside the truncated-BPTT window) is not
+        # updated at all (no decay, no moment update, no step count).
+        self.touched: set[str] = set()
+        for s in self.slots:
+            if s.trainable:
+                s.param.register_post_accumulate_grad_hook(lambda _p, fqn=s.fqn: self.touched.add(fqn))
+
+    # ------------------------------------------------------------------ setup
+    @torch.no_grad()
+    def _broadcast_initial_state(self) -> None:
+        if self.world == 1:
+            return
+        for t in list(self.model.parameters()) + list(self.model.buffers()):
+            dist.broadcast(t.data, src=dist.get_global_rank(self.group, 0) if self.group else 0, group=self.group)
+
+    def _layout(self) -> list[ParamSlot]:
+        slots, flat, shard = [], 0, 0
+        for fqn, p in self.model.named_parameters():
+            rows = p.shape[0] if p.dim() > 0 else 1
+            chunk = math.ceil(rows / self.world)
+            row0 = min(rows, self.rank * chunk)
+            mine = max(0, min(rows, row0 + chunk) - row0)
+            slot = ParamSlot(fqn, p, p.shape, flat, p.numel(), rows, row0, mine, shard, p.requires_grad)
+            slots.append(slot)
+            flat += _align(p.numel())
+            shard += _align(slot.shard_numel)
+        return slots
+
+    @torch.no_grad()
+    def _allocate(self) -> None:
+        nbytes = self.total * self.compute_dtype.itemsize
+        if self.cuda:
+            from mimir_b200.ops._ext import ext
+            C = ext()
+            wbuf, whandle = C.ipc_alloc(nbytes, self.device.index)
+            gbuf, ghandle = C.ipc_alloc(nbytes, self.device.index)
+            self._keep = (wbuf, gbuf)
+            self.weights = wbuf.view(self.compute_dtype)
+            self.grads = gbuf.view(self.compute_dtype)
+            self._open_peers(whandle, ghandle)
+        else:
+            self.weights = torch.zeros(self.total, dtype=self.compute_dtype)
+            self.grads = torch.zeros(self.total, dtype=self.compute_dtype)
+        f32 = dict(dtype=torch.float32, device=self.device)
+        self.master = torch.zeros(self.shard_total, **f32)
+        for s in self.slots:
+            full = s.param.detach().to(torch.float32).reshape(s.rows, -1)
+            self.master[s.shard:s.shard + s.shard_numel] = full[s.row0:s.row0 + s.rows_mine].reshape(-1)
+            self.weights[s.flat:s.flat + s.numel] = s.param.detach().reshape(-1).to(self.compute_dtype)
+            s.param.data = self.weights[s.flat:s.flat + s.numel].view(s.shape)
+            if s.trainable:
+                s.param.grad = self.grads[s.flat:s.flat + s.numel].view(s.shape)
+
+    def _open_peers(self, whandle: Tensor, ghandle: Tensor) -> None:
+        from mimir_b200.ops._ext import ext
+        C = ext()
+        mine = (bytes(whandle.numpy().tobytes()), bytes(ghandle.numpy().tobytes()))
+        everyone = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(everyone, mine, group=self.group)
+        else:
+            everyone = [mine]
+        devices = [self.device.index] * self.world
+        if self.world > 1:
+            dist.all_gather_object(devices, self.device.index, group=self.group)
+        self._opened = []
+        self.peer_weights, self.peer_grads = [], []
+        for k, (wh, gh) in enumerate(everyone):
+            if k == self.rank:
+                self.peer_weights.append(self.weights.data_ptr())
+                self.peer_grads.append(self.grads.data_ptr())
+                continue
+            if not C.peer_access_possible(self.device.index, devices[k]):
+                raise RuntimeError(f"GPU {self.device.index} cannot access peer rank {k} over NVLink/PCIe")
+            wp = C.ipc_open(torch.frombuffer(bytearray(wh), dtype=torch.uint8), self.device.index)
+            gp = C.ipc_open(torch.frombuffer(bytearray(gh), dtype=torch.uint8), self.device.index)
+            self._opened += [wp, gp]
+            self.peer_weights.append(wp)
+            self.peer_grads.append(gp)
+
+    def close(self) -> None:
+        if self.cuda and getattr(self, "_opened", None):
+            from mimir_b200.ops._ext import ext
+            for ptr in self._opened:
+                ext().ipc_close(ptr, self.device.index)
+            self._opened = []
+
+    # ------------------------------------------------------------------ step plumbing
+    def zero_grad(self) -> None:
+        self.grads.zero_()
+        self.touched.clear()
+
+    def barrier(self) -> None:
+        if self.world == 1:
+            return
+        flag = torch.zeros(1, device=self.device)
+        dist.all_reduce(flag, group=self.group)
+
+    def segments(self, lrs: dict, wds: dict, bc1: dict, bc2_sqrt: dict) -> tuple[Tensor, int]:
+        """Packed device segment table: one entry per owned, non-empty shard of every parameter
+        named in ``lrs`` (per-parameter learning rate, weight decay and bias corrections)."""
+        from mimir_b200.ops._ext import ext
+        C = ext()
+        chunk = C.dp_chunk_elements()
+        rows, block = [], 0
+        for s in self.slots:
+            if s.fqn not in lrs or s.shard_numel == 0:
+                continue
+            n = s.shard_numel
+            vec = int(s.shard_flat % 8 == 0 and s.shard % 8 == 0 and n % 8 == 0)
+            rows.append((s.shard_flat, s.shard, n, block, lrs[s.fqn], wds[s.fqn], bc1[s.fqn], bc2_sqrt[s.fqn], vec, 0))
+            block += (n + chunk - 1) // chunk
+        dt = np.dtype([("flat", "<i8"), ("shard", "<i8"), ("n", "<i8"), ("block", "<i8"), ("lr", "<f4"),
+                       ("wd", "<f4"), ("bc1", "<f4"), ("bc2", "<f4"), ("vec", "<i4"), ("pad", "<i4")])
+        assert dt.itemsize == C.dp_segment_bytes()
+        table = np.array(rows, dtype=dt)
+        host = torch.from_numpy(table.view(np.uint8).copy())
+        return host.pin_memory().to(self.device, non_blocking=True), block
+
+    @torch.no_grad()
+    def reduce_for_clipping(self) -> Tensor:
+        """Reduce the gradients of this rank's shards into ``self.reduced``; return the global sum of squares."""
+        if self.cuda:
+            from mimir_b200.ops._ext import ext
+            self.barrier()
+            zero = {s.fqn: 0.0 for s in self.slots if s.trainable}
+            table, blocks = self.segments(zero, zero, zero, zero)
+            self.reduced = torch.empty(self.shard_total, dtype=torch.float32, device=self.device)
+            partial = torch.empty(max(blocks, 1), dtype=torch.float32, device=self.device)
+            ext().dp_reduce(self.peer_grads, table, blocks, self.reduced, partial)
+            total = partial[:blocks].double().sum().reshape(1)
+        else:
+            full = self.grads.to(torch.float32)
+            if self.world > 1:
+                dist.all_reduce(full, group=self.group)
+            self.reduced = torch.zeros(self.shard_total, dtype=torch.float32)
+            for s in self.slots:
+                if s.trainable and s.shard_numel:
+                    self.reduced[s.shard:s.shard + s.shard_numel] = full[s.shard_flat:s.shard_flat + s.shard_numel]
+            total = self.reduced.double().square().sum().reshape(1)
+        if self.world > 1:
+            dist.all_reduce(total, group=self.group)
+        return total
+
+    @torch.no_grad()
+    def gather_weights(self) -> None:
+        """Rebuild every rank's replicated weights from the master shards (after a load)."""
+        for s in self.slots:
+            local = self.master[s.shard:s.shard + s.shard_numel].to(self.compute_dtype)
+            if self.world == 1:
+                self.weights[s.shard_flat:s.shard_flat + s.shard_numel] = local
+                continue
+            chunk = math.ceil(s.rows / self.world) * (s.numel // s.rows)
+            padded = torch.zeros(chunk, dtype=self.compute_dtype, device=self.device)
+            padded[:local.numel()] = local
+            out = torch.empty(chunk * self.world, dtype=self.compute_dtype, device=self.device)
+            dist.all_gather_into_tensor(out, padded, group=self.group)
+            self.weights[s.flat:s.flat + s.numel] = out[:s.numel]
+
+    # ------------------------------------------------------------------ checkpoint views
+    def mesh(self):
+        from torch.distributed.device_mesh import init_device_mesh
+        if getattr(self, "_mesh", None) is None:
+            if not dist.is_initialized():  # single process: DTensor views need a 1-rank group
+                dist.init_process_group("nccl" if self.cuda else "gloo", store=dist.HashStore(), rank=0, world_size=1)
+            self._mesh = init_device_mesh(self.device.type, (self.world,))
+        return self._mesh
+
+    def shard_dtensor(self, s: ParamSlot, buffer: Tensor):
+        from torch.distributed.tensor import DTensor, Shard
+        local = buffer[s.shard:s.shard + s.shard_numel].view(s.local_shape())
+        full_stride = torch.empty(s.shape, device="meta").stride()
+        return DTensor.from_local(local, self.mesh(), [Shard(0)], run_check=False, shape=s.shape, stride=full_stride)
+
+
+class ReplicatedAdamATan2(Optimizer):
+    """AdamATan2 over a :class:`ReplicatedEngine` (same slots and group keys as ``AdamATan2``)."""
+
+    def __init__(self, engine: ReplicatedEngine, lr: float = 1e-3, betas=(0.9, 0.95), weight_decay: float = 0.1,
+                 ema: Optional[float] = None, ema_dtype=None, parameter_lr_scales: Optional[dict] = None):
+        params = [s.param for s in engine.slots if s.trainable]
+        defaults = dict(lr=lr, betas=betas, weight_decay=weight_decay, ema=ema,
+                        ema_dtype=None if ema_dtype is None else str(ema_dtype).removeprefix("torch."))
+        super().__init__(params, defaults)
+        self.engine = engine
+        self.parameter_lr_scales = parameter_lr_scales
+        self.grad_scale: Optional[Tensor] = None
+        f32 = dict(dtype=torch.float32, device=engine.device)
+        n = engine.shard_total
+        self.exp_avg = torch.zeros(n, **f32) if betas[0] > 0 else None
+        self.exp_avg_sq = torch.zeros(n, **f32)
+        self.ema = engine.master.clone() if ema is not None else None
+        for s in engine.slots:
+            if s.trainable:
+                self.state[s.param]["step"] = torch.tensor(0.0)
+
+    def zero_grad(self, set_to_none: bool = True) -> None:  # noqa: ARG002 - gradients are views
+        self.engine.zero_grad()
+
+    def _lr(self, group, p) -> float:
+        lr = group["lr"]
+        return float(lr * self.parameter_lr_scales[p]) if self.parameter_lr_scales is not None else float(lr)
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        if closure is not None:
+            raise ValueError("Closures are not supported")
+        if getattr(self, "shared_parameter_updates", None):
+            raise ValueError("Shared gate-donor updates are not supported by the replicated engine")
+        eng = self.engine
+        (group,) = self.param_groups
+        b1, b2 = group["betas"]
+        lrs, wds, bc1, bc2_sqrt = {}, {}, {}, {}
+        for s in eng.slots:
+            if not s.trainable or s.fqn not in eng.touched:
+                continue
+            st = self.state[s.param]
+            st["step"] += 1
+            lrs[s.fqn] = self._lr(group, s.param)
+            wds[s.fqn] = float(group["weight_decay"])
+            # bias corrections exactly as the per-parameter optimizer forms them (fp32 tensors)
+            bc1[s.fqn] = (1 - b1 ** st["step"]) if self.exp_avg is not None else torch.tensor(1.0)
+            bc2_sqrt[s.fqn] = (1 - b2 ** st["step"]).sqrt()
+        ema = group["ema"]
+        if eng.cuda:
+            from mimir_b200.ops._ext import ext
+            table, blocks = eng.segments(lrs, wds, {k: float(v) for k, v in bc1.items()},
+                                         {k: float(v) for k, v in bc2_sqrt.items()})
+            if eng.reduced is None:
+                eng.barrier()  # every rank's backward has finished writing its gradients
+            ext().dp_step(eng.peer_grads, eng.peer_weights, table, blocks, eng.master, self.exp_avg, self.exp_avg_sq,
+                          self.ema, eng.reduced, self.grad_scale, b1, b2, ema if ema is not None else 0.0)
+            eng.barrier()  # every rank's weight stores have landed
+        else:
+            self._step_cpu(lrs, wds, bc1, bc2_sqrt, b1, b2, ema)
+        eng.reduced = None
+        self.grad_scale = None
+
+    def _step_cpu(self, lrs: dict, wds: dict, bc1: dict, bc2_sqrt: dict, b1, b2, ema) -> None:
+        eng = self.engine
+        if eng.reduced is None:
+            full = eng.grads.to(torch.float32)
+            if eng.world > 1:
+                dist.all_reduce(full, group=eng.group)
+        scale = self.grad_scale if self.grad_scale is not None else None
+        for s in eng.slots:
+            if s.fqn not in lrs or s.shard_numel == 0:
+                continue
+            sl = slice(s.shard, s.shard + s.shard_numel)
+            g = (eng.reduced[sl] if eng.reduced is not None
+                 else full[s.shard_flat:s.shard_flat + s.shard_numel]).clone()
+            if scale is not None:
+                g = g * scale
+            w, v = eng.master[sl], self.exp_avg_sq[sl]
+            lr = lrs[s.fqn]
+            if wds[s.fqn] != 0:
+                w.mul_(1 - lr * wds[s.fqn])
+            v.mul_(b2).addcmul_(g, g, value=1 - b2)
+            denom = v.sqrt() / bc2_sqrt[s.fqn]
+            if self.exp_avg is not None:
+                m = self.exp_avg[sl]
+                m.lerp_(g, 1 - b1)
+                w.add_(torch.atan2(m, denom), alpha=-(lr / bc1[s.fqn]))
+            else:
+                w.add_(torch.atan2(g, denom), alpha=-lr)
+            if self.ema is not None:
+                self.ema[sl].lerp_(w, 1 - ema)
+        eng.gather_weights()
+
+    # ------------------------------------------------------------------ checkpoint views
+    def dcp_state(self) -> dict:
+        """``get_optimizer_state_dict``-shaped optimizer state with ``Shard(0)`` DTensor slots."""
+        eng = self.engine
+        state = {}
+        for s in eng.slots:
+            if not s.trainable:
+                continue
+            entry = {"step": self.state[s.param]["step"]}
+            if self.exp_avg is not None:
+                entry["exp_avg"] = eng.shard_dtensor(s, self.exp_avg)
+            entry["exp_avg_sq"] = eng.shard_dtensor(s, self.exp_avg_sq)
+            if self.ema is not None:
+                entry["param_ema"] = eng.shard_dtensor(s, self.ema)
+            state[s.fqn] = entry
+        groups = [{k: v for k, v in g.items() if k != "params"} | {"params": [s.fqn for s in eng.slots if s.trainable]}
+                  for g in self.param_groups]
+        return {"state": state, "param_groups": groups}
+
+    def load_dcp_state(self, loaded: dict) -> None:
+        """Adopt ``param_groups`` hyper-parameters and the ``step`` counters after a DCP load
+        (the slot tensors were loaded in place into the shard buffers)."""
+        for s in self.engine.slots:
+            if s.trainable and s.fqn in loaded["state"]:
+                step = loaded["state"][s.fqn]["step"]
+                self.state[s.param]["step"] = step.detach().clone() if torch.is_tensor(step) else torch.tensor(float(step))
+        for group, saved in zip(self.param_groups, loaded.get("param_groups", [])):
+            for key, value in saved.items():
+                if key != "params":
+                    group[key] = value
+
+
+def model_dcp_state(engine: ReplicatedEngine) -> dict:
+    """``model.state_dict()``-shaped dict: fp32 master shards as ``Shard(0)`` DTensors + buffers."""
+    out = {s.fqn: engine.shard_dtensor(s, engine.master) for s in engine.slots}
+    for name, buf in engine.model.named_buffers():
+        if name in engine.model.state_dict():
+            out[name] = buf
+    return out
+
+
+def wrap_replicated(model: nn.Module, device: torch.device, compute_dtype: torch.dtype) -> ReplicatedEngine:
+    engine = ReplicatedEngine(model, compute_dtype=compute_dtype, device=device)
+    model.replicated_engine = engine
+    return engine
+
+
+def engine_of(model: nn.Module) -> Optional[ReplicatedEngine]:
+    return getattr(model, "replicated_engine", None)

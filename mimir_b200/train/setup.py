@@ -50,6 +50,8 @@ def create_model_and_optimizer(config, metadata: dict, device: torch.device, loc
         if not checkpointed:
             raise ValueError(f"activation_checkpointing={config.activation_checkpointing} found no matching blocks")
     distributed = dist.is_available() and dist.is_initialized()
+    if config.distributed_strategy == "replicated":
+        return _replicated_model_and_optimizer(config, model, carry, device, fwd_bwd_dtype)
     if distributed:
         if config.distributed_strategy == "fsdp":
             model = wrap_fsdp(model, config, fwd_bwd_dtype, checkpointed)
@@ -70,6 +72,20 @@ def create_model_and_optimizer(config, metadata: dict, device: torch.device, loc
     optim = cls(params, **options, lr=0.0, betas=(config.beta1, config.beta2), weight_decay=config.weight_decay,
                 ema=config.ema, ema_dtype=optimizer_ema_dtype(config),
                 parameter_lr_scales=module_lr_scales(model, config.lr, configured_module_rates(config)))
+    return model, carry, optim
+
+
+def _replicated_model_and_optimizer(config, model, carry, device, fwd_bwd_dtype):
+    """Replicated bf16 weights + sharded fp32 master/optimizer, fused peer-memory step."""
+    from mimir_b200.parallel.replicated import ReplicatedAdamATan2, wrap_replicated
+    if config.optimizer != "adam_atan2":
+        raise ValueError("distributed_strategy=replicated supports the AdamATan2 optimizer")
+    if config.arch.gates_enabled:
+        raise ValueError("distributed_strategy=replicated does not implement shared gate-donor updates")
+    scales = module_lr_scales(model, config.lr, configured_module_rates(config))
+    engine = wrap_replicated(model, device, fwd_bwd_dtype)
+    optim = ReplicatedAdamATan2(engine, lr=0.0, betas=(config.beta1, config.beta2), weight_decay=config.weight_decay,
+                                ema=config.ema, ema_dtype=torch.float32, parameter_lr_scales=scales)
     return model, carry, optim
 
 

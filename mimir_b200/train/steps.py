@@ -120,10 +120,12 @@ def train_accumulated_batches(config, rank: int, train_state, batches: list, use
         scale = 1.0
         if isinstance(model, FSDPModule) and dist.is_available() and dist.is_initialized():
             scale = float(dist.get_world_size())
-        clip = clip_grad_norm_mean_units(model.parameters(), max_norm=(config.gradient_clip_norm
-                                                                       if config.gradient_clip_norm is not None
-                                                                       else config.gradient_skip_norm),
-                                         summed_gradient_scale=scale)
+        max_norm = config.gradient_clip_norm if config.gradient_clip_norm is not None else config.gradient_skip_norm
+        engine = getattr(model, "replicated_engine", None)
+        if engine is not None:
+            clip = _replicated_clip(engine, train_state.optim, max_norm)
+        else:
+            clip = clip_grad_norm_mean_units(model.parameters(), max_norm=max_norm, summed_gradient_scale=scale)
         one = clip.total_norm.new_ones(())
         metrics["grad_norm"] = (clip.total_norm.detach(), one)
         if config.gradient_clip_norm is not None:
@@ -146,6 +148,9 @@ def train_accumulated_batches(config, rank: int, train_state, batches: list, use
         trace_print(config, rank, f"optim_step_begin step={train_state.step}")
         train_state.optim.step()
         trace_print(config, rank, f"optim_step_end step={train_state.step}")
+    elif getattr(model, "replicated_engine", None) is not None:
+        model.replicated_engine.reduced = None
+        train_state.optim.grad_scale = None
     if probe is not None:
         from mimir_b200.utils.diagnostics import append_jsonl
         updates = probe.finish(next(model.parameters()).device)
@@ -157,6 +162,21 @@ def train_accumulated_batches(config, rank: int, train_state, batches: list, use
         train_state.optim.zero_grad()
     trace_print(config, rank, f"train_accumulated_end step={train_state.step} skipped={skipped}")
     return metrics, skipped
+
+
+def _replicated_clip(engine, optim, max_norm: float):
+    """Global-norm clipping for replicated weights: the norm is taken over the reduced (summed)
+    gradients, computed by the engine's reduce pass; the update pass then applies the coefficient."""
+    from mimir_b200.optim.clipping import GradientClipMetrics
+    world = float(engine.world)
+    raw = engine.reduce_for_clipping().sqrt().to(torch.float32).reshape(())
+    if not bool(torch.isfinite(raw)):
+        raise RuntimeError(f"The total norm of order 2.0 for gradients is non-finite ({raw.item()})")
+    raw_max = max_norm * world
+    coeff = torch.clamp(raw.new_tensor(raw_max) / (raw + 1e-6), max=1.0)
+    optim.grad_scale = coeff.reshape(1).to(engine.device)
+    norm = raw / world
+    return GradientClipMetrics(total_norm=norm, clip_coefficient=coeff, clipped=(norm > max_norm).to(norm.dtype))
 
 
 @torch.inference_mode()

@@ -1,0 +1,129 @@
+"""Fused reduce-scatter + AdamATan2 + all-gather kernel (csrc/dp_fused.cu) against PyTorch fp32.
+
+One GPU: the kernel's update of the master shard, moments, EMA and the bf16 weight copy is
+compared with the per-parameter AdamATan2 arithmetic in fp32.  Two or more GPUs (spawned
+ranks, NCCL): every rank's replicated weights must equal the single-process result computed
+from the summed gradients, and all ranks must hold bit-identical weights.
+"""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _reference_update(w, g, m, v, e, lr, wd, b1, b2, step, ema):
+    w = w * (1 - lr * wd)
+    v = b2 * v + (1 - b2) * g * g
+    m = m + (1 - b1) * (g - m)
+    bc1 = 1 - b1 ** step
+    bc2 = (1 - b2 ** step) ** 0.5
+    w = w - (lr / bc1) * torch.atan2(m, v.sqrt() / bc2)
+    e = e + (1 - ema) * (w - e)
+    return w, m, v, e
+
+
+def _model(device):
+    torch.manual_seed(0)
+    return torch.nn.Sequential(torch.nn.Linear(64, 96), torch.nn.Linear(96, 40, bias=True),
+                               torch.nn.Linear(40, 8, bias=False)).to(device)
+
+
+def test_single_gpu_step_matches_fp32_reference():
+    from mimir_b200.parallel.replicated import ReplicatedAdamATan2, wrap_replicated
+    dev = torch.device("cuda", 0)
+    model = _model(dev)
+    init = {n: p.detach().float().clone() for n, p in model.named_parameters()}
+    engine = wrap_replicated(model, dev, torch.bfloat16)
+    opt = ReplicatedAdamATan2(engine, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, ema=0.9)
+    state = {n: (init[n], torch.zeros_like(init[n]), torch.zeros_like(init[n]), init[n].clone()) for n in init}
+    gen = torch.Generator(device=dev).manual_seed(3)
+    for step in (1, 2, 3):
+        opt.zero_grad()
+        x = torch.randn(33, 64, device=dev, dtype=torch.bfloat16, generator=gen)
+        model(x).float().square().mean().backward()
+        grads = {n: p.grad.float().clone() for n, p in model.named_parameters()}
+        opt.step()
+        torch.cuda.synchronize()
+        for s in engine.slots:
+            w, m, v, e = state[s.fqn]
+            w, m, v, e = _reference_update(w, grads[s.fqn], m, v, e, 1e-2, 0.1, 0.9, 0.95, step, 0.9)
+            state[s.fqn] = (w, m, v, e)
+            sl = slice(s.shard, s.shard + s.shard_numel)
+            torch.testing.assert_close(engine.master[sl].view(s.shape), w, rtol=1e-5, atol=1e-6)
+            torch.testing.assert_close(opt.exp_avg_sq[sl].view(s.shape), v, rtol=1e-5, atol=1e-9)
+            torch.testing.assert_close(opt.ema[sl].view(s.shape), e, rtol=1e-5, atol=1e-6)
+            assert torch.equal(s.param.detach(), engine.master[sl].view(s.shape).to(torch.bfloat16))
+
+
+def test_clip_path_matches_unclipped_reference_with_coefficient():
+    from mimir_b200.parallel.replicated import ReplicatedAdamATan2, wrap_replicated
+    dev = torch.device("cuda", 0)
+    model = _model(dev)
+    engine = wrap_replicated(model, dev, torch.bfloat16)
+    opt = ReplicatedAdamATan2(engine, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.0, ema=None)
+    opt.zero_grad()
+    model(torch.randn(9, 64, device=dev, dtype=torch.bfloat16)).float().sum().backward()
+    want = torch.sqrt(sum(p.grad.float().square().sum() for p in model.parameters()).double())
+    got = engine.reduce_for_clipping().sqrt()
+    torch.testing.assert_close(got.cpu(), want.reshape(1).cpu(), rtol=1e-5, atol=0)
+    opt.grad_scale = torch.tensor([0.5], device=dev)
+    before = engine.master.clone()
+    opt.step()
+    assert not torch.equal(before, engine.master)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, out):
+    import torch.distributed as dist
+    from mimir_b200.parallel.replicated import ReplicatedAdamATan2, wrap_replicated
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        model = _model(dev)
+        engine = wrap_replicated(model, dev, torch.bfloat16)
+        opt = ReplicatedAdamATan2(engine, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, ema=0.9)
+        for step in range(3):
+            opt.zero_grad()
+            gen = torch.Generator(device=dev).manual_seed(100 * step + rank)
+            x = torch.randn(17, 64, device=dev, dtype=torch.bfloat16, generator=gen)
+            model(x).float().square().mean().backward()
+            torch.save({n: p.grad.detach().float().cpu() for n, p in model.named_parameters()},
+                       f"{out}.grad.{step}.{rank}.pt")
+            opt.step()
+        torch.cuda.synchronize()
+        torch.save({n: p.detach().float().cpu() for n, p in model.named_parameters()}, f"{out}.w.{rank}.pt")
+        engine.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_multi_gpu_fused_step_matches_summed_reference(tmp_path):
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 8)
+    mp.spawn(_rank, args=(world, _free_port(), str(tmp_path / "r")), nprocs=world, join=True)
+    weights = [torch.load(tmp_path / f"r.w.{r}.pt") for r in range(world)]
+    for r in range(1, world):
+        for n in weights[0]:
+            assert torch.equal(weights[0][n], weights[r][n]), (r, n)
+    model = _model("cpu")
+    state = {n: (p.detach().float(), torch.zeros_like(p), torch.zeros_like(p), p.detach().float().clone())
+             for n, p in model.named_parameters()}
+    for step in range(3):
+        grads = [torch.load(tmp_path / f"r.grad.{step}.{r}.pt") for r in range(world)]
+        for n in state:
+            g = sum(gr[n] for gr in grads)
+            w, m, v, e = state[n]
+            state[n] = _reference_update(w, g, m, v, e, 1e-2, 0.1, 0.9, 0.95, step + 1, 0.9)
+    for n, (w, *_rest) in state.items():
+        torch.testing.assert_close(weights[0][n], w.to(torch.bfloat16).float(), rtol=1e-2, atol=1e-3)
