@@ -10,8 +10,9 @@ and sparse mixture ``:69-104``, upcycling ``:107-165``) and
   aux-loss-free balancing is on (the per-expert ``selection_bias`` only steers selection).
 * For top-1 with several experts a straight-through surrogate gives the router a gradient.
 * The sparse path runs each expert only on its tokens and still calls every expert (even
-  with zero tokens) so all ranks issue identical collectives.  On CUDA the token
-  permutation is done by the fused kernels in :mod:`mimir_b200.ops.moe`.
+  with zero tokens) so all ranks issue identical collectives.  The token lists of all experts
+  come from one stable (expert, token) ordering (:mod:`mimir_b200.ops.moe`) with a single
+  host transfer of the per-expert counts.
 """
 from __future__ import annotations
 
