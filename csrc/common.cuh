@@ -275,4 +275,20 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x on the FMA/integer pipes, for softmax probabilities that are rounded to bf16 anyway
+// (max relative error 7.6e-5; inputs below -125, including -inf, give exactly 0).
+// Range reduction: adding 1.5*2^23 rounds x to the nearest integer n held in the low mantissa
+// bits of t, leaving f = x - n in [-0.5, 0.5]; 2^f is a degree-3 polynomial fitted (minimax in
+// relative error, Lawson reweighting) for this file; n is added to the exponent field.
+__device__ __forceinline__ float poly_exp2(float x) {
+  const float xc = fmaxf(x, -125.f);
+  const float t = xc + 12582912.f;
+  const float f = xc - (t - 12582912.f);
+  float q = fmaf(0.05517098f, f, 0.2426097f);
+  q = fmaf(q, f, 0.69326097f);
+  q = fmaf(q, f, 0.99992816f);
+  const float y = __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+  return x < -125.f ? 0.f : y;
+}
+
 }  // namespace mimir

@@ -9,7 +9,7 @@
 // The owned ranges of all parameters are the rank's "segments"; its fp32 master weights and
 // moments are stored back to back in segment order.
 //
-// Kernel (one CTA per 8192-element chunk of a segment):
+// Kernel (persistent CTAs walking 8192-element chunks of the segments):
 //   g   = sum_k grad_k[flat + i]   (peer loads, fixed rank order, fp32)
 //   g  *= grad_scale               (global clipping coefficient or 1)
 //   w   = w * (1 - lr*wd);  v = b2 v + (1-b2) g^2;  m += (1-b1)(g - m)
@@ -61,7 +61,7 @@ struct StepArgs {
   float* ema;            // nullptr without EMA
   const float* reduced;  // update variant: read gradients from here instead of the peers
   float* reduced_out;    // reduce variant: write the reduced gradient shard here
-  float* sumsq_out;      // reduce variant: one partial sum of squares per CTA
+  float* sumsq_out;      // reduce variant: one partial sum of squares per chunk
   const float* grad_scale;  // device scalar (clip coefficient) or nullptr for 1
   float b1, b2, ema_decay;
 };
@@ -101,25 +101,6 @@ __device__ __forceinline__ void st8(float* p, const float (&f)[8]) {
   *reinterpret_cast<float4*>(p + 4) = make_float4(f[4], f[5], f[6], f[7]);
 }
 
-// Gradient of 8 consecutive elements summed over the ranks (fixed order 0..world-1).
-__device__ __forceinline__ void reduce8(const Peers& peers, int world, int64_t flat, float (&g)[8]) {
-  uint4 raw[kMaxRanks];
-#pragma unroll
-  for (int k = 0; k < kMaxRanks; ++k)
-    if (k < world) raw[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peers.grad[k]) + flat);
-#pragma unroll
-  for (int e = 0; e < 8; ++e) g[e] = 0.f;
-#pragma unroll
-  for (int k = 0; k < kMaxRanks; ++k) {
-    if (k < world) {
-      float f[8];
-      unpack8(raw[k], f);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) g[e] += f[e];
-    }
-  }
-}
-
 __device__ __forceinline__ float reduce1(const Peers& peers, int world, int64_t flat) {
   float g = 0.f;
   for (int k = 0; k < world; ++k) g += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(peers.grad[k])[flat]);
@@ -141,81 +122,138 @@ __device__ __forceinline__ float adam1(float g, float& w, float* m, float& v, fl
   return w;
 }
 
-template <bool kFromPeers>
-__global__ void __launch_bounds__(kThreads) dp_update_kernel(const __grid_constant__ Peers peers, const StepArgs a) {
-  const Segment s = a.segs[find_segment(a.segs, a.nsegs, blockIdx.x)];
-  const int64_t start = (int64_t(blockIdx.x) - s.block_start) * kChunk;
-  const int64_t end = min(start + int64_t(kChunk), s.n);
-  const float scale = a.grad_scale != nullptr ? *a.grad_scale : 1.f;
-  if (s.vec) {
-    for (int64_t i = start + int64_t(threadIdx.x) * kVec; i < end; i += int64_t(kThreads) * kVec) {
-      const int64_t sh = s.shard + i;
-      float g[8], w[8], v[8], m[8], e[8];
-      if (kFromPeers) reduce8(peers, a.world, s.flat + i, g);
-      else ld8(a.reduced + sh, g);
-      ld8(a.master + sh, w);
-      ld8(a.exp_avg_sq + sh, v);
-      if (a.exp_avg != nullptr) ld8(a.exp_avg + sh, m);
-      if (a.ema != nullptr) ld8(a.ema + sh, e);
+// Load the 8-element gradient group at flat offset `flat` of every rank (raw bf16 words).
+__device__ __forceinline__ void load_grads(const Peers& peers, int world, int64_t flat, uint4 (&raw)[kMaxRanks]) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        adam1(g[k] * scale, w[k], a.exp_avg != nullptr ? &m[k] : nullptr, v[k], a.ema != nullptr ? &e[k] : nullptr, s, a);
-      st8(a.master + sh, w);
-      st8(a.exp_avg_sq + sh, v);
-      if (a.exp_avg != nullptr) st8(a.exp_avg + sh, m);
-      if (a.ema != nullptr) st8(a.ema + sh, e);
-      const uint4 packed = pack8(w);
-#pragma unroll
-      for (int k = 0; k < kMaxRanks; ++k)
-        if (k < a.world) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers.weight[k]) + s.flat + i) = packed;
-    }
-  } else {
-    for (int64_t i = start + threadIdx.x; i < end; i += kThreads) {
-      const int64_t sh = s.shard + i;
-      const float g = (kFromPeers ? reduce1(peers, a.world, s.flat + i) : a.reduced[sh]) * scale;
-      float w = a.master[sh], v = a.exp_avg_sq[sh];
-      w = adam1(g, w, a.exp_avg != nullptr ? a.exp_avg + sh : nullptr, v, a.ema != nullptr ? a.ema + sh : nullptr, s, a);
-      a.master[sh] = w;
-      a.exp_avg_sq[sh] = v;
-      const __nv_bfloat16 b = __float2bfloat16(w);
-      for (int k = 0; k < a.world; ++k) reinterpret_cast<__nv_bfloat16*>(peers.weight[k])[s.flat + i] = b;
-    }
-  }
-  __threadfence_system();  // peer stores are visible before the caller's closing collective
+  for (int k = 0; k < kMaxRanks; ++k)
+    if (k < world) raw[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peers.grad[k]) + flat);
 }
 
-__global__ void __launch_bounds__(kThreads) dp_reduce_kernel(const __grid_constant__ Peers peers, const StepArgs a) {
-  const Segment s = a.segs[find_segment(a.segs, a.nsegs, blockIdx.x)];
-  const int64_t start = (int64_t(blockIdx.x) - s.block_start) * kChunk;
-  const int64_t end = min(start + int64_t(kChunk), s.n);
-  float sq = 0.f;
-  if (s.vec) {
-    for (int64_t i = start + int64_t(threadIdx.x) * kVec; i < end; i += int64_t(kThreads) * kVec) {
-      float g[8];
-      reduce8(peers, a.world, s.flat + i, g);
-      st8(a.reduced_out + s.shard + i, g);
+__device__ __forceinline__ void sum_grads(const uint4 (&raw)[kMaxRanks], int world, float (&g)[8]) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) sq += g[k] * g[k];
-    }
-  } else {
-    for (int64_t i = start + threadIdx.x; i < end; i += kThreads) {
-      const float g = reduce1(peers, a.world, s.flat + i);
-      a.reduced_out[s.shard + i] = g;
-      sq += g * g;
+  for (int e = 0; e < 8; ++e) g[e] = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxRanks; ++k) {
+    if (k < world) {
+      float f[8];
+      unpack8(raw[k], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) g[e] += f[e];
     }
   }
-  // deterministic block sum: warp shuffles, then warp 0 over the warp partials
+}
+
+__device__ __forceinline__ void update8(const float (&gin)[8], float scale, int64_t sh, const Segment& s,
+                                        const StepArgs& a, float (&w)[8]) {
+  float v[8], m[8], e[8];
+  ld8(a.master + sh, w);
+  ld8(a.exp_avg_sq + sh, v);
+  if (a.exp_avg != nullptr) ld8(a.exp_avg + sh, m);
+  if (a.ema != nullptr) ld8(a.ema + sh, e);
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    adam1(gin[k] * scale, w[k], a.exp_avg != nullptr ? &m[k] : nullptr, v[k], a.ema != nullptr ? &e[k] : nullptr, s, a);
+  st8(a.master + sh, w);
+  st8(a.exp_avg_sq + sh, v);
+  if (a.exp_avg != nullptr) st8(a.exp_avg + sh, m);
+  if (a.ema != nullptr) st8(a.ema + sh, e);
+}
+
+// Persistent: CTA b handles chunks b, b + gridDim.x, ...  Within a chunk each thread walks its
+// 8-element groups with the next group's gradient loads (peer loads over NVLink) issued before
+// the current group is updated, so NVLink latency overlaps the HBM traffic of the update.
+template <bool kFromPeers>
+__global__ void __launch_bounds__(kThreads, 2) dp_update_kernel(const __grid_constant__ Peers peers,
+                                                                   const StepArgs a, int64_t nchunks) {
+  const float scale = a.grad_scale != nullptr ? *a.grad_scale : 1.f;
+  for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
+    const Segment s = a.segs[find_segment(a.segs, a.nsegs, chunk)];
+    const int64_t start = (chunk - s.block_start) * kChunk;
+    const int64_t end = min(start + int64_t(kChunk), s.n);
+    if (s.vec) {
+      int64_t i = start + int64_t(threadIdx.x) * kVec;
+      uint4 raw[kMaxRanks];
+      if (kFromPeers && i < end) load_grads(peers, a.world, s.flat + i, raw);
+      for (; i < end; i += int64_t(kThreads) * kVec) {
+        float g[8];
+        if (kFromPeers) {
+          sum_grads(raw, a.world, g);
+          const int64_t nxt = i + int64_t(kThreads) * kVec;
+          if (nxt < end) load_grads(peers, a.world, s.flat + nxt, raw);
+        } else {
+          ld8(a.reduced + s.shard + i, g);
+        }
+        float w[8];
+        update8(g, scale, s.shard + i, s, a, w);
+        const uint4 packed = pack8(w);
+#pragma unroll
+        for (int k = 0; k < kMaxRanks; ++k)
+          if (k < a.world)
+            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers.weight[k]) + s.flat + i) = packed;
+      }
+    } else {
+      for (int64_t i = start + threadIdx.x; i < end; i += kThreads) {
+        const int64_t sh = s.shard + i;
+        const float g = (kFromPeers ? reduce1(peers, a.world, s.flat + i) : a.reduced[sh]) * scale;
+        float w = a.master[sh], v = a.exp_avg_sq[sh];
+        w = adam1(g, w, a.exp_avg != nullptr ? a.exp_avg + sh : nullptr, v, a.ema != nullptr ? a.ema + sh : nullptr,
+                  s, a);
+        a.master[sh] = w;
+        a.exp_avg_sq[sh] = v;
+        const __nv_bfloat16 b = __float2bfloat16(w);
+        for (int k = 0; k < a.world; ++k) reinterpret_cast<__nv_bfloat16*>(peers.weight[k])[s.flat + i] = b;
+      }
+    }
+  }
+  __threadfence_system();  // once per thread: its peer stores are visible before the closing collective
+}
+
+__global__ void __launch_bounds__(kThreads, 2) dp_reduce_kernel(const __grid_constant__ Peers peers,
+                                                                   const StepArgs a, int64_t nchunks) {
+  // One partial sum of squares per chunk (written by the CTA that owns the chunk), so the host
+  // sums a fixed set of partials in a fixed order whatever the grid size.
   __shared__ float part[kThreads / 32];
+  for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
+    const Segment s = a.segs[find_segment(a.segs, a.nsegs, chunk)];
+    const int64_t start = (chunk - s.block_start) * kChunk;
+    const int64_t end = min(start + int64_t(kChunk), s.n);
+    float sq = 0.f;
+    if (s.vec) {
+      for (int64_t i = start + int64_t(threadIdx.x) * kVec; i < end; i += int64_t(kThreads) * kVec) {
+        uint4 raw[kMaxRanks];
+        float g[8];
+        load_grads(peers, a.world, s.flat + i, raw);
+        sum_grads(raw, a.world, g);
+        st8(a.reduced_out + s.shard + i, g);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sq;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float t = threadIdx.x < kThreads / 32 ? part[threadIdx.x] : 0.f;
+        for (int k = 0; k < 8; ++k) sq += g[k] * g[k];
+      }
+    } else {
+      for (int64_t i = start + threadIdx.x; i < end; i += kThreads) {
+        const float g = reduce1(peers, a.world, s.flat + i);
+        a.reduced_out[s.shard + i] = g;
+        sq += g * g;
+      }
+    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    if (threadIdx.x == 0) a.sumsq_out[blockIdx.x] = t;
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < kThreads / 32 ? part[threadIdx.x] : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      if (threadIdx.x == 0) a.sumsq_out[chunk] = t;
+    }
+    __syncthreads();
   }
+}
+
+// Two resident CTAs per SM (the launch bounds), capped by the number of chunks.
+unsigned persistent_grid(int64_t nchunks, int device) {
+  int sms = 0;
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  return static_cast<unsigned>(std::min<int64_t>(nchunks, int64_t(sms) * 2));
 }
 
 Peers make_peers(const std::vector<int64_t>& grads, const std::vector<int64_t>& weights) {
@@ -267,11 +305,12 @@ void dp_step(std::vector<int64_t> peer_grads, std::vector<int64_t> peer_weights,
   StepArgs a = make_args(segs, peer_grads.size(), master, exp_avg, exp_avg_sq, ema, grad_scale, b1, b2, ema_decay);
   if (nblocks == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
+  const unsigned grid = persistent_grid(nblocks, master.device().index());
   if (reduced) {
     a.reduced = reduced->data_ptr<float>();
-    dp_update_kernel<false><<<static_cast<unsigned>(nblocks), kThreads, 0, stream>>>(peers, a);
+    dp_update_kernel<false><<<grid, kThreads, 0, stream>>>(peers, a, nblocks);
   } else {
-    dp_update_kernel<true><<<static_cast<unsigned>(nblocks), kThreads, 0, stream>>>(peers, a);
+    dp_update_kernel<true><<<grid, kThreads, 0, stream>>>(peers, a, nblocks);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -289,7 +328,8 @@ void dp_reduce(std::vector<int64_t> peer_grads, at::Tensor segs, int64_t nblocks
   a.reduced_out = reduced_out.data_ptr<float>();
   a.sumsq_out = sumsq_out.data_ptr<float>();
   if (nblocks == 0) return;
-  dp_reduce_kernel<<<static_cast<unsigned>(nblocks), kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(peers, a);
+  dp_reduce_kernel<<<persistent_grid(nblocks, reduced_out.device().index()), kThreads, 0,
+                     at::cuda::getCurrentCUDAStream()>>>(peers, a, nblocks);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -39,6 +39,10 @@ constexpr int kThreads = 192;
 constexpr uint32_t kTileBytes = kTile * kHeadDim * 2;  // 32 KB
 constexpr uint32_t kChunkBytes = kTileBytes / 2;       // 64-column half: 16 KB
 constexpr float kRescaleThreshold = 8.0f;              // log2 units
+#ifndef MIMIR_FMHA_POLY_EVERY
+#define MIMIR_FMHA_POLY_EVERY 4
+#endif
+constexpr int kPolyEvery = MIMIR_FMHA_POLY_EVERY;      // 0: every exponential on the MUFU pipe
 
 struct FwdParams {
   __nv_bfloat16* y;            // [T, H*128] output (gated when gate != nullptr)
@@ -282,8 +286,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t pk[64];
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        const float a = fast_exp2(fmaf(sv[2 * c], p.scale_log2, -m_use));
-        const float b = fast_exp2(fmaf(sv[2 * c + 1], p.scale_log2, -m_use));
+        // Every kPolyEvery-th pair takes the FMA-pipe exponential so the MUFU pipe is not the
+        // only exp2 unit in use.
+        const bool poly = kPolyEvery > 0 && (c % kPolyEvery) == kPolyEvery - 1;
+        const float xa = fmaf(sv[2 * c], p.scale_log2, -m_use), xb = fmaf(sv[2 * c + 1], p.scale_log2, -m_use);
+        const float a = poly ? poly_exp2(xa) : fast_exp2(xa);
+        const float b = poly ? poly_exp2(xb) : fast_exp2(xb);
         sums[c & 7] += a + b;
         pk[c] = pack_bf16x2(a, b);
       }
