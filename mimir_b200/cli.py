@@ -2,7 +2,8 @@
 
 Commands mirror the reference CLI (``src/mimir/cli.py:11-98``): ``train`` (Hydra-style
 overrides passed through unchanged, ``--suspendable``), ``checkpoint import``, ``export``,
-``serve``, ``eval``, ``schedule``, ``monitor`` and ``doctor``.  Built on argparse.
+``serve``, ``eval``, ``schedule``, ``monitor`` and ``doctor``, plus ``qualify-cpu`` (the reference's
+``tools/qualify_cpu.py`` campaign).  Built on argparse.
 """
 from __future__ import annotations
 
@@ -76,6 +77,11 @@ def _monitor(args, _rest):
     monitor(Store(args.database), args.watch)
 
 
+def _qualify(args, _rest):
+    from mimir_b200.qualify import main as qualify
+    print(qualify(args.output))
+
+
 def _doctor(_args, _rest):
     """Read-only dependency and capability report; never allocates a GPU."""
     from importlib.metadata import PackageNotFoundError, version
@@ -141,6 +147,9 @@ def parser() -> argparse.ArgumentParser:
     mo.add_argument("--watch", action="store_true")
     mo.set_defaults(fn=_monitor)
     sub.add_parser("doctor").set_defaults(fn=_doctor)
+    qc = sub.add_parser("qualify-cpu", help="isolated CPU campaign: train, export, eval, resume, suspend (bit-exact)")
+    qc.add_argument("output", type=Path)
+    qc.set_defaults(fn=_qualify)
     return p
 
 

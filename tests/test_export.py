@@ -80,3 +80,11 @@ def test_export_refuses_corrupt_checkpoint(trained, tmp_path):
     with pytest.raises(ValueError, match="Corrupt"):
         export(copy, tmp_path / "out", tok)
     assert not (tmp_path / "out").exists()
+
+
+def test_cpu_qualification_campaign(tmp_path):
+    """Train / split+resume / EMA export + smoke eval / disk suspension, all bit-exact."""
+    from mimir_b200.qualify import main
+    result = json.loads(main(tmp_path / "campaign").read_text())
+    assert result["status"] == "passed"
+    assert (tmp_path / "campaign" / "evaluation" / "receipt.json").is_file()
