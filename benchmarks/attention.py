@@ -51,11 +51,13 @@ def main():
     do = torch.randn(T, H * 128, device="cuda", dtype=torch.bfloat16)
     C = ops.ext()
     cu, pl = meta["cu_seqlens"], meta["prefix_lens"]
-    tiles, ntiles = attention_plan(cu, pl, nseq, T, args.causal)
+    from mimir_b200.ops.attention import forward_kernel
+    fwd_kernel, kind = forward_kernel()
+    tiles, ntiles = attention_plan(cu, pl, nseq, T, args.causal, kind=kind)
     kv_tiles, kv_ntiles = attention_plan(cu, pl, nseq, T, args.causal, backward=True)
 
     def fwd():
-        return C.fmha_fwd(q, 0, k, 0, v, 0, None, 0, H, KV, args.causal, cu, pl, nseq, tiles, ntiles)
+        return fwd_kernel(q, 0, k, 0, v, 0, None, 0, H, KV, args.causal, cu, pl, nseq, tiles, ntiles)
 
     out, lse = fwd()
     delta = C.attn_delta(do, out, H)

@@ -32,6 +32,13 @@ std::vector<at::Tensor> fmha_fwd(at::Tensor q_src, int64_t q_col, at::Tensor k_s
                                  int64_t KV, bool is_causal, at::Tensor cu_seqlens, at::Tensor prefix_lens,
                                  int64_t numseqs, at::Tensor tiles, at::Tensor ntiles);
 int64_t fmha_status(at::Device dev);
+// fmha_fwd2.cu
+std::vector<at::Tensor> fmha_plan2(at::Tensor cu_seqlens, at::Tensor prefix_lens, int64_t numseqs,
+                                   int64_t total_tokens, bool is_causal);
+std::vector<at::Tensor> fmha_fwd2(at::Tensor q_src, int64_t q_col, at::Tensor k_src, int64_t k_col, at::Tensor v_src,
+                                  int64_t v_col, c10::optional<at::Tensor> gate_src, int64_t gate_col, int64_t H,
+                                  int64_t KV, bool is_causal, at::Tensor cu_seqlens, at::Tensor prefix_lens,
+                                  int64_t numseqs, at::Tensor tiles, at::Tensor ntiles);
 // fmha_bwd.cu
 std::vector<at::Tensor> fmha_bwd_plan(at::Tensor cu_seqlens, at::Tensor prefix_lens, int64_t numseqs,
                                       int64_t total_tokens, bool is_causal);
@@ -73,6 +80,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fmha_plan", &fmha_plan);
   m.def("fmha_fwd", &fmha_fwd);
   m.def("fmha_status", &fmha_status);
+  m.def("fmha_plan2", &fmha_plan2);
+  m.def("fmha_fwd2", &fmha_fwd2);
   m.def("fmha_bwd_plan", &fmha_bwd_plan);
   m.def("dp_segment_bytes", &dp_segment_bytes);
   m.def("dp_chunk_elements", &dp_chunk_elements);

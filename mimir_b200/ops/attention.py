@@ -16,6 +16,8 @@ also applies RoPE to Q/K beforehand and the ``sigmoid(gate)`` output gate in its
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.nn.functional as F
 
@@ -75,14 +77,26 @@ def _fmha_bwd_ready() -> bool:
     return hasattr(ext(), "fmha_bwd")
 
 
+def forward_kernel():
+    """``(kernel, plan kind)`` of the attention forward: the two-query-tile kernel
+    (``fmha_fwd2``, default) or the one-tile kernel (``MIMIR_FMHA_FWD=1``)."""
+    C = ext()
+    if os.environ.get("MIMIR_FMHA_FWD", "2") == "2" and hasattr(C, "fmha_fwd2"):
+        return C.fmha_fwd2, "fwd2"
+    return C.fmha_fwd, "fwd"
+
+
 def attention_plan(cu_seqlens: torch.Tensor, prefix_lens: torch.Tensor, numseqs: int, total_tokens: int,
-                   is_causal: bool, backward: bool = False):
+                   is_causal: bool, backward: bool = False, kind: str | None = None):
     """Device tile schedule ``(tiles, ntiles)`` for a packed batch, cached on the metadata tensor.
 
-    Every attention layer of a forward (and its backward) sees the same packed layout, so the
+    ``kind`` is ``"bwd"`` (key blocks), ``"fwd"`` (128-row query tiles) or ``"fwd2"`` (256-row
+    query tiles); by default the backward schedule or the active forward kernel's.  Every
+    attention layer of a forward (and its backward) sees the same packed layout, so the
     schedule is built once per batch; the cache is invalidated if ``cu_seqlens`` is modified.
     """
-    key = (bool(backward), bool(is_causal), int(numseqs), int(total_tokens), prefix_lens.data_ptr(),
+    kind = kind or ("bwd" if backward else forward_kernel()[1])
+    key = (kind, bool(is_causal), int(numseqs), int(total_tokens), prefix_lens.data_ptr(),
            prefix_lens._version)
     cache = getattr(cu_seqlens, "_mimir_fmha_plans", None)
     if cache is None or cache[0] != cu_seqlens._version:
@@ -93,7 +107,7 @@ def attention_plan(cu_seqlens: torch.Tensor, prefix_lens: torch.Tensor, numseqs:
             pass
     plan = cache[1].get(key)
     if plan is None:
-        build = ext().fmha_bwd_plan if backward else ext().fmha_plan
+        build = {"bwd": ext().fmha_bwd_plan, "fwd": ext().fmha_plan, "fwd2": getattr(ext(), "fmha_plan2", None)}[kind]
         plan = build(cu_seqlens, prefix_lens, int(numseqs), int(total_tokens), bool(is_causal))
         cache[1][key] = plan
     return plan
@@ -108,8 +122,9 @@ class _PrefixLMAttentionFn(torch.autograd.Function):
         KV = k.shape[1]
         q2, k2, v2 = q.reshape(T, H * D).contiguous(), k.reshape(T, KV * D).contiguous(), v.reshape(T, KV * D).contiguous()
         cu, pl = cu_seqlens.to(torch.int32).contiguous(), prefix_lens.to(torch.int32).contiguous()
-        tiles, ntiles = attention_plan(cu, pl, numseqs, T, is_causal)
-        out, lse = ext().fmha_fwd(q2, 0, k2, 0, v2, 0, None, 0, H, KV, is_causal, cu, pl, numseqs, tiles, ntiles)
+        fwd, kind = forward_kernel()
+        tiles, ntiles = attention_plan(cu, pl, numseqs, T, is_causal, kind=kind)
+        out, lse = fwd(q2, 0, k2, 0, v2, 0, None, 0, H, KV, is_causal, cu, pl, numseqs, tiles, ntiles)
         ctx.save_for_backward(q2, k2, v2, out, lse, cu, pl, tiles, ntiles)
         ctx.info = (H, KV, is_causal, numseqs)
         return out.view(T, H, D)
@@ -155,9 +170,10 @@ class _GatedAttentionFn(torch.autograd.Function):
         C = ext()
         T = gqkv.shape[0]
         qk = C.rope_qk(gqkv, cos, sin, positions, H, KV)  # rotated [T, (H+KV)*hd]
-        tiles, ntiles = attention_plan(cu_seqlens, prefix_lens, numseqs, T, is_causal)
+        fwd, kind = forward_kernel()
+        tiles, ntiles = attention_plan(cu_seqlens, prefix_lens, numseqs, T, is_causal, kind=kind)
         # q at column 0 of qk, k at H*hd; v at (2H+KV)*hd of gqkv; gate at column 0 of gqkv.
-        y, lse, o = C.fmha_fwd(qk, 0, qk, H * hd, gqkv, (2 * H + KV) * hd, gqkv, 0, H, KV, is_causal,
+        y, lse, o = fwd(qk, 0, qk, H * hd, gqkv, (2 * H + KV) * hd, gqkv, 0, H, KV, is_causal,
                                cu_seqlens, prefix_lens, numseqs, tiles, ntiles)
         ctx.save_for_backward(gqkv, qk, o, lse, cos, sin, positions, cu_seqlens, prefix_lens, tiles, ntiles)
         ctx.info = (H, KV, hd, is_causal, numseqs)

@@ -129,6 +129,19 @@ def test_fmha_forward(lengths, prefixes, H, KV, causal):
     _close(out[:total], ref[:total], 2e-2, 2e-2, "fmha fwd")
 
 
+@pytest.mark.parametrize("lengths,prefixes,H,KV", CASES)
+def test_fmha_forward_kernels_agree(lengths, prefixes, H, KV, monkeypatch):
+    """The two-query-tile forward (default) and the one-tile forward give the same rows and LSE."""
+    q, k, v, meta = _packed(lengths, prefixes, H, KV, pad=37, seed=3)
+    total = sum(lengths)
+    outs = {}
+    for version in ("1", "2"):
+        monkeypatch.setenv("MIMIR_FMHA_FWD", version)
+        outs[version] = ops.prefixlm_attention(q, k, v, False, **meta)
+    assert ops.ext().fmha_status(q.device) == 0
+    _close(outs["2"][:total], outs["1"][:total], 2e-2, 2e-2, "fmha fwd2 vs fwd1")
+
+
 def test_gated_attention_block_matches_composite():
     from mimir_b200.models.layers import RotaryEmbedding
     torch.manual_seed(0)
