@@ -15,7 +15,8 @@
 // memory.  A new S_X is issued only after the PV that reads P_X, and P_X is only rewritten after
 // that PV has completed (o_done), so the aliasing is ordered both ways.
 //
-// Warps (320 threads): 0 TMA producer, 1 TMEM owner + MMA issuer, 2..5 softmax/epilogue of tile
+// Warps (320 threads; with 3 warps on two of the four SM sub-partitions the register cap is 168 per
+// thread): 0 TMA producer, 1 TMEM owner + MMA issuer, 2..5 softmax/epilogue of tile
 // A, 6..9 softmax/epilogue of tile B (warp w reaches TMEM lanes 32*(w%4)..+31).  Lazy O
 // rescaling (only when a row max grows by more than 2^8).  Every mbarrier wait is bounded
 // (common.cuh); a timeout records a status code and all roles fall through to a teardown that
@@ -129,7 +130,7 @@ __device__ __forceinline__ void tmem_st32_u(uint32_t taddr, const uint32_t* v) {
       : "memory");
 }
 
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kThreads, 1)
     fmha_fwd2_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                      const __grid_constant__ CUtensorMap map_v, const Fwd2Params p) {
   extern __shared__ uint8_t smem_raw[];
