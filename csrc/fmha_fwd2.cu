@@ -41,10 +41,8 @@ constexpr int kThreads = 320;
 constexpr uint32_t kTileBytes = kTile * kHeadDim * 2;  // 32 KB
 constexpr uint32_t kChunkBytes = kTileBytes / 2;       // one 64-column half
 constexpr float kRescaleThreshold = 8.0f;
-#ifndef MIMIR_FMHA2_POLY_EVERY
-#define MIMIR_FMHA2_POLY_EVERY 4
-#endif
-constexpr int kPolyEvery = MIMIR_FMHA2_POLY_EVERY;     // every kPolyEvery-th exponential pair on the FMA pipe
+// Every kPolyEvery-th exponential pair is computed on the FMA pipe (poly_exp2) instead of MUFU;
+// the kernel is instantiated for 0 (off), 2, 4 and 8 and MIMIR_FMHA2_POLY_EVERY selects (default 4).
 
 struct Fwd2Params {
   __nv_bfloat16* y;
@@ -130,6 +128,7 @@ __device__ __forceinline__ void tmem_st32_u(uint32_t taddr, const uint32_t* v) {
       : "memory");
 }
 
+template <int kPolyEvery>
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_fwd2_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                      const __grid_constant__ CUtensorMap map_v, const Fwd2Params p) {
@@ -538,13 +537,22 @@ std::vector<at::Tensor> fmha_fwd2(at::Tensor q_src, int64_t q_col, at::Tensor k_
   prm.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
   prm.status = fmha_status_ptr(q_src.device());
 
+  static const int poly = [] {
+    const char* env = std::getenv("MIMIR_FMHA2_POLY_EVERY");
+    const int v = env != nullptr ? std::atoi(env) : 4;
+    TORCH_CHECK(v == 0 || v == 2 || v == 4 || v == 8, "MIMIR_FMHA2_POLY_EVERY must be 0, 2, 4 or 8");
+    return v;
+  }();
+  auto kernel = poly == 0 ? fmha_fwd2_kernel<0> : poly == 2 ? fmha_fwd2_kernel<2>
+              : poly == 8 ? fmha_fwd2_kernel<8> : fmha_fwd2_kernel<4>;
   static bool attr_set[16] = {false};
   if (!attr_set[q_src.device().index()]) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(fmha_fwd2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    for (auto k : {fmha_fwd2_kernel<0>, fmha_fwd2_kernel<2>, fmha_fwd2_kernel<4>, fmha_fwd2_kernel<8>})
+      C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
     attr_set[q_src.device().index()] = true;
   }
   dim3 grid((unsigned)H, (unsigned)tiles.size(0));
-  fmha_fwd2_kernel<<<grid, kThreads, kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(mq, mk, mv, prm);
+  kernel<<<grid, kThreads, kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(mq, mk, mv, prm);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return gated ? std::vector<at::Tensor>{y, lse, o} : std::vector<at::Tensor>{y, lse};
 }
