@@ -42,7 +42,8 @@ constexpr uint32_t kTileBytes = kTile * kHeadDim * 2;  // 32 KB
 constexpr uint32_t kChunkBytes = kTileBytes / 2;       // one 64-column half
 constexpr float kRescaleThreshold = 8.0f;
 // Every kPolyEvery-th exponential pair is computed on the FMA pipe (poly_exp2) instead of MUFU;
-// the kernel is instantiated for 0 (off), 2, 4 and 8 and MIMIR_FMHA2_POLY_EVERY selects (default 4).
+// the kernel is instantiated for 0 (off), 2, 4 and 8 and MIMIR_FMHA2_POLY_EVERY selects; the default is
+// 0: with two softmax warpgroups MUFU is not the limit and the polynomial costs issue slots (measured).
 
 struct Fwd2Params {
   __nv_bfloat16* y;
@@ -539,7 +540,7 @@ std::vector<at::Tensor> fmha_fwd2(at::Tensor q_src, int64_t q_col, at::Tensor k_
 
   static const int poly = [] {
     const char* env = std::getenv("MIMIR_FMHA2_POLY_EVERY");
-    const int v = env != nullptr ? std::atoi(env) : 4;
+    const int v = env != nullptr ? std::atoi(env) : 0;
     TORCH_CHECK(v == 0 || v == 2 || v == 4 || v == 8, "MIMIR_FMHA2_POLY_EVERY must be 0, 2, 4 or 8");
     return v;
   }();
