@@ -94,11 +94,8 @@ constexpr uint32_t kSmemDS = kSmemP + kPBytes;
 constexpr uint32_t kSmemDQ = kSmemDS + kPBytes;                  // 2 x [32 rows][128] fp32 staging tiles
 constexpr int kDqRows = 32;                                         // rows per TMA reduce
 constexpr uint32_t kDqTileBytes = kDqRows * kHeadDim * 4;           // 16 KB
-constexpr uint32_t kSmemStash = kSmemDQ + 2 * kDqTileBytes;        // [parity][half][lse 32 | delta 32] fp32
-constexpr uint32_t kStashBytes = 2 * 2 * 64 * 4;
-constexpr uint32_t kSmemBar = kSmemStash + kStashBytes;
+constexpr uint32_t kSmemBar = kSmemDQ + 2 * kDqTileBytes;
 constexpr uint32_t kSmemBytes = kSmemBar + sizeof(Barriers) + 1024;
-static_assert(kSmemBytes <= 232448, "backward shared memory exceeds 227 KB");
 
 __device__ __forceinline__ uint8_t* q_stage(uint8_t* b, int s) { return b + kSmemQ0 + s * 2 * kQBytes; }
 __device__ __forceinline__ uint8_t* do_stage(uint8_t* b, int s) { return q_stage(b, s) + kQBytes; }
@@ -288,7 +285,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t col_off = half * 32;
     const uint32_t sP = smem_u32(smem + kSmemP);
     const uint32_t sDS = smem_u32(smem + kSmemDS);
-    const uint32_t sStash = smem_u32(smem + kSmemStash);
     // LSE / Delta of this warp's 32 queries live in registers (lane l holds query 32*half + l)
     // and are fetched one iteration ahead to hide the global latency.
     auto fetch = [&](int i, float& lse2, float& dl) {
@@ -315,39 +311,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&bar->s_free);
       wmark(i, 1);
       uint32_t pk[16], dk[16];
-      // The 32 query columns' LSE/Delta are the same for every lane (key row): stage them in
-      // shared memory (each of the half's four warps writes the identical values, parity-double-
-      // buffered because a warp can be one iteration ahead of another) and read them back as
-      // 16-byte broadcasts instead of two shuffles per element.
-      const uint32_t st = sStash + ((i & 1) * 2 + half) * 256;
-      st_shared_f32(st + lane * 4, cur_lse);
-      st_shared_f32(st + 128 + lane * 4, cur_dl);
-      __syncwarp();
-      // Tiles that every key row sees completely skip the mask arithmetic; the others give masked
-      // entries an exponent argument of -inf (exp2 -> 0) in one branch-free block.
+      // Branch-free element loop: masked entries get an exponent argument of -inf (exp2 -> 0), so
+      // the compiler keeps one basic block and interleaves the 32 independent element chains.
       const bool full = (q0 + kQRows <= L) && (k0 + kKeys - 1 <= (q0 < P ? P - 1 : q0));
       const int qbase = q0 + (int)col_off;
 #pragma unroll
-      for (int c = 0; c < 32; c += 4) {
-        float lv[4], dv[4], pe[4], de[4];
-        ld_shared_v4f(st + c * 4, lv[0], lv[1], lv[2], lv[3]);
-        ld_shared_v4f(st + 128 + c * 4, dv[0], dv[1], dv[2], dv[3]);
+      for (int c = 0; c < 32; c += 2) {
+        float pe[2], de[2];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
+        for (int e = 0; e < 2; ++e) {
           const int col = c + e;
-          float arg = fmaf(sv[col], p.scale_log2, -lv[e]);
-          if (!full) {
-            const int q = qbase + col;
-            const int lim = q < P ? P - 1 : q;
-            arg = ((q < L) & (key <= lim)) ? arg : -INFINITY;
-          }
-          pe[e] = fast_exp2(arg);
-          de[e] = pe[e] * (dpv[col] - dv[e]);
+          const float lse_c = __shfl_sync(0xffffffffu, cur_lse, col);
+          const float dl_c = __shfl_sync(0xffffffffu, cur_dl, col);
+          const int q = qbase + col;
+          const int lim = q < P ? P - 1 : q;
+          const bool vis = full | ((q < L) & (key <= lim));
+          const float arg = vis ? fmaf(sv[col], p.scale_log2, -lse_c) : -INFINITY;
+          const float pv = fast_exp2(arg);
+          pe[e] = pv;
+          de[e] = pv * (dpv[col] - dl_c);
         }
         pk[c >> 1] = pack_bf16x2(pe[0], pe[1]);
-        pk[(c >> 1) + 1] = pack_bf16x2(pe[2], pe[3]);
         dk[c >> 1] = pack_bf16x2(de[0], de[1]);
-        dk[(c >> 1) + 1] = pack_bf16x2(de[2], de[3]);
       }
       wmark(i, 2);
       if (i > 0 && !warp_wait(&bar->pds_free, (i - 1) & 1, p.status, kStatusTimeoutP)) { ok = false; break; }
