@@ -4,6 +4,8 @@
 // elementwise.cu
 std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, double eps);
 at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor rstd);
+std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, at::Tensor delta, double eps);
+at::Tensor rmsnorm_bwd_res(at::Tensor dy, at::Tensor x, at::Tensor rstd, at::Tensor dres);
 at::Tensor swiglu_fwd(at::Tensor gu);
 at::Tensor swiglu_bwd(at::Tensor dp, at::Tensor gu);
 at::Tensor rope_qk(at::Tensor gqkv, at::Tensor cos_t, at::Tensor sin_t, at::Tensor pos, int64_t H, int64_t KV);
@@ -66,6 +68,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mimir_b200 hand-written sm_100a kernels";
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
+  m.def("rmsnorm_bwd_res", &rmsnorm_bwd_res);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("rope_qk", &rope_qk);

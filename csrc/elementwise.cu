@@ -136,6 +136,81 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const T* __restrict__ 
   }
 }
 
+// h = x + delta (rounded to T, as the unfused residual add stores it); y = rmsnorm(h).
+template <typename T, int VPT>
+__global__ void __launch_bounds__(256) add_rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ delta,
+                                                              T* __restrict__ h, T* __restrict__ y,
+                                                              float* __restrict__ rstd_out, int d, float eps) {
+  constexpr int N = Vec<T>::N;
+  __shared__ float scratch[32];
+  const int64_t row = blockIdx.x;
+  float v[VPT][N];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (i * blockDim.x + threadIdx.x) * N;
+    if (c < d) {
+      float a[N];
+      Vec<T>::load(x + row * d + c, v[i]);
+      Vec<T>::load(delta + row * d + c, a);
+#pragma unroll
+      for (int j = 0; j < N; ++j) v[i][j] += a[j];
+      Vec<T>::store(h + row * d + c, v[i]);
+      Vec<T>::load(h + row * d + c, v[i]);  // the rounded sum, exactly what a separate add would store
+#pragma unroll
+      for (int j = 0; j < N; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  ss = block_sum(ss, scratch);
+  const float r = rsqrtf(ss / d + eps);
+  if (threadIdx.x == 0) rstd_out[row] = r;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (i * blockDim.x + threadIdx.x) * N;
+    if (c < d) {
+      float o[N];
+#pragma unroll
+      for (int j = 0; j < N; ++j) o[j] = v[i][j] * r;
+      Vec<T>::store(y + row * d + c, o);
+    }
+  }
+}
+
+// dx = rmsnorm_bwd(dy; x, rstd) + dres: the residual stream's own gradient joins in the same pass.
+template <typename T, int VPT>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_res_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                                              const float* __restrict__ rstd,
+                                                              const T* __restrict__ dres, T* __restrict__ dx, int d) {
+  constexpr int N = Vec<T>::N;
+  __shared__ float scratch[32];
+  const int64_t row = blockIdx.x;
+  const float r = rstd[row];
+  float xv[VPT][N], gv[VPT][N];
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (i * blockDim.x + threadIdx.x) * N;
+    if (c < d) {
+      Vec<T>::load(x + row * d + c, xv[i]);
+      Vec<T>::load(dy + row * d + c, gv[i]);
+#pragma unroll
+      for (int j = 0; j < N; ++j) dot += gv[i][j] * xv[i][j] * r;
+    }
+  }
+  dot = block_sum(dot, scratch) / d;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (i * blockDim.x + threadIdx.x) * N;
+    if (c < d) {
+      float o[N], rv[N];
+      Vec<T>::load(dres + row * d + c, rv);
+#pragma unroll
+      for (int j = 0; j < N; ++j) o[j] = r * (gv[i][j] - xv[i][j] * r * dot) + rv[j];
+      Vec<T>::store(dx + row * d + c, o);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ SwiGLU
 __device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
 
@@ -352,6 +427,48 @@ void launch_rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Ten
   else TORCH_CHECK(false, "rmsnorm: hidden size too large");
 }
 
+template <typename T>
+void launch_add_rmsnorm_fwd(const at::Tensor& x, const at::Tensor& delta, at::Tensor& h, at::Tensor& y,
+                            at::Tensor& rstd, float eps, cudaStream_t st) {
+  const int d = x.size(-1);
+  const int64_t rows = x.numel() / d;
+  const int vecs = d / Vec<T>::N;
+  const int threads = std::min(256, ((vecs + 31) / 32) * 32);
+  const int vpt = (vecs + threads - 1) / threads;
+  auto xp = reinterpret_cast<const T*>(x.data_ptr());
+  auto dp = reinterpret_cast<const T*>(delta.data_ptr());
+  auto hp = reinterpret_cast<T*>(h.data_ptr());
+  auto yp = reinterpret_cast<T*>(y.data_ptr());
+  float* rp = rstd.data_ptr<float>();
+  if (rows == 0) return;
+  if (vpt <= 1) add_rmsnorm_fwd_kernel<T, 1><<<rows, threads, 0, st>>>(xp, dp, hp, yp, rp, d, eps);
+  else if (vpt <= 2) add_rmsnorm_fwd_kernel<T, 2><<<rows, threads, 0, st>>>(xp, dp, hp, yp, rp, d, eps);
+  else if (vpt <= 4) add_rmsnorm_fwd_kernel<T, 4><<<rows, threads, 0, st>>>(xp, dp, hp, yp, rp, d, eps);
+  else if (vpt <= 8) add_rmsnorm_fwd_kernel<T, 8><<<rows, threads, 0, st>>>(xp, dp, hp, yp, rp, d, eps);
+  else TORCH_CHECK(false, "add_rmsnorm: hidden size too large");
+}
+
+template <typename T>
+void launch_rmsnorm_bwd_res(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& rstd,
+                            const at::Tensor& dres, at::Tensor& dx, cudaStream_t st) {
+  const int d = x.size(-1);
+  const int64_t rows = x.numel() / d;
+  const int vecs = d / Vec<T>::N;
+  const int threads = std::min(256, ((vecs + 31) / 32) * 32);
+  const int vpt = (vecs + threads - 1) / threads;
+  auto a = reinterpret_cast<const T*>(dy.data_ptr());
+  auto b = reinterpret_cast<const T*>(x.data_ptr());
+  auto res = reinterpret_cast<const T*>(dres.data_ptr());
+  auto o = reinterpret_cast<T*>(dx.data_ptr());
+  const float* r = rstd.data_ptr<float>();
+  if (rows == 0) return;
+  if (vpt <= 1) rmsnorm_bwd_res_kernel<T, 1><<<rows, threads, 0, st>>>(a, b, r, res, o, d);
+  else if (vpt <= 2) rmsnorm_bwd_res_kernel<T, 2><<<rows, threads, 0, st>>>(a, b, r, res, o, d);
+  else if (vpt <= 4) rmsnorm_bwd_res_kernel<T, 4><<<rows, threads, 0, st>>>(a, b, r, res, o, d);
+  else if (vpt <= 8) rmsnorm_bwd_res_kernel<T, 8><<<rows, threads, 0, st>>>(a, b, r, res, o, d);
+  else TORCH_CHECK(false, "rmsnorm: hidden size too large");
+}
+
 void check_cuda_contig(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
   TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
@@ -381,6 +498,37 @@ at::Tensor rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor rstd) {
   auto st = at::cuda::getCurrentCUDAStream();
   if (x.scalar_type() == at::kBFloat16) launch_rmsnorm_bwd<__nv_bfloat16>(dy, x, rstd, dx, st);
   else if (x.scalar_type() == at::kFloat) launch_rmsnorm_bwd<float>(dy, x, rstd, dx, st);
+  else TORCH_CHECK(false, "rmsnorm: unsupported dtype");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dx;
+}
+
+std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, at::Tensor delta, double eps) {
+  check_cuda_contig(x, "x");
+  check_cuda_contig(delta, "delta");
+  TORCH_CHECK(x.sizes() == delta.sizes() && x.scalar_type() == delta.scalar_type(), "add_rmsnorm: x/delta mismatch");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto h = at::empty_like(x);
+  auto y = at::empty_like(x);
+  const int64_t rows = x.numel() / x.size(-1);
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (x.scalar_type() == at::kBFloat16) launch_add_rmsnorm_fwd<__nv_bfloat16>(x, delta, h, y, rstd, (float)eps, st);
+  else if (x.scalar_type() == at::kFloat) launch_add_rmsnorm_fwd<float>(x, delta, h, y, rstd, (float)eps, st);
+  else TORCH_CHECK(false, "add_rmsnorm: unsupported dtype");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {h, y, rstd};
+}
+
+at::Tensor rmsnorm_bwd_res(at::Tensor dy, at::Tensor x, at::Tensor rstd, at::Tensor dres) {
+  check_cuda_contig(dy, "dy");
+  check_cuda_contig(x, "x");
+  check_cuda_contig(dres, "dres");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto dx = at::empty_like(x);
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (x.scalar_type() == at::kBFloat16) launch_rmsnorm_bwd_res<__nv_bfloat16>(dy, x, rstd, dres, dx, st);
+  else if (x.scalar_type() == at::kFloat) launch_rmsnorm_bwd_res<float>(dy, x, rstd, dres, dx, st);
   else TORCH_CHECK(false, "rmsnorm: unsupported dtype");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dx;

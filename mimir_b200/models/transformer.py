@@ -101,8 +101,8 @@ class TransformerBlock(nn.Module):
                 raise ValueError("stability_scope is required when diagnostics are enabled")
             return self._forward_with_diagnostics(x, stability_diagnostics, stability_scope, **seq_info)
         if self.norm_type == "pre":
-            x = x + self.attn(self.norm(x), **seq_info)
-            return x + self.mlp(self.norm(x))
+            h, n = ops.add_rms_norm(x, self.attn(self.norm(x), **seq_info), self.norm.eps)
+            return h + self.mlp(n)
         x = self.norm(x + self.attn(x, **seq_info))
         return self.norm(x + self.mlp(x))
 

@@ -5,7 +5,7 @@ CUDA tensors and to a plain PyTorch formulation otherwise (CPU, or
 ``MIMIR_DISABLE_KERNELS=1``).
 """
 from mimir_b200.ops._ext import ext, available, kernels_enabled  # noqa: F401
-from mimir_b200.ops.norm import rms_norm  # noqa: F401
+from mimir_b200.ops.norm import add_rms_norm, rms_norm  # noqa: F401
 from mimir_b200.ops.swiglu import swiglu, swiglu_reference  # noqa: F401
 from mimir_b200.ops.attention import (  # noqa: F401
     dense_prefixlm_attention, prefixlm_attention, gated_prefixlm_attention, gated_attention_composite)

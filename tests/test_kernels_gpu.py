@@ -30,6 +30,27 @@ def test_rmsnorm(d):
     _close(x.grad, xr.grad, 3e-2, 2e-2, "rmsnorm bwd")
 
 
+def test_add_rmsnorm_matches_composite():
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(300, 2048, device="cuda", generator=g).to(torch.bfloat16).requires_grad_(True)
+    a = torch.randn(300, 2048, device="cuda", generator=g).to(torch.bfloat16).requires_grad_(True)
+    h, y = ops.add_rms_norm(x, a, 1e-6)
+    hr = (x.float() + a.float()).to(torch.bfloat16)
+    yr = torch.nn.functional.rms_norm(hr.float(), (2048,), eps=1e-6)
+    assert torch.equal(h, hr)
+    _close(y.float(), yr, 2e-2, 2e-2, "add_rmsnorm fwd")
+    dh = torch.randn_like(h)
+    dy = torch.randn_like(y)
+    (h.float() * dh.float()).sum().add((y.float() * dy.float()).sum()).backward()
+    xr = x.detach().float().requires_grad_(True)
+    ar = a.detach().float().requires_grad_(True)
+    hr2 = xr + ar
+    yr2 = torch.nn.functional.rms_norm(hr2, (2048,), eps=1e-6)
+    (hr2 * dh.float()).sum().add((yr2 * dy.float()).sum()).backward()
+    _close(x.grad.float(), xr.grad, 3e-2, 3e-2, "add_rmsnorm bwd x")
+    assert torch.equal(x.grad, a.grad)
+
+
 def test_swiglu():
     gu = torch.randn(257, 2 * 5632, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     out = ops.swiglu(gu)
