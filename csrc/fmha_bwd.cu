@@ -58,7 +58,7 @@ struct BwdParams {
   int* status;
   unsigned long long* trace;   // optional event timestamps of CTA (0, trace_tile) for profiling
   int trace_tile;
-  int mode;                    // profiling experiments only: bit0 no shuffles, bit1 no mask, bit2 no exp
+  int mode;                    // profiling experiments only (results invalid): bit3 no dQ reduce-add, bit4 no dQ staging
 };
 
 // Event slots per iteration in the optional trace buffer.
@@ -416,15 +416,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tile = sdq_addr + sb * kDqTileBytes;
         const float* src = h2 == 0 ? a : c2;
 #pragma unroll
-        for (int c = 0; c < 32; ++c)
-          st_shared_f32(tile + (c * kHeadDim + d) * 4, (q0 + 32 * h2 + c < L) ? src[c] * p.scale : 0.f);
+        if (!(p.mode & 16))
+          for (int c = 0; c < 32; ++c)
+            st_shared_f32(tile + (c * kHeadDim + d) * 4, (q0 + 32 * h2 + c < L) ? src[c] * p.scale : 0.f);
         fence_async_shared();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar->dqs_full[sb]);
         bool ok2 = true;
         if (issuer) {
           ok2 = mbar_wait(&bar->dqs_full[sb], (ph >> 1) & 1, p.status, kStatusTimeoutOther);
-          if (ok2) {
+          if (ok2 && (p.mode & 8)) {
+            if (ph >= 1) mbar_arrive(&bar->dqs_free[sb ^ 1]);  // experiment: no global dQ reduction
+          } else if (ok2) {
             tma_reduce_add_2d(&map_dq, smem + kSmemDQ + sb * kDqTileBytes, hq * kHeadDim, start + q0 + 32 * h2);
             bulk_commit_group();
             pending = true;
