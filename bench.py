@@ -1,8 +1,11 @@
 """Training-throughput benchmark: Mimir2 dense ~1.3B (24 x 2048, 16 Q / 4 KV heads of 128,
 SwiGLU 5632, vocab 65536), seq 4096, 4 sequences per GPU, prefix-LM mask with prompt length
 uniform in [0, 2048], FSDP2 bf16 compute / fp32 master weights, AdamATan2 (+EMA).
+``--optimizer muon`` is the Muon variant of the same model (5 Newton-Schulz iterations,
+coefficients (3.4445, -4.7750, 2.0315), momentum 0.95 on every 2-D hidden matrix; Adam for
+embeddings, norms and the head).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--optimizer adam_atan2|muon]
 
 For N > 1 run under ``torch.distributed.run`` (one rank per GPU).  Rank 0 prints one JSON
 line.  ``value`` is device-timed (CUDA events around exactly K steps, barrier + synchronize
@@ -29,6 +32,9 @@ SEQ_LEN, SEQS_PER_GPU, VOCAB = 4096, 4, 65536
 MODEL = dict(n_layers=24, hidden_size=2048, num_heads=16, num_key_value_heads=4, expansion=4.125)
 METRIC = "train tokens/sec (box, device-timed, max over ranks) at 1/2/4/8 B200; MFU"
 BASELINE_VALUE = None  # the reference publishes no throughput number
+OPTIMIZER_LABEL = {"adam_atan2": "AdamATan2 + EMA",
+                   "muon": "MuonAdamW + EMA (Muon on 2-D hidden matrices, 5 Newton-Schulz iterations in fp32, "
+                           "momentum 0.95; Adam on the rest)"}
 
 
 def arch_dict(kv_heads=4):
@@ -186,7 +192,8 @@ def run_ours(args, rank, world, local):
     vocab = arch.pop("vocab_size")
     config = PretrainConfig(arch=arch, data=dict(path="synthetic"), global_batch_size=SEQ_LEN * SEQS_PER_GPU * world,
                             epochs=1, lr=3e-4, lr_warmup_steps=0, lr_min_ratio=1.0, weight_decay=0.1, beta1=0.9,
-                            beta2=0.95, ema=0.9999, distributed_strategy=args.dp, lr_auto=False)
+                            beta2=0.95, ema=0.9999, distributed_strategy=args.dp, lr_auto=False,
+                            optimizer=args.optimizer, muon_momentum=0.95, muon_ns_steps=5)
     torch.manual_seed(0)
     model, carry, optim = create_model_and_optimizer(config, {"vocab_size": vocab, "max_seq_len": SEQ_LEN}, device)
     state = make_train_state(config, model, carry, optim, total_steps=10_000, device=device)
@@ -221,8 +228,15 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     e2e_seconds = max_over_ranks(time.perf_counter() - t0)
     flops = model_flops_per_step(hosts[0][0], MODEL["num_key_value_heads"])
-    label = (f"dp{world}: replicated bf16 weights, fp32 master+AdamATan2 state sharded like FSDP2, one fused "
-             "NVLink reduce-scatter+update+all-gather kernel per step" if args.dp == "replicated" else f"fsdp{world}")
+    if args.dp != "replicated":
+        label = f"fsdp{world}"
+    elif args.optimizer == "muon":
+        label = (f"dp{world}: replicated bf16 weights, fp32 master+optimizer state sharded like FSDP2; fused NVLink "
+                 "reduce + Adam/momentum + gather-to-owner kernel, Newton-Schulz once per matrix on its owner rank, "
+                 "fused scatter + update + all-gather kernel")
+    else:
+        label = (f"dp{world}: replicated bf16 weights, fp32 master+AdamATan2 state sharded like FSDP2, one fused "
+                 "NVLink reduce-scatter+update+all-gather kernel per step")
     return emit(args, world, seconds, e2e_seconds, h2d, 4, flops, clock_info, launches, impl="ours",
                 extra={"final_loss": losses[-1], "parallelism": label})
 
@@ -293,7 +307,12 @@ def run_reference(args, rank, world, local):
     for module in fsdp_wrap_modules(model, "transformer_block"):
         apply_fsdp(module, torch.bfloat16)
     apply_fsdp(model, torch.bfloat16)
-    optim = RefAdam(model.parameters(), lr=0.0, betas=(0.9, 0.95), weight_decay=0.1, ema=0.9999)
+    if args.optimizer == "muon":
+        from mimir.model.muon import MuonAdamW as RefMuon
+        optim = RefMuon(model.named_parameters(), momentum=0.95, ns_steps=5, muon_lr_scale=1.0, lr=0.0,
+                        betas=(0.9, 0.95), weight_decay=0.1, ema=0.9999)
+    else:
+        optim = RefAdam(model.parameters(), lr=0.0, betas=(0.9, 0.95), weight_decay=0.1, ema=0.9999)
     state = TrainState(model=model, carry=None, optim=optim, step=0, total_steps=10_000, fwd_bwd_dtype=torch.bfloat16,
                        use_cuda_autocast=False)
     hosts = [synthetic_batch(rank, i) for i in range(2)]
@@ -350,7 +369,7 @@ def emit(args, world, seconds, e2e_seconds, h2d_bytes, d2h_bytes, flops_per_step
                    "global_batch": SEQ_LEN * SEQS_PER_GPU * world, "seq_len": SEQ_LEN, "micro_batch": SEQS_PER_GPU,
                    "parallelism": (extra or {}).pop("parallelism", f"fsdp{world}"),
                    "mask": "prefix-LM, prompt length uniform [0,2048]",
-                   "optimizer": "AdamATan2 + EMA", "l2": "inputs larger than L2 (weights+activations >> 126 MB)"},
+                   "optimizer": OPTIMIZER_LABEL[args.optimizer], "l2": "inputs larger than L2 (weights+activations >> 126 MB)"},
         "mfu": round(achieved / 2.25e15, 4),
         "frac_of_measured_bf16": round(achieved / (peaks.get("bf16_tflops_sustained", 1422.4) * 1e12), 4),
         "clocks": clocks,
@@ -373,6 +392,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--optimizer", choices=["adam_atan2", "muon"], default="adam_atan2",
+                    help="adam_atan2: the headline config; muon: the Muon variant of the same model")
     ap.add_argument("--dp", choices=["replicated", "fsdp"], default="replicated",
                     help="data-parallel engine of our arm (the reference arm always uses its FSDP2)")
     args = ap.parse_args()

@@ -56,7 +56,7 @@ int64_t dp_chunk_elements();
 void dp_step(std::vector<int64_t> peer_grads, std::vector<int64_t> peer_weights, at::Tensor segs, int64_t nblocks,
              at::Tensor master, c10::optional<at::Tensor> exp_avg, at::Tensor exp_avg_sq, c10::optional<at::Tensor> ema,
              c10::optional<at::Tensor> reduced, c10::optional<at::Tensor> grad_scale, double b1, double b2,
-             double ema_decay);
+             double ema_decay, std::vector<int64_t> peer_work);
 void dp_reduce(std::vector<int64_t> peer_grads, at::Tensor segs, int64_t nblocks, at::Tensor reduced_out,
                at::Tensor sumsq_out);
 std::vector<at::Tensor> ipc_alloc(int64_t nbytes, int64_t device);

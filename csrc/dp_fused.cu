@@ -19,6 +19,18 @@
 // A reduce-only variant writes the fp32 reduced gradient shard and per-CTA sums of squares for
 // global-norm clipping; the update variant can then read that shard instead of the peers.
 //
+// Segment kinds (one per parameter shard; the whole chunk takes one branch):
+//   kAdamATan2   the update above.
+//   kAdamEps     MuonAdamW's Adam for non-matrix parameters:
+//                m = lerp(m, g, 1-b1);  v = lerp(v, g^2, 1-b2)
+//                w = w (1 - lr wd) - lr * (m / bc1) / (sqrt(v / bc2) + 1e-8)
+//   kMuonGather  Muon momentum on the fp32 shard, Nesterov input to the matrix's owner rank:
+//                mom = lerp(mom, g, 1-beta);  u = lerp(g, mom, beta)
+//                work_owner[dst + i] = u      (fp32 peer store; beta is carried in `bc1`)
+//   kMuonApply   after the owner orthogonalised the gathered matrix in place:
+//                O = work_owner[dst + i]      (fp32 peer load)
+//                w = w (1 - lr wd) - lr O;  EMA;  bf16(w) to every rank
+//
 // The caller orders the step with the other ranks (a collective before: every rank's backward
 // is complete; and after: every rank's stores have landed).  Nothing here waits on a peer.
 #include <ATen/cuda/CUDAContext.h>
@@ -36,19 +48,25 @@ constexpr int kIters = 4;
 constexpr int kChunk = kThreads * kVec * kIters;     // 8192 elements per CTA
 constexpr int kMaxRanks = 8;
 
+enum SegmentKind : int32_t { kAdamATan2 = 0, kAdamEps = 1, kMuonGather = 2, kMuonApply = 3 };
+
 struct Segment {
   int64_t flat;         // element offset in the flat bf16 weight/grad buffers
   int64_t shard;        // element offset in the fp32 shard buffers
   int64_t n;            // elements
   int64_t block_start;  // first chunk index
-  float lr, wd, bc1, bc2_sqrt;
-  int32_t vec;          // flat % 8 == 0, shard % 8 == 0, n % 8 == 0
-  int32_t pad;
+  float lr, wd, bc1, bc2_sqrt;  // kAdamEps: bc2_sqrt holds bc2 itself; kMuonGather: bc1 holds beta
+  int32_t vec;          // flat % 8 == 0, shard % 8 == 0, n % 8 == 0 (and dst % 8 == 0 for Muon)
+  int32_t kind;         // SegmentKind
+  int64_t dst;          // Muon: element offset of this shard in the owner's fp32 workspace
+  int32_t dst_rank;     // Muon: owner rank of the matrix
+  int32_t has_m;        // kAdamEps: the parameter keeps a first moment (beta1 > 0)
 };
 
 struct Peers {
   uint64_t grad[kMaxRanks];
   uint64_t weight[kMaxRanks];
+  uint64_t work[kMaxRanks];  // fp32 Muon workspaces (0 when unused)
 };
 
 struct StepArgs {
@@ -107,19 +125,53 @@ __device__ __forceinline__ float reduce1(const Peers& peers, int world, int64_t 
   return g;
 }
 
+// torch.lerp's two-sided form (the same rounding as the per-parameter optimizers' lerp_).
+__device__ __forceinline__ float lerpf(float a, float b, float t) {
+  return fabsf(t) < 0.5f ? a + t * (b - a) : b - (b - a) * (1.f - t);
+}
+
 __device__ __forceinline__ float adam1(float g, float& w, float* m, float& v, float* e, const Segment& s,
                                        const StepArgs& a) {
-  if (s.wd != 0.f) w = w * (1.f - s.lr * s.wd);
-  v = a.b2 * v + (1.f - a.b2) * g * g;
-  const float denom = sqrtf(v) / s.bc2_sqrt;
-  if (m != nullptr) {
-    *m = *m + (1.f - a.b1) * (g - *m);
-    w = w - (s.lr / s.bc1) * atan2f(*m, denom);
+  if (s.kind == kAdamEps) {
+    w = w * (1.f - s.lr * s.wd);
+    v = lerpf(v, g * g, 1.f - a.b2);
+    float num = g;
+    if (m != nullptr && s.has_m) {
+      *m = lerpf(*m, g, 1.f - a.b1);
+      num = *m / s.bc1;
+    }
+    w = w - s.lr * (num / (sqrtf(v / s.bc2_sqrt) + 1e-8f));
   } else {
-    w = w - s.lr * atan2f(g, denom);
+    if (s.wd != 0.f) w = w * (1.f - s.lr * s.wd);
+    v = a.b2 * v + (1.f - a.b2) * g * g;
+    const float denom = sqrtf(v) / s.bc2_sqrt;
+    if (m != nullptr) {
+      *m = *m + (1.f - a.b1) * (g - *m);
+      w = w - (s.lr / s.bc1) * atan2f(*m, denom);
+    } else {
+      w = w - s.lr * atan2f(g, denom);
+    }
   }
   if (e != nullptr) *e = *e + (1.f - a.ema_decay) * (w - *e);
   return w;
+}
+
+// Muon: momentum on the fp32 shard (kept in the first-moment buffer) and the Nesterov input.
+__device__ __forceinline__ float muon_gather1(float g, float* mom, float beta) {
+  *mom = lerpf(*mom, g, 1.f - beta);
+  return lerpf(g, *mom, beta);
+}
+
+// Muon: decoupled decay and the orthogonalised update, then the EMA.
+__device__ __forceinline__ float muon_apply1(float o, float w, float* e, const Segment& s, const StepArgs& a) {
+  w = w * (1.f - s.lr * s.wd);
+  w = w - s.lr * o;
+  if (e != nullptr) *e = *e + (1.f - a.ema_decay) * (w - *e);
+  return w;
+}
+
+__device__ __forceinline__ float* work_ptr(const Peers& peers, const Segment& s) {
+  return reinterpret_cast<float*>(peers.work[s.dst_rank]) + s.dst;
 }
 
 // Load the 8-element gradient group at flat offset `flat` of every rank (raw bf16 words).
@@ -170,13 +222,15 @@ __global__ void __launch_bounds__(kThreads, 2) dp_update_kernel(const __grid_con
     const Segment s = a.segs[find_segment(a.segs, a.nsegs, chunk)];
     const int64_t start = (chunk - s.block_start) * kChunk;
     const int64_t end = min(start + int64_t(kChunk), s.n);
+    const bool needs_grad = s.kind != kMuonApply;
     if (s.vec) {
       int64_t i = start + int64_t(threadIdx.x) * kVec;
       uint4 raw[kMaxRanks];
-      if (kFromPeers && i < end) load_grads(peers, a.world, s.flat + i, raw);
+      if (kFromPeers && needs_grad && i < end) load_grads(peers, a.world, s.flat + i, raw);
       for (; i < end; i += int64_t(kThreads) * kVec) {
         float g[8];
-        if (kFromPeers) {
+        if (!needs_grad) {
+        } else if (kFromPeers) {
           sum_grads(raw, a.world, g);
           const int64_t nxt = i + int64_t(kThreads) * kVec;
           if (nxt < end) load_grads(peers, a.world, s.flat + nxt, raw);
@@ -184,7 +238,27 @@ __global__ void __launch_bounds__(kThreads, 2) dp_update_kernel(const __grid_con
           ld8(a.reduced + s.shard + i, g);
         }
         float w[8];
-        update8(g, scale, s.shard + i, s, a, w);
+        if (s.kind == kMuonGather) {
+          float m[8];
+          ld8(a.exp_avg + s.shard + i, m);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) g[k] = muon_gather1(g[k] * scale, &m[k], s.bc1);
+          st8(a.exp_avg + s.shard + i, m);
+          st8(work_ptr(peers, s) + i, g);
+          continue;
+        }
+        if (s.kind == kMuonApply) {
+          float o[8], e[8];
+          ld8(work_ptr(peers, s) + i, o);
+          ld8(a.master + s.shard + i, w);
+          if (a.ema != nullptr) ld8(a.ema + s.shard + i, e);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) w[k] = muon_apply1(o[k], w[k], a.ema != nullptr ? &e[k] : nullptr, s, a);
+          st8(a.master + s.shard + i, w);
+          if (a.ema != nullptr) st8(a.ema + s.shard + i, e);
+        } else {
+          update8(g, scale, s.shard + i, s, a, w);
+        }
         const uint4 packed = pack8(w);
 #pragma unroll
         for (int k = 0; k < kMaxRanks; ++k)
@@ -194,12 +268,21 @@ __global__ void __launch_bounds__(kThreads, 2) dp_update_kernel(const __grid_con
     } else {
       for (int64_t i = start + threadIdx.x; i < end; i += kThreads) {
         const int64_t sh = s.shard + i;
-        const float g = (kFromPeers ? reduce1(peers, a.world, s.flat + i) : a.reduced[sh]) * scale;
-        float w = a.master[sh], v = a.exp_avg_sq[sh];
-        w = adam1(g, w, a.exp_avg != nullptr ? a.exp_avg + sh : nullptr, v, a.ema != nullptr ? a.ema + sh : nullptr,
-                  s, a);
+        float* e = a.ema != nullptr ? a.ema + sh : nullptr;
+        float w = a.master[sh];
+        if (s.kind == kMuonApply) {
+          w = muon_apply1(work_ptr(peers, s)[i], w, e, s, a);
+        } else {
+          const float g = (kFromPeers ? reduce1(peers, a.world, s.flat + i) : a.reduced[sh]) * scale;
+          if (s.kind == kMuonGather) {
+            work_ptr(peers, s)[i] = muon_gather1(g, a.exp_avg + sh, s.bc1);
+            continue;
+          }
+          float v = a.exp_avg_sq[sh];
+          w = adam1(g, w, a.exp_avg != nullptr ? a.exp_avg + sh : nullptr, v, e, s, a);
+          a.exp_avg_sq[sh] = v;
+        }
         a.master[sh] = w;
-        a.exp_avg_sq[sh] = v;
         const __nv_bfloat16 b = __float2bfloat16(w);
         for (int k = 0; k < a.world; ++k) reinterpret_cast<__nv_bfloat16*>(peers.weight[k])[s.flat + i] = b;
       }
@@ -256,14 +339,20 @@ unsigned persistent_grid(int64_t nchunks, int device) {
   return static_cast<unsigned>(std::min<int64_t>(nchunks, int64_t(sms) * 2));
 }
 
-Peers make_peers(const std::vector<int64_t>& grads, const std::vector<int64_t>& weights) {
+Peers make_peers(const std::vector<int64_t>& grads, const std::vector<int64_t>& weights,
+                 const std::vector<int64_t>& work = {}) {
   TORCH_CHECK(grads.size() == weights.size() && grads.size() >= 1 && grads.size() <= kMaxRanks,
               "dp step supports 1..", kMaxRanks, " ranks");
+  TORCH_CHECK(work.empty() || work.size() == grads.size(), "one Muon workspace per rank");
   Peers p{};
   for (size_t k = 0; k < grads.size(); ++k) {
     TORCH_CHECK(grads[k] % 16 == 0 && weights[k] % 16 == 0, "peer buffers must be 16-byte aligned");
     p.grad[k] = static_cast<uint64_t>(grads[k]);
     p.weight[k] = static_cast<uint64_t>(weights[k]);
+    if (!work.empty()) {
+      TORCH_CHECK(work[k] % 32 == 0, "Muon workspaces must be 32-byte aligned");
+      p.work[k] = static_cast<uint64_t>(work[k]);
+    }
   }
   return p;
 }
@@ -299,9 +388,9 @@ int64_t dp_chunk_elements() { return kChunk; }
 void dp_step(std::vector<int64_t> peer_grads, std::vector<int64_t> peer_weights, at::Tensor segs, int64_t nblocks,
              at::Tensor master, c10::optional<at::Tensor> exp_avg, at::Tensor exp_avg_sq, c10::optional<at::Tensor> ema,
              c10::optional<at::Tensor> reduced, c10::optional<at::Tensor> grad_scale, double b1, double b2,
-             double ema_decay) {
+             double ema_decay, std::vector<int64_t> peer_work) {
   const c10::cuda::CUDAGuard guard(master.device());
-  const Peers peers = make_peers(peer_grads, peer_weights);
+  const Peers peers = make_peers(peer_grads, peer_weights, peer_work);
   StepArgs a = make_args(segs, peer_grads.size(), master, exp_avg, exp_avg_sq, ema, grad_scale, b1, b2, ema_decay);
   if (nblocks == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();

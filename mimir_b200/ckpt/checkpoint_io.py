@@ -344,8 +344,8 @@ def _load_unsharded_replicated(engine, train_state: TrainState, path: str) -> No
         saved = ckpt["optim"]["state"].get(s.fqn)
         if saved is None or not s.trainable:
             continue
-        for slot, buf in (("exp_avg", optim.exp_avg), ("exp_avg_sq", optim.exp_avg_sq), ("param_ema", optim.ema)):
-            if buf is not None and slot in saved:
+        for slot, buf in optim.slot_buffers(s).items():
+            if slot in saved:
                 buf[sl] = saved[slot].reshape(s.rows, -1)[rows].reshape(-1).to(buf)
     optim.load_dcp_state(ckpt["optim"])
     engine.gather_weights()

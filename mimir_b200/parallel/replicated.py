@@ -142,31 +142,41 @@ class ReplicatedEngine:
                 s.param.grad = self.grads[s.flat:s.flat + s.numel].view(s.shape)
 
     def _open_peers(self, whandle: Tensor, ghandle: Tensor) -> None:
+        self._opened = []
+        self.peer_weights, self.peer_grads = self._share([whandle, ghandle], [self.weights, self.grads])
+
+    def _share(self, handles: list, locals_: list) -> list:
+        """Exchange CUDA IPC handles with every rank; per handle, the list of every rank's pointer."""
         from mimir_b200.ops._ext import ext
         C = ext()
-        mine = (bytes(whandle.numpy().tobytes()), bytes(ghandle.numpy().tobytes()))
-        everyone = [None] * self.world
+        mine = tuple(bytes(h.numpy().tobytes()) for h in handles)
+        everyone = [mine]
+        devices = [self.device.index]
         if self.world > 1:
+            everyone, devices = [None] * self.world, [None] * self.world
             dist.all_gather_object(everyone, mine, group=self.group)
-        else:
-            everyone = [mine]
-        devices = [self.device.index] * self.world
-        if self.world > 1:
             dist.all_gather_object(devices, self.device.index, group=self.group)
-        self._opened = []
-        self.peer_weights, self.peer_grads = [], []
-        for k, (wh, gh) in enumerate(everyone):
-            if k == self.rank:
-                self.peer_weights.append(self.weights.data_ptr())
-                self.peer_grads.append(self.grads.data_ptr())
-                continue
-            if not C.peer_access_possible(self.device.index, devices[k]):
+        out = [[] for _ in handles]
+        for k, theirs in enumerate(everyone):
+            if k != self.rank and not C.peer_access_possible(self.device.index, devices[k]):
                 raise RuntimeError(f"GPU {self.device.index} cannot access peer rank {k} over NVLink/PCIe")
-            wp = C.ipc_open(torch.frombuffer(bytearray(wh), dtype=torch.uint8), self.device.index)
-            gp = C.ipc_open(torch.frombuffer(bytearray(gh), dtype=torch.uint8), self.device.index)
-            self._opened += [wp, gp]
-            self.peer_weights.append(wp)
-            self.peer_grads.append(gp)
+            for j, h in enumerate(theirs):
+                if k == self.rank:
+                    out[j].append(locals_[j].data_ptr())
+                    continue
+                ptr = C.ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8), self.device.index)
+                self._opened.append(ptr)
+                out[j].append(ptr)
+        return out
+
+    def shared_buffer(self, nbytes: int) -> tuple[Tensor, list]:
+        """A zeroed device buffer every rank can address: (this rank's uint8 tensor, all ranks' pointers)."""
+        if not self.cuda:
+            return torch.zeros(nbytes, dtype=torch.uint8), []
+        from mimir_b200.ops._ext import ext
+        buf, handle = ext().ipc_alloc(max(nbytes, 32), self.device.index)
+        self._keep = self._keep + (buf,)
+        return buf, self._share([handle], [buf])[0]
 
     def close(self) -> None:
         if self.cuda and getattr(self, "_opened", None):
@@ -186,9 +196,12 @@ class ReplicatedEngine:
         flag = torch.zeros(1, device=self.device)
         dist.all_reduce(flag, group=self.group)
 
-    def segments(self, lrs: dict, wds: dict, bc1: dict, bc2_sqrt: dict) -> tuple[Tensor, int]:
+    def segments(self, lrs: dict, wds: dict, bc1: dict, bc2_sqrt: dict, extra: Optional[dict] = None
+                 ) -> tuple[Tensor, int]:
         """Packed device segment table: one entry per owned, non-empty shard of every parameter
-        named in ``lrs`` (per-parameter learning rate, weight decay and bias corrections)."""
+        named in ``lrs`` (per-parameter learning rate, weight decay and bias corrections).
+        ``extra`` maps a name to ``(kind, dst, dst_rank, has_m)`` for the non-AdamATan2 kinds
+        (1 Adam with eps, 2 Muon gather to the owner's workspace offset ``dst``, 3 Muon apply)."""
         from mimir_b200.ops._ext import ext
         C = ext()
         chunk = C.dp_chunk_elements()
@@ -197,11 +210,14 @@ class ReplicatedEngine:
             if s.fqn not in lrs or s.shard_numel == 0:
                 continue
             n = s.shard_numel
-            vec = int(s.shard_flat % 8 == 0 and s.shard % 8 == 0 and n % 8 == 0)
-            rows.append((s.shard_flat, s.shard, n, block, lrs[s.fqn], wds[s.fqn], bc1[s.fqn], bc2_sqrt[s.fqn], vec, 0))
+            kind, dst, dst_rank, has_m = (extra or {}).get(s.fqn, (0, 0, 0, 1))
+            vec = int(s.shard_flat % 8 == 0 and s.shard % 8 == 0 and n % 8 == 0 and dst % 8 == 0)
+            rows.append((s.shard_flat, s.shard, n, block, lrs[s.fqn], wds[s.fqn], bc1[s.fqn], bc2_sqrt[s.fqn], vec,
+                         kind, dst, dst_rank, has_m))
             block += (n + chunk - 1) // chunk
         dt = np.dtype([("flat", "<i8"), ("shard", "<i8"), ("n", "<i8"), ("block", "<i8"), ("lr", "<f4"),
-                       ("wd", "<f4"), ("bc1", "<f4"), ("bc2", "<f4"), ("vec", "<i4"), ("pad", "<i4")])
+                       ("wd", "<f4"), ("bc1", "<f4"), ("bc2", "<f4"), ("vec", "<i4"), ("kind", "<i4"),
+                       ("dst", "<i8"), ("dst_rank", "<i4"), ("has_m", "<i4")])
         assert dt.itemsize == C.dp_segment_bytes()
         table = np.array(rows, dtype=dt)
         host = torch.from_numpy(table.view(np.uint8).copy())
@@ -319,7 +335,7 @@ class ReplicatedAdamATan2(Optimizer):
             if eng.reduced is None:
                 eng.barrier()  # every rank's backward has finished writing its gradients
             ext().dp_step(eng.peer_grads, eng.peer_weights, table, blocks, eng.master, self.exp_avg, self.exp_avg_sq,
-                          self.ema, eng.reduced, self.grad_scale, b1, b2, ema if ema is not None else 0.0)
+                          self.ema, eng.reduced, self.grad_scale, b1, b2, ema if ema is not None else 0.0, [])
             eng.barrier()  # every rank's weight stores have landed
         else:
             self._step_cpu(lrs, wds, bc1, bc2_sqrt, b1, b2, ema)
@@ -358,6 +374,12 @@ class ReplicatedAdamATan2(Optimizer):
         eng.gather_weights()
 
     # ------------------------------------------------------------------ checkpoint views
+    def slot_buffers(self, s: ParamSlot) -> dict:
+        """Optimizer slot name -> the shard buffer holding it, for parameter slot ``s``."""
+        out = {"exp_avg": self.exp_avg} if self.exp_avg is not None else {}
+        out["exp_avg_sq"] = self.exp_avg_sq
+        return out | ({"param_ema": self.ema} if self.ema is not None else {})
+
     def dcp_state(self) -> dict:
         """``get_optimizer_state_dict``-shaped optimizer state with ``Shard(0)`` DTensor slots."""
         eng = self.engine
@@ -387,6 +409,203 @@ class ReplicatedAdamATan2(Optimizer):
             for key, value in saved.items():
                 if key != "params":
                     group[key] = value
+
+
+class ReplicatedMuonAdamW(ReplicatedAdamATan2):
+    """MuonAdamW over a :class:`ReplicatedEngine`: Muon (Newton-Schulz orthogonalised momentum)
+    for the hidden matrices, Adam (eps 1e-8) for everything else, with the state slots
+    (``momentum_buffer`` / ``exp_avg`` / ``exp_avg_sq`` / ``param_ema``) and group keys of
+    :class:`mimir_b200.optim.muon.MuonAdamW`, so checkpoints interchange with the FSDP2 path.
+
+    Reference behaviour: ``src/mimir/model/muon.py:62-108``, where every rank all-gathers every
+    matrix and runs the same Newton-Schulz chain.  Here each matrix has one owner rank (greedy
+    balance of the Newton-Schulz FLOPs) holding an fp32 workspace that every rank can address,
+    and one step is:
+
+    1. fused kernel, every rank over its ``Shard(0)`` rows: peer-load and sum the bf16 gradients;
+       Adam for the non-matrix parameters (new bf16 weights stored to every rank); for each Muon
+       matrix the momentum update on the fp32 shard, with the Nesterov input stored straight into
+       the owner's workspace (the gather);
+    2. every owner orthogonalises its matrices in place, batched over equal-shape logical pieces,
+       so each matrix is orthogonalised once per job instead of once per rank;
+    3. fused kernel: every rank peer-loads its rows of the orthogonalised matrices from their
+       owners, applies decoupled decay, the update and the EMA to its fp32 master shard and stores
+       the bf16 weights to every rank (the scatter and the all-gather).
+
+    One-element all-reduces order the phases.  Without CUDA the same algorithm runs with
+    PyTorch collectives.
+    """
+
+    def __init__(self, engine: ReplicatedEngine, *, momentum: float = 0.95, ns_steps: int = 5,
+                 muon_lr_scale: float = 1.0, **kwargs):
+        from mimir_b200.optim.muon import matrix_splits
+        if not 0 <= momentum < 1 or ns_steps < 1 or muon_lr_scale <= 0:
+            raise ValueError("Invalid Muon momentum, iterations or LR scale")
+        super().__init__(engine, **kwargs)
+        for group in self.param_groups:
+            group.update(optimizer_kind="muon_adamw", muon_momentum=momentum, muon_ns_steps=ns_steps,
+                         muon_lr_scale=muon_lr_scale)
+        self.has_m = self.exp_avg is not None
+        if self.exp_avg is None:  # the Muon momentum lives in the first-moment buffer
+            self.exp_avg = torch.zeros(engine.shard_total, dtype=torch.float32, device=engine.device)
+        self.splits = {s.fqn: matrix_splits(s.fqn, s.param) for s in engine.slots if s.trainable}
+        self.owner, self.work_offset, sizes = self._assign_owners()
+        self.work_buf, self.peer_work = engine.shared_buffer(4 * max(sizes, default=0))
+        self.work = self.work_buf.view(torch.float32)
+
+    def _assign_owners(self):
+        def cost(s):
+            rows, cols = s.rows // self.splits[s.fqn], s.numel // s.rows
+            m, n = min(rows, cols), max(rows, cols)
+            return self.splits[s.fqn] * (2 * m * m * n + m ** 3)
+        world = self.engine.world
+        matrices = [s for s in self.engine.slots if self.splits.get(s.fqn)]
+        load, owner, offset, sizes = [0] * world, {}, {}, [0] * world
+        for s in sorted(matrices, key=cost, reverse=True):  # stable: ties keep model order
+            k = min(range(world), key=lambda r: (load[r], r))
+            load[k] += cost(s)
+            owner[s.fqn], offset[s.fqn] = k, sizes[k]
+            sizes[k] += _align(s.numel)
+        return owner, offset, sizes
+
+    def slot_buffers(self, s: ParamSlot) -> dict:
+        if self.splits.get(s.fqn):
+            out = {"momentum_buffer": self.exp_avg}
+        else:
+            out = ({"exp_avg": self.exp_avg} if self.has_m else {}) | {"exp_avg_sq": self.exp_avg_sq}
+        return out | ({"param_ema": self.ema} if self.ema is not None else {})
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        if closure is not None:
+            raise ValueError("Closures are not supported")
+        if getattr(self, "shared_parameter_updates", None):
+            raise ValueError("Shared gate-donor updates are not supported by the replicated engine")
+        eng = self.engine
+        (group,) = self.param_groups
+        b1, b2 = group["betas"]
+        beta, wd = float(group["muon_momentum"]), float(group["weight_decay"])
+        first = {"lr": {}, "wd": {}, "bc1": {}, "bc2": {}, "extra": {}}
+        second = {"lr": {}, "wd": {}, "bc1": {}, "bc2": {}, "extra": {}}
+        owned = []
+        for s in eng.slots:
+            if not s.trainable or s.fqn not in eng.touched:
+                continue
+            st = self.state[s.param]
+            st["step"] += 1
+            lr = self._lr(group, s.param)
+            if self.splits.get(s.fqn):
+                dst = self.work_offset[s.fqn] + s.row0 * (s.numel // s.rows)
+                k = self.owner[s.fqn]
+                for table, entry in ((first, (0.0, 0.0, beta, 1.0, (2, dst, k, 0))),
+                                     (second, (lr * group["muon_lr_scale"], wd, 1.0, 1.0, (3, dst, k, 0)))):
+                    for key, value in zip(("lr", "wd", "bc1", "bc2", "extra"), entry):
+                        table[key][s.fqn] = value
+                if k == eng.rank:
+                    owned.append(s)
+            else:
+                first["lr"][s.fqn], first["wd"][s.fqn] = lr, wd
+                first["bc1"][s.fqn] = float(1 - b1 ** st["step"]) if self.has_m else 1.0
+                first["bc2"][s.fqn] = float(1 - b2 ** st["step"])
+                first["extra"][s.fqn] = (1, 0, 0, int(self.has_m))
+        ema = group["ema"]
+        if not eng.cuda:
+            self._step_cpu_muon(first, second, owned, group)
+        else:
+            from mimir_b200.ops._ext import ext
+            C = ext()
+            ema_decay = ema if ema is not None else 0.0
+            if eng.reduced is None:
+                eng.barrier()  # every rank's backward has finished writing its gradients
+            table, blocks = eng.segments(first["lr"], first["wd"], first["bc1"], first["bc2"], first["extra"])
+            C.dp_step(eng.peer_grads, eng.peer_weights, table, blocks, eng.master, self.exp_avg, self.exp_avg_sq,
+                      self.ema, eng.reduced, self.grad_scale, b1, b2, ema_decay, self.peer_work)
+            eng.barrier()  # every shard of every matrix has reached its owner
+            self._orthogonalise(owned, group["muon_ns_steps"])
+            eng.barrier()  # every owner has finished
+            table, blocks = eng.segments(second["lr"], second["wd"], second["bc1"], second["bc2"], second["extra"])
+            C.dp_step(eng.peer_grads, eng.peer_weights, table, blocks, eng.master, self.exp_avg, self.exp_avg_sq,
+                      self.ema, None, None, b1, b2, ema_decay, self.peer_work)
+            eng.barrier()  # every rank's weight stores have landed
+        eng.reduced = None
+        self.grad_scale = None
+
+    def _matrix(self, s: ParamSlot) -> Tensor:
+        off = self.work_offset[s.fqn]
+        return self.work[off:off + s.numel].view(s.rows, -1)
+
+    def _orthogonalise(self, owned: list, steps: int) -> None:
+        """Newton-Schulz in place on this rank's matrices, batched over equal-shape logical pieces."""
+        from mimir_b200.optim.muon import orthogonalize
+        by_shape: dict = {}
+        for s in owned:
+            for piece in self._matrix(s).chunk(self.splits[s.fqn], dim=0):
+                by_shape.setdefault(tuple(piece.shape), []).append(piece)
+        for (rows, cols), pieces in by_shape.items():
+            out = orthogonalize(torch.stack(pieces), steps) * math.sqrt(max(1, rows / cols))
+            for piece, o in zip(pieces, out):
+                piece.copy_(o)
+
+    def _step_cpu_muon(self, first: dict, second: dict, owned: list, group) -> None:
+        eng = self.engine
+        b1, b2 = group["betas"]
+        ema = group["ema"]
+        if eng.reduced is None:
+            full = eng.grads.to(torch.float32)
+            if eng.world > 1:
+                dist.all_reduce(full, group=eng.group)
+        for s in eng.slots:
+            if s.fqn not in first["lr"]:
+                continue
+            sl = slice(s.shard, s.shard + s.shard_numel)
+            g = (eng.reduced[sl] if eng.reduced is not None else full[s.shard_flat:s.shard_flat + s.shard_numel]).clone()
+            if self.grad_scale is not None:
+                g = g * self.grad_scale
+            w = eng.master[sl]
+            if self.splits.get(s.fqn):
+                mom = self.exp_avg[sl]
+                mom.lerp_(g, 1 - group["muon_momentum"])
+                matrix = torch.zeros(s.rows, s.numel // s.rows)
+                matrix[s.row0:s.row0 + s.rows_mine] = g.lerp(mom, group["muon_momentum"]).view(s.local_shape())
+                if eng.world > 1:
+                    dist.all_reduce(matrix, group=eng.group)  # disjoint rows: the gather
+                if self.owner[s.fqn] == eng.rank:  # the workspace holds only the owner's matrices
+                    self._matrix(s).copy_(matrix)
+                continue
+            lr, wd = first["lr"][s.fqn], first["wd"][s.fqn]
+            if self.has_m:
+                self.exp_avg[sl].lerp_(g, 1 - b1)
+                num = self.exp_avg[sl] / first["bc1"][s.fqn]
+            else:
+                num = g
+            self.exp_avg_sq[sl].lerp_(g.square(), 1 - b2)
+            upd = num / ((self.exp_avg_sq[sl] / first["bc2"][s.fqn]).sqrt() + 1e-8)
+            w.mul_(1 - lr * wd).add_(upd, alpha=-lr)
+            if self.ema is not None:
+                self.ema[sl].lerp_(w, 1 - ema)
+        self._orthogonalise(owned, group["muon_ns_steps"])
+        for s in eng.slots:
+            if s.fqn not in second["lr"]:
+                continue
+            mine = self.owner[s.fqn] == eng.rank
+            matrix = self._matrix(s).clone() if mine else torch.empty(s.rows, s.numel // s.rows)
+            if eng.world > 1:
+                dist.broadcast(matrix, src=dist.get_global_rank(eng.group, self.owner[s.fqn]) if eng.group
+                               else self.owner[s.fqn], group=eng.group)
+            sl = slice(s.shard, s.shard + s.shard_numel)
+            lr, w = second["lr"][s.fqn], eng.master[sl]
+            w.mul_(1 - lr * second["wd"][s.fqn]).add_(matrix[s.row0:s.row0 + s.rows_mine].reshape(-1), alpha=-lr)
+            if self.ema is not None:
+                self.ema[sl].lerp_(w, 1 - ema)
+        eng.gather_weights()
+
+    def dcp_state(self) -> dict:
+        out = super().dcp_state()
+        for s in self.engine.slots:
+            if s.trainable:
+                out["state"][s.fqn] = {"step": self.state[s.param]["step"]} | {
+                    name: self.engine.shard_dtensor(s, buf) for name, buf in self.slot_buffers(s).items()}
+        return out
 
 
 def model_dcp_state(engine: ReplicatedEngine) -> dict:

@@ -77,15 +77,20 @@ def create_model_and_optimizer(config, metadata: dict, device: torch.device, loc
 
 def _replicated_model_and_optimizer(config, model, carry, device, fwd_bwd_dtype):
     """Replicated bf16 weights + sharded fp32 master/optimizer, fused peer-memory step."""
-    from mimir_b200.parallel.replicated import ReplicatedAdamATan2, wrap_replicated
-    if config.optimizer != "adam_atan2":
-        raise ValueError("distributed_strategy=replicated supports the AdamATan2 optimizer")
+    from mimir_b200.parallel.replicated import ReplicatedAdamATan2, ReplicatedMuonAdamW, wrap_replicated
+    if config.optimizer not in ("adam_atan2", "muon"):
+        raise ValueError(f"distributed_strategy=replicated does not implement optimizer={config.optimizer}")
     if config.arch.gates_enabled:
         raise ValueError("distributed_strategy=replicated does not implement shared gate-donor updates")
     scales = module_lr_scales(model, config.lr, configured_module_rates(config))
     engine = wrap_replicated(model, device, fwd_bwd_dtype)
-    optim = ReplicatedAdamATan2(engine, lr=0.0, betas=(config.beta1, config.beta2), weight_decay=config.weight_decay,
-                                ema=config.ema, ema_dtype=torch.float32, parameter_lr_scales=scales)
+    common = dict(lr=0.0, betas=(config.beta1, config.beta2), weight_decay=config.weight_decay, ema=config.ema,
+                  ema_dtype=torch.float32, parameter_lr_scales=scales)
+    if config.optimizer == "muon":
+        optim = ReplicatedMuonAdamW(engine, momentum=config.muon_momentum, ns_steps=config.muon_ns_steps,
+                                    muon_lr_scale=config.muon_lr_scale, **common)
+    else:
+        optim = ReplicatedAdamATan2(engine, **common)
     return model, carry, optim
 
 

@@ -127,3 +127,102 @@ def test_multi_gpu_fused_step_matches_summed_reference(tmp_path):
             state[n] = _reference_update(w, g, m, v, e, 1e-2, 0.1, 0.9, 0.95, step + 1, 0.9)
     for n, (w, *_rest) in state.items():
         torch.testing.assert_close(weights[0][n], w.to(torch.bfloat16).float(), rtol=1e-2, atol=1e-3)
+
+
+# ------------------------------------------------------------------ MuonAdamW on the fused engine
+def _muon_net(device):
+    from test_replicated_muon import _Net
+    torch.manual_seed(0)
+    return _Net().to(device)
+
+
+MUON_HP = dict(lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, ema=0.9, momentum=0.95, ns_steps=5, muon_lr_scale=0.5)
+
+
+def _muon_reference(model, grads_per_step):
+    """Per-parameter MuonAdamW in fp32 fed with the given (summed) gradients."""
+    from mimir_b200.optim.muon import MuonAdamW
+    opt = MuonAdamW(model.named_parameters(), **MUON_HP)
+    for grads in grads_per_step:
+        for n, p in model.named_parameters():
+            p.grad = grads[n].to(p.device)
+        opt.step()
+    return {n: p.detach().float().cpu() for n, p in model.named_parameters()}
+
+
+def _muon_tokens(gen, dev):
+    return torch.randint(0, 11, (6, 5), device=dev, generator=gen)
+
+
+def test_single_gpu_muon_step_matches_fp32_reference():
+    from mimir_b200.parallel.replicated import ReplicatedMuonAdamW, wrap_replicated
+    dev = torch.device("cuda", 0)
+    model = _muon_net(dev)
+    shadow = _muon_net(dev)
+    engine = wrap_replicated(model, dev, torch.bfloat16)
+    opt = ReplicatedMuonAdamW(engine, **MUON_HP)
+    gen = torch.Generator(device=dev).manual_seed(3)
+    history = []
+    for _ in range(3):
+        opt.zero_grad()
+        model(_muon_tokens(gen, dev)).float().square().mean().backward()
+        history.append({n: p.grad.float().clone() for n, p in model.named_parameters()})
+        opt.step()
+    torch.cuda.synchronize()
+    want = _muon_reference(shadow, history)
+    for s in engine.slots:
+        got = engine.master[s.shard:s.shard + s.shard_numel].view(s.shape).cpu()
+        torch.testing.assert_close(got, want[s.fqn], rtol=1e-4, atol=1e-5, msg=lambda m, n=s.fqn: f"{n}: {m}")
+        assert torch.equal(s.param.detach().cpu(), got.to(torch.bfloat16))
+
+
+def _muon_rank(rank, world, port, out):
+    import sys
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.dirname(__file__))
+    from mimir_b200.parallel.replicated import ReplicatedMuonAdamW, wrap_replicated
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        model = _muon_net(dev)
+        engine = wrap_replicated(model, dev, torch.bfloat16)
+        opt = ReplicatedMuonAdamW(engine, **MUON_HP)
+        for step in range(3):
+            opt.zero_grad()
+            gen = torch.Generator(device=dev).manual_seed(100 * step + rank)
+            model(_muon_tokens(gen, dev)).float().square().mean().backward()
+            torch.save({n: p.grad.detach().float().cpu() for n, p in model.named_parameters()},
+                       f"{out}.grad.{step}.{rank}.pt")
+            opt.step()
+        torch.cuda.synchronize()
+        torch.save({n: p.detach().float().cpu() for n, p in model.named_parameters()}, f"{out}.w.{rank}.pt")
+        torch.save({s.fqn: engine.master[s.shard:s.shard + s.shard_numel].cpu() for s in engine.slots},
+                   f"{out}.m.{rank}.pt")
+        engine.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_multi_gpu_muon_step_matches_summed_reference(tmp_path):
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 8)
+    mp.spawn(_muon_rank, args=(world, _free_port(), str(tmp_path / "r")), nprocs=world, join=True)
+    weights = [torch.load(tmp_path / f"r.w.{r}.pt") for r in range(world)]
+    for r in range(1, world):
+        for n in weights[0]:
+            assert torch.equal(weights[0][n], weights[r][n]), (r, n)
+    history = []
+    for step in range(3):
+        grads = [torch.load(tmp_path / f"r.grad.{step}.{r}.pt") for r in range(world)]
+        history.append({n: sum(gr[n] for gr in grads) for n in grads[0]})
+    want = _muon_reference(_muon_net("cpu"), history)
+    masters = [torch.load(tmp_path / f"r.m.{r}.pt") for r in range(world)]
+    for n, w in want.items():
+        rows = w.shape[0] if w.dim() else 1
+        chunk = -(-rows // world)
+        for r in range(world):
+            piece = w.reshape(rows, -1)[r * chunk:(r + 1) * chunk].reshape(-1)
+            torch.testing.assert_close(masters[r][n], piece, rtol=1e-4, atol=1e-5, msg=lambda m, n=n: f"{n}: {m}")
