@@ -56,13 +56,18 @@ int64_t dp_chunk_elements();
 void dp_step(std::vector<int64_t> peer_grads, std::vector<int64_t> peer_weights, at::Tensor segs, int64_t nblocks,
              at::Tensor master, c10::optional<at::Tensor> exp_avg, at::Tensor exp_avg_sq, c10::optional<at::Tensor> ema,
              c10::optional<at::Tensor> reduced, c10::optional<at::Tensor> grad_scale, double b1, double b2,
-             double ema_decay, std::vector<int64_t> peer_work);
+             double ema_decay, std::vector<int64_t> peer_work, int64_t rank);
 void dp_reduce(std::vector<int64_t> peer_grads, at::Tensor segs, int64_t nblocks, at::Tensor reduced_out,
-               at::Tensor sumsq_out);
+               at::Tensor sumsq_out, int64_t rank);
 std::vector<at::Tensor> ipc_alloc(int64_t nbytes, int64_t device);
 int64_t ipc_open(at::Tensor handle_bytes, int64_t device);
 void ipc_close(int64_t ptr, int64_t device);
 bool peer_access_possible(int64_t device, int64_t peer);
+void moe_dispatch(at::Tensor x, at::Tensor rows, at::Tensor dst, std::vector<int64_t> recv, int64_t k);
+at::Tensor moe_combine(std::vector<int64_t> y, at::Tensor rows, at::Tensor dst, c10::optional<at::Tensor> w,
+                       int64_t T, int64_t k, int64_t d);
+at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::Tensor dst, std::vector<int64_t> y,
+                           std::vector<int64_t> dy, int64_t k);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mimir_b200 hand-written sm_100a kernels";
@@ -95,6 +100,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
   m.def("peer_access_possible", &peer_access_possible);
+  m.def("moe_dispatch", &moe_dispatch);
+  m.def("moe_combine", &moe_combine);
+  m.def("moe_combine_bwd", &moe_combine_bwd);
   m.def("fmha_bwd", &fmha_bwd, py::arg("q_src"), py::arg("q_col"), py::arg("k_src"), py::arg("k_col"),
         py::arg("v_src"), py::arg("v_col"), py::arg("d_o"), py::arg("lse"), py::arg("delta"), py::arg("H"),
         py::arg("KV"), py::arg("is_causal"), py::arg("cu_seqlens"), py::arg("prefix_lens"), py::arg("numseqs"),

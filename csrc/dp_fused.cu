@@ -49,6 +49,7 @@ constexpr int kChunk = kThreads * kVec * kIters;     // 8192 elements per CTA
 constexpr int kMaxRanks = 8;
 
 enum SegmentKind : int32_t { kAdamATan2 = 0, kAdamEps = 1, kMuonGather = 2, kMuonApply = 3 };
+constexpr int32_t kLocalFlag = 256;  // OR-ed into `kind`: a rank-local (expert-parallel) parameter
 
 struct Segment {
   int64_t flat;         // element offset in the flat bf16 weight/grad buffers
@@ -73,6 +74,7 @@ struct StepArgs {
   const Segment* segs;
   int nsegs;
   int world;
+  int rank;
   float* master;
   float* exp_avg;        // nullptr without a first moment
   float* exp_avg_sq;
@@ -119,9 +121,10 @@ __device__ __forceinline__ void st8(float* p, const float (&f)[8]) {
   *reinterpret_cast<float4*>(p + 4) = make_float4(f[4], f[5], f[6], f[7]);
 }
 
-__device__ __forceinline__ float reduce1(const Peers& peers, int world, int64_t flat) {
+__device__ __forceinline__ float reduce1(const Peers& peers, int r0, int world, int64_t flat) {
   float g = 0.f;
-  for (int k = 0; k < world; ++k) g += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(peers.grad[k])[flat]);
+  for (int k = 0; k < world; ++k)
+    g += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(peers.grad[r0 + k])[flat]);
   return g;
 }
 
@@ -132,7 +135,7 @@ __device__ __forceinline__ float lerpf(float a, float b, float t) {
 
 __device__ __forceinline__ float adam1(float g, float& w, float* m, float& v, float* e, const Segment& s,
                                        const StepArgs& a) {
-  if (s.kind == kAdamEps) {
+  if ((s.kind & ~kLocalFlag) == kAdamEps) {
     w = w * (1.f - s.lr * s.wd);
     v = lerpf(v, g * g, 1.f - a.b2);
     float num = g;
@@ -175,10 +178,12 @@ __device__ __forceinline__ float* work_ptr(const Peers& peers, const Segment& s)
 }
 
 // Load the 8-element gradient group at flat offset `flat` of every rank (raw bf16 words).
-__device__ __forceinline__ void load_grads(const Peers& peers, int world, int64_t flat, uint4 (&raw)[kMaxRanks]) {
+__device__ __forceinline__ void load_grads(const Peers& peers, int r0, int world, int64_t flat,
+                                           uint4 (&raw)[kMaxRanks]) {
 #pragma unroll
   for (int k = 0; k < kMaxRanks; ++k)
-    if (k < world) raw[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peers.grad[k]) + flat);
+    if (k < world)
+      raw[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peers.grad[r0 + k]) + flat);
 }
 
 __device__ __forceinline__ void sum_grads(const uint4 (&raw)[kMaxRanks], int world, float (&g)[8]) {
@@ -222,23 +227,27 @@ __global__ void __launch_bounds__(kThreads, 2) dp_update_kernel(const __grid_con
     const Segment s = a.segs[find_segment(a.segs, a.nsegs, chunk)];
     const int64_t start = (chunk - s.block_start) * kChunk;
     const int64_t end = min(start + int64_t(kChunk), s.n);
-    const bool needs_grad = s.kind != kMuonApply;
+    // A rank-local segment (expert-parallel parameter) is reduced over and written to this rank only.
+    const bool local = (s.kind & kLocalFlag) != 0;
+    const int r0 = local ? a.rank : 0, nr = local ? 1 : a.world;
+    const int kind = s.kind & ~kLocalFlag;
+    const bool needs_grad = kind != kMuonApply;
     if (s.vec) {
       int64_t i = start + int64_t(threadIdx.x) * kVec;
       uint4 raw[kMaxRanks];
-      if (kFromPeers && needs_grad && i < end) load_grads(peers, a.world, s.flat + i, raw);
+      if (kFromPeers && needs_grad && i < end) load_grads(peers, r0, nr, s.flat + i, raw);
       for (; i < end; i += int64_t(kThreads) * kVec) {
         float g[8];
         if (!needs_grad) {
         } else if (kFromPeers) {
-          sum_grads(raw, a.world, g);
+          sum_grads(raw, nr, g);
           const int64_t nxt = i + int64_t(kThreads) * kVec;
-          if (nxt < end) load_grads(peers, a.world, s.flat + nxt, raw);
+          if (nxt < end) load_grads(peers, r0, nr, s.flat + nxt, raw);
         } else {
           ld8(a.reduced + s.shard + i, g);
         }
         float w[8];
-        if (s.kind == kMuonGather) {
+        if (kind == kMuonGather) {
           float m[8];
           ld8(a.exp_avg + s.shard + i, m);
 #pragma unroll
@@ -247,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 2) dp_update_kernel(const __grid_con
           st8(work_ptr(peers, s) + i, g);
           continue;
         }
-        if (s.kind == kMuonApply) {
+        if (kind == kMuonApply) {
           float o[8], e[8];
           ld8(work_ptr(peers, s) + i, o);
           ld8(a.master + s.shard + i, w);
@@ -262,19 +271,19 @@ __global__ void __launch_bounds__(kThreads, 2) dp_update_kernel(const __grid_con
         const uint4 packed = pack8(w);
 #pragma unroll
         for (int k = 0; k < kMaxRanks; ++k)
-          if (k < a.world)
-            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers.weight[k]) + s.flat + i) = packed;
+          if (k < nr)
+            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers.weight[r0 + k]) + s.flat + i) = packed;
       }
     } else {
       for (int64_t i = start + threadIdx.x; i < end; i += kThreads) {
         const int64_t sh = s.shard + i;
         float* e = a.ema != nullptr ? a.ema + sh : nullptr;
         float w = a.master[sh];
-        if (s.kind == kMuonApply) {
+        if (kind == kMuonApply) {
           w = muon_apply1(work_ptr(peers, s)[i], w, e, s, a);
         } else {
-          const float g = (kFromPeers ? reduce1(peers, a.world, s.flat + i) : a.reduced[sh]) * scale;
-          if (s.kind == kMuonGather) {
+          const float g = (kFromPeers ? reduce1(peers, r0, nr, s.flat + i) : a.reduced[sh]) * scale;
+          if (kind == kMuonGather) {
             work_ptr(peers, s)[i] = muon_gather1(g, a.exp_avg + sh, s.bc1);
             continue;
           }
@@ -284,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 2) dp_update_kernel(const __grid_con
         }
         a.master[sh] = w;
         const __nv_bfloat16 b = __float2bfloat16(w);
-        for (int k = 0; k < a.world; ++k) reinterpret_cast<__nv_bfloat16*>(peers.weight[k])[s.flat + i] = b;
+        for (int k = 0; k < nr; ++k) reinterpret_cast<__nv_bfloat16*>(peers.weight[r0 + k])[s.flat + i] = b;
       }
     }
   }
@@ -300,20 +309,22 @@ __global__ void __launch_bounds__(kThreads, 2) dp_reduce_kernel(const __grid_con
     const Segment s = a.segs[find_segment(a.segs, a.nsegs, chunk)];
     const int64_t start = (chunk - s.block_start) * kChunk;
     const int64_t end = min(start + int64_t(kChunk), s.n);
+    const bool local = (s.kind & kLocalFlag) != 0;
+    const int r0 = local ? a.rank : 0, nr = local ? 1 : a.world;
     float sq = 0.f;
     if (s.vec) {
       for (int64_t i = start + int64_t(threadIdx.x) * kVec; i < end; i += int64_t(kThreads) * kVec) {
         uint4 raw[kMaxRanks];
         float g[8];
-        load_grads(peers, a.world, s.flat + i, raw);
-        sum_grads(raw, a.world, g);
+        load_grads(peers, r0, nr, s.flat + i, raw);
+        sum_grads(raw, nr, g);
         st8(a.reduced_out + s.shard + i, g);
 #pragma unroll
         for (int k = 0; k < 8; ++k) sq += g[k] * g[k];
       }
     } else {
       for (int64_t i = start + threadIdx.x; i < end; i += kThreads) {
-        const float g = reduce1(peers, a.world, s.flat + i);
+        const float g = reduce1(peers, r0, nr, s.flat + i);
         a.reduced_out[s.shard + i] = g;
         sq += g * g;
       }
@@ -388,10 +399,12 @@ int64_t dp_chunk_elements() { return kChunk; }
 void dp_step(std::vector<int64_t> peer_grads, std::vector<int64_t> peer_weights, at::Tensor segs, int64_t nblocks,
              at::Tensor master, c10::optional<at::Tensor> exp_avg, at::Tensor exp_avg_sq, c10::optional<at::Tensor> ema,
              c10::optional<at::Tensor> reduced, c10::optional<at::Tensor> grad_scale, double b1, double b2,
-             double ema_decay, std::vector<int64_t> peer_work) {
+             double ema_decay, std::vector<int64_t> peer_work, int64_t rank) {
   const c10::cuda::CUDAGuard guard(master.device());
   const Peers peers = make_peers(peer_grads, peer_weights, peer_work);
   StepArgs a = make_args(segs, peer_grads.size(), master, exp_avg, exp_avg_sq, ema, grad_scale, b1, b2, ema_decay);
+  TORCH_CHECK(rank >= 0 && rank < a.world, "bad rank");
+  a.rank = static_cast<int>(rank);
   if (nblocks == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   const unsigned grid = persistent_grid(nblocks, master.device().index());
@@ -405,7 +418,7 @@ void dp_step(std::vector<int64_t> peer_grads, std::vector<int64_t> peer_weights,
 }
 
 void dp_reduce(std::vector<int64_t> peer_grads, at::Tensor segs, int64_t nblocks, at::Tensor reduced_out,
-               at::Tensor sumsq_out) {
+               at::Tensor sumsq_out, int64_t rank) {
   const c10::cuda::CUDAGuard guard(reduced_out.device());
   const Peers peers = make_peers(peer_grads, peer_grads);
   TORCH_CHECK(reduced_out.dtype() == at::kFloat && sumsq_out.dtype() == at::kFloat && sumsq_out.numel() >= nblocks,
@@ -414,6 +427,8 @@ void dp_reduce(std::vector<int64_t> peer_grads, at::Tensor segs, int64_t nblocks
   a.segs = reinterpret_cast<const Segment*>(segs.data_ptr());
   a.nsegs = static_cast<int>(segs.numel() / sizeof(Segment));
   a.world = static_cast<int>(peer_grads.size());
+  TORCH_CHECK(rank >= 0 && rank < a.world, "bad rank");
+  a.rank = static_cast<int>(rank);
   a.reduced_out = reduced_out.data_ptr<float>();
   a.sumsq_out = sumsq_out.data_ptr<float>();
   if (nblocks == 0) return;

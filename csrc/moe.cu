@@ -1,0 +1,231 @@
+// Mixture-of-experts token exchange over NVLink peer memory (expert parallelism), fused with the
+// top-k permutation and the routing-weight combine.
+//
+// Every rank owns E/W experts.  A token-slot (t, j) — token t's j-th routed expert e — has a
+// destination rank dst = e / (E/W) and a row in that rank's receive buffer; rows are grouped by
+// expert, then by source rank, then by token (the host computes them from the all-gathered
+// per-expert counts, so the layout is "capacity free": a buffer holds exactly the routed rows).
+// The receive buffers are CUDA-IPC mappings, so the exchange is plain loads and stores:
+//
+//   dispatch      recv[dst][row(t,j)]  = x[t]                       (one load of x[t], k peer stores)
+//   combine       out[t] = sum_j w[t,j] * y[dst][row(t,j)]          (peer loads, fp32 accumulate)
+//   combine_bwd   dy[dst][row(t,j)] = w[t,j] * dout[t]              (peer stores)
+//                 dw[t,j] = <dout[t], y[dst][row(t,j)]>             (peer loads, fp32)
+//   gather_sum    dx[t] = sum_j dxp[dst][row(t,j)]                  (combine with unit weights)
+//
+// One warp per token walks the hidden dimension in 16-byte vectors.  With W = 1 the same
+// kernels are the local permutation and un-permutation.  Nothing here waits on a peer: the
+// caller orders each exchange with the other ranks by a collective before and after it.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kMaxRanks = 8;
+constexpr int kWarps = 8;
+constexpr int kMaxTopK = 8;
+
+struct PeerRows {
+  uint64_t ptr[kMaxRanks];  // every rank's buffer (bf16 [rows, d])
+};
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 t = __bfloat1622float2(h[k]);
+    f[2 * k] = t.x;
+    f[2 * k + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  return make_uint4(mimir::pack_bf16x2(f[0], f[1]), mimir::pack_bf16x2(f[2], f[3]), mimir::pack_bf16x2(f[4], f[5]),
+                    mimir::pack_bf16x2(f[6], f[7]));
+}
+
+__device__ __forceinline__ const uint4* row_ptr(const PeerRows& p, int rank, int64_t row, int64_t d) {
+  return reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.ptr[rank]) + row * d);
+}
+
+__device__ __forceinline__ uint4* row_ptr_mut(const PeerRows& p, int rank, int64_t row, int64_t d) {
+  return reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.ptr[rank]) + row * d);
+}
+
+__global__ void __launch_bounds__(kWarps * 32) moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                    const int32_t* __restrict__ rows,
+                                                                    const int32_t* __restrict__ dst,
+                                                                    const __grid_constant__ PeerRows recv, int64_t T,
+                                                                    int k, int64_t d) {
+  const int64_t t = int64_t(blockIdx.x) * kWarps + threadIdx.x / 32;
+  if (t >= T) return;
+  const int lane = threadIdx.x & 31;
+  int r[kMaxTopK], q[kMaxTopK];
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j)
+    if (j < k) r[j] = rows[t * k + j], q[j] = dst[t * k + j];
+  const uint4* src = reinterpret_cast<const uint4*>(x + t * d);
+  for (int64_t v = lane; v < d / 8; v += 32) {
+    const uint4 val = src[v];
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j)
+      if (j < k) row_ptr_mut(recv, q[j], r[j], d)[v] = val;
+  }
+  __threadfence_system();  // this thread's peer stores are visible before the closing collective
+}
+
+// out[t] = sum_j w[t,j] * y[dst][row]   (w == nullptr: unit weights)
+__global__ void __launch_bounds__(kWarps * 32) moe_combine_kernel(const __grid_constant__ PeerRows y,
+                                                                   const int32_t* __restrict__ rows,
+                                                                   const int32_t* __restrict__ dst,
+                                                                   const float* __restrict__ w,
+                                                                   __nv_bfloat16* __restrict__ out, int64_t T, int k,
+                                                                   int64_t d) {
+  const int64_t t = int64_t(blockIdx.x) * kWarps + threadIdx.x / 32;
+  if (t >= T) return;
+  const int lane = threadIdx.x & 31;
+  int r[kMaxTopK], q[kMaxTopK];
+  float wt[kMaxTopK];
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j)
+    if (j < k) r[j] = rows[t * k + j], q[j] = dst[t * k + j], wt[j] = w != nullptr ? w[t * k + j] : 1.f;
+  uint4* o = reinterpret_cast<uint4*>(out + t * d);
+  for (int64_t v = lane; v < d / 8; v += 32) {
+    uint4 raw[kMaxTopK];
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j)
+      if (j < k) raw[j] = row_ptr(y, q[j], r[j], d)[v];
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+      if (j < k) {
+        float f[8];
+        unpack8(raw[j], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += wt[j] * f[e];
+      }
+    }
+    o[v] = pack8(acc);
+  }
+}
+
+// dy[dst][row] = bf16(w[t,j] * dout[t]);  dw[t,j] = <dout[t], y[dst][row]>
+__global__ void __launch_bounds__(kWarps * 32) moe_combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout,
+                                                                       const float* __restrict__ w,
+                                                                       const int32_t* __restrict__ rows,
+                                                                       const int32_t* __restrict__ dst,
+                                                                       const __grid_constant__ PeerRows y,
+                                                                       const __grid_constant__ PeerRows dy,
+                                                                       float* __restrict__ dw, int64_t T, int k,
+                                                                       int64_t d) {
+  const int64_t t = int64_t(blockIdx.x) * kWarps + threadIdx.x / 32;
+  if (t >= T) return;
+  const int lane = threadIdx.x & 31;
+  int r[kMaxTopK], q[kMaxTopK];
+  float wt[kMaxTopK], dot[kMaxTopK];
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j)
+    if (j < k) r[j] = rows[t * k + j], q[j] = dst[t * k + j], wt[j] = w[t * k + j], dot[j] = 0.f;
+  const uint4* g = reinterpret_cast<const uint4*>(dout + t * d);
+  for (int64_t v = lane; v < d / 8; v += 32) {
+    float gf[8];
+    unpack8(g[v], gf);
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+      if (j < k) {
+        float yf[8], s[8];
+        unpack8(row_ptr(y, q[j], r[j], d)[v], yf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          dot[j] += gf[e] * yf[e];
+          s[e] = wt[j] * gf[e];
+        }
+        row_ptr_mut(dy, q[j], r[j], d)[v] = pack8(s);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    if (j < k) {
+      float s = dot[j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) dw[t * k + j] = s;
+    }
+  }
+  __threadfence_system();
+}
+
+PeerRows make_rows(const std::vector<int64_t>& ptrs) {
+  TORCH_CHECK(ptrs.size() >= 1 && ptrs.size() <= kMaxRanks, "expert parallelism supports 1..", kMaxRanks, " ranks");
+  PeerRows p{};
+  for (size_t k = 0; k < ptrs.size(); ++k) {
+    TORCH_CHECK(ptrs[k] % 16 == 0, "peer row buffers must be 16-byte aligned");
+    p.ptr[k] = static_cast<uint64_t>(ptrs[k]);
+  }
+  return p;
+}
+
+void check_routes(const at::Tensor& rows, const at::Tensor& dst, int64_t T, int64_t k) {
+  TORCH_CHECK(k >= 1 && k <= kMaxTopK, "top-k must be in [1, ", kMaxTopK, "]");
+  for (const at::Tensor* t : {&rows, &dst})
+    TORCH_CHECK(t->is_cuda() && t->dtype() == at::kInt && t->is_contiguous() && t->numel() == T * k,
+                "routes must be contiguous int32 [T, k]");
+}
+
+unsigned blocks_for(int64_t T) { return static_cast<unsigned>((T + kWarps - 1) / kWarps); }
+
+}  // namespace
+
+void moe_dispatch(at::Tensor x, at::Tensor rows, at::Tensor dst, std::vector<int64_t> recv, int64_t k) {
+  TORCH_CHECK(x.is_cuda() && x.dtype() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "x: bf16 [T, d]");
+  const int64_t T = x.size(0), d = x.size(1);
+  TORCH_CHECK(d % 8 == 0, "hidden size must be a multiple of 8");
+  check_routes(rows, dst, T, k);
+  const c10::cuda::CUDAGuard guard(x.device());
+  if (T == 0) return;
+  moe_dispatch_kernel<<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), rows.data_ptr<int32_t>(), dst.data_ptr<int32_t>(),
+      make_rows(recv), T, static_cast<int>(k), d);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+at::Tensor moe_combine(std::vector<int64_t> y, at::Tensor rows, at::Tensor dst, c10::optional<at::Tensor> w,
+                       int64_t T, int64_t k, int64_t d) {
+  TORCH_CHECK(d % 8 == 0, "hidden size must be a multiple of 8");
+  check_routes(rows, dst, T, k);
+  if (w) TORCH_CHECK(w->is_cuda() && w->dtype() == at::kFloat && w->is_contiguous() && w->numel() == T * k,
+                     "weights: fp32 [T, k]");
+  const c10::cuda::CUDAGuard guard(rows.device());
+  at::Tensor out = at::empty({T, d}, rows.options().dtype(at::kBFloat16));
+  if (T == 0) return out;
+  moe_combine_kernel<<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      make_rows(y), rows.data_ptr<int32_t>(), dst.data_ptr<int32_t>(), w ? w->data_ptr<float>() : nullptr,
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), T, static_cast<int>(k), d);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
+at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::Tensor dst, std::vector<int64_t> y,
+                           std::vector<int64_t> dy, int64_t k) {
+  TORCH_CHECK(dout.is_cuda() && dout.dtype() == at::kBFloat16 && dout.is_contiguous() && dout.dim() == 2,
+              "dout: bf16 [T, d]");
+  const int64_t T = dout.size(0), d = dout.size(1);
+  TORCH_CHECK(d % 8 == 0, "hidden size must be a multiple of 8");
+  check_routes(rows, dst, T, k);
+  TORCH_CHECK(w.is_cuda() && w.dtype() == at::kFloat && w.is_contiguous() && w.numel() == T * k,
+              "weights: fp32 [T, k]");
+  TORCH_CHECK(y.size() == dy.size(), "one y and one dy buffer per rank");
+  const c10::cuda::CUDAGuard guard(dout.device());
+  at::Tensor dw = at::empty({T, k}, w.options());
+  if (T == 0) return dw;
+  moe_combine_bwd_kernel<<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), w.data_ptr<float>(), rows.data_ptr<int32_t>(),
+      dst.data_ptr<int32_t>(), make_rows(y), make_rows(dy), dw.data_ptr<float>(), T, static_cast<int>(k), d);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dw;
+}

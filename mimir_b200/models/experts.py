@@ -88,27 +88,95 @@ class TopKRouter(nn.Module):
 
 
 class MLPMixture(nn.Module):
+    """Router + experts (+ optional always-on shared experts).
+
+    ``expert_intermediate_size`` gives the experts their own SwiGLU width (otherwise they are
+    copies of the dense MLP, as in the reference).  ``grouped`` runs the sparse path as one
+    token exchange: the top-k slots are permuted into per-expert row blocks, each expert runs
+    one GEMM pair on its block and the outputs are combined with the routing weights
+    (:func:`mimir_b200.ops.moe.grouped_experts`).  ``expert_parallel`` additionally splits the
+    experts over the ranks: this rank keeps experts ``first .. first + local - 1`` (still named
+    ``experts.<global index>``) and exchanges token rows with the other ranks over NVLink.
+    """
+
     def __init__(self, mlp, hidden_size, n, k, *, freeze_base=False, top1_straight_through=True, sparse=False,
-                 balance_enabled=False, balance_update_rate=0.001):
+                 balance_enabled=False, balance_update_rate=0.001, expert_intermediate_size=None, shared_experts=0,
+                 grouped=False, expert_parallel=False):
         super().__init__()
-        self.experts = nn.ModuleList([mlp] + [copy.deepcopy(mlp) for _ in range(n - 1)])
+        if expert_intermediate_size is None:
+            make = lambda i: mlp if i == 0 else copy.deepcopy(mlp)  # noqa: E731
+        else:
+            from mimir_b200.models.layers import SwiGLU
+            make = lambda i: SwiGLU(hidden_size, expert_intermediate_size)  # noqa: E731
         self.router = TopKRouter(hidden_size, n, k, freeze_base=freeze_base,
                                  top1_straight_through=top1_straight_through, balance_enabled=balance_enabled,
                                  balance_update_rate=balance_update_rate)
-        self.sparse = sparse
+        self.sparse, self.grouped, self.k, self.n = sparse, grouped or expert_parallel, k, n
+        self.expert_parallel = expert_parallel
+        if expert_parallel:
+            import torch.distributed as dist
+            world = dist.get_world_size() if dist.is_initialized() else 1
+            rank = dist.get_rank() if dist.is_initialized() else 0
+            if n % world:
+                raise ValueError(f"{n} experts cannot be split over {world} expert-parallel ranks")
+            local = n // world
+            experts = [make(i) for i in range(n)]  # every rank draws every expert's init: EP-independent weights
+            self.experts = nn.ModuleDict({str(i): experts[i] for i in range(rank * local, (rank + 1) * local)})
+            del experts
+            for p in self.experts.parameters():
+                p._mimir_rank_local = True
+            self.expert_ids = list(range(rank * local, (rank + 1) * local))
+        else:
+            self.experts = nn.ModuleList([make(i) for i in range(n)])
+            self.expert_ids = list(range(n))
+        width = expert_intermediate_size if expert_intermediate_size is not None else None
+        if shared_experts:
+            from mimir_b200.models.layers import SwiGLU
+            self.shared_experts = nn.ModuleList(
+                SwiGLU(hidden_size, width) if width is not None else copy.deepcopy(mlp) for _ in range(shared_experts))
         if freeze_base:
             self.experts[0].requires_grad_(False)
 
+    def _expert(self, i):
+        return self.experts[str(i)] if self.expert_parallel else self.experts[i]
+
+    def _shared(self, x, stability_diagnostics=None, stability_scope=None):
+        out = None
+        for i, expert in enumerate(getattr(self, "shared_experts", [])):
+            y = expert(x, stability_diagnostics=stability_diagnostics,
+                       stability_scope=f"{stability_scope}/shared_{i}" if stability_scope else None)
+            out = y if out is None else out + y
+        return out
+
     def forward(self, x, stability_diagnostics=None, stability_scope=None, routing_bias=None):
         weights = self.router(x, routing_bias)
-        if self.sparse:
-            return self._dispatch(x, weights, stability_diagnostics, stability_scope)
-        out = torch.zeros_like(x)
-        for i, expert in enumerate(self.experts):
-            y = expert(x, stability_diagnostics=stability_diagnostics,
-                       stability_scope=f"{stability_scope}/expert_{i}" if stability_scope else None)
-            out = out + weights[..., i:i + 1].to(y.dtype) * y
-        return out
+        shared = self._shared(x, stability_diagnostics, stability_scope)
+        if self.grouped and (stability_diagnostics is None or self.expert_parallel):
+            out = self._grouped(x, weights)
+        elif self.sparse:
+            out = self._dispatch(x, weights, stability_diagnostics, stability_scope)
+        else:
+            out = torch.zeros_like(x)
+            for i, expert in enumerate(self.experts):
+                y = expert(x, stability_diagnostics=stability_diagnostics,
+                           stability_scope=f"{stability_scope}/expert_{i}" if stability_scope else None)
+                out = out + weights[..., i:i + 1].to(y.dtype) * y
+        return out if shared is None else out + shared
+
+    @torch.compiler.disable
+    def _grouped(self, x, weights):
+        from mimir_b200.ops.moe import grouped_experts
+        from mimir_b200.parallel.expert import expert_parallel
+        flat = x.reshape(-1, x.shape[-1])
+        w = weights.reshape(-1, self.n)
+        topw, topi = w.topk(self.k, dim=-1)
+        ep = expert_parallel(self.n if self.expert_parallel else self.n, flat.device,
+                             distributed=self.expert_parallel)
+        params = []
+        for i in self.expert_ids:
+            e = self._expert(i)
+            params += [e.gate_up_proj.weight, e.down_proj.weight]
+        return grouped_experts(flat, topw, topi, ep, params).reshape_as(x)
 
     @torch.compiler.disable
     def _dispatch(self, x, weights, diagnostics, scope):
@@ -155,7 +223,7 @@ class RoutedBlock(TransformerBlock):
 # ----------------------------------------------------------------------------------------
 NEW_V2_COMPONENTS = {
     "router", "stack_router", "invocation_gates", "gate_alpha", "attn_residual", "mlp_residual", "residual_alpha",
-    "residual_readout", "memory", "ngram", "routing_bias_scale", "l_branch_mixer",
+    "residual_readout", "memory", "ngram", "routing_bias_scale", "l_branch_mixer", "shared_experts",
 }
 
 

@@ -14,7 +14,7 @@ from __future__ import annotations
 
 import copy
 import math
-from typing import Literal
+from typing import Optional, Literal
 
 import torch
 import torch.nn.functional as F
@@ -58,6 +58,15 @@ class Mimir2Config(RecurrentConfig):
     h_branch_l_mixing: bool = False
     upcycle_from_dense: bool = False
     moe_sparse: bool = False
+    # Additions beyond the reference (defaults keep its behaviour and checkpoint keys):
+    # expert FFN width (None: the dense MLP width, experts start as copies of the dense MLP),
+    # always-on shared experts of the expert width, the grouped token-exchange implementation of
+    # the sparse path, and expert parallelism (experts split over the ranks, tokens exchanged
+    # over NVLink peer memory).
+    moe_expert_intermediate_size: Optional[int] = Field(default=None, ge=8)
+    moe_shared_experts: int = Field(default=0, ge=0)
+    moe_dispatch: Literal["index", "grouped"] = "index"
+    moe_expert_parallel: bool = False
     mos_sparse: bool = False
     mos_sparse_routing: Literal["first_token", "prefix_mean"] = "first_token"
     h_memory_branches: int = Field(default=1, ge=1)
@@ -117,6 +126,15 @@ class Mimir2Config(RecurrentConfig):
             raise ValueError("Use only one migration mode")
         if self.gate_initialize_from_v1 and not self.gates_enabled:
             raise ValueError("gate_initialize_from_v1 requires gates_enabled=true")
+        if (self.moe_dispatch == "grouped" or self.moe_expert_parallel) and not (self.moe_sparse
+                                                                               and self.moe_num_experts > 1):
+            raise ValueError("The grouped MoE dispatch and expert parallelism need moe_sparse with several experts")
+        if self.moe_expert_parallel and self.moe_dispatch != "grouped":
+            raise ValueError("moe_expert_parallel requires moe_dispatch=grouped")
+        if self.upcycle_from_dense and (self.moe_expert_intermediate_size is not None or self.moe_shared_experts):
+            raise ValueError("Upcycling copies the dense MLP: it needs the dense expert width and no shared experts")
+        if self.moe_expert_parallel and (self.specialist_training or self.expert_freeze_base):
+            raise ValueError("Expert parallelism does not support specialist training or a frozen base expert")
         if self.moe_top_k > self.moe_num_experts or self.mos_top_k > self.mos_num_experts:
             raise ValueError("Expert top_k must not exceed num_experts")
         if self.gate_initialize_from_v1 and (self.moe_num_experts > 1 or self.mos_num_experts > 1
@@ -165,7 +183,10 @@ class Mimir2(RecurrentBackbone):
             if config.moe_levels in (name, "both"):
                 install_mlp_mixtures(level.core, self.hidden_size, config.moe_num_experts, config.moe_top_k,
                                      sparse=config.moe_sparse, balance_enabled=config.moe_aux_loss_free,
-                                     balance_update_rate=config.routing_bias_update_rate, **router_opts)
+                                     balance_update_rate=config.routing_bias_update_rate,
+                                     expert_intermediate_size=config.moe_expert_intermediate_size,
+                                     shared_experts=config.moe_shared_experts, grouped=config.moe_dispatch == "grouped",
+                                     expert_parallel=config.moe_expert_parallel, **router_opts)
                 if config.moe_num_experts > 1:
                     norm = config.H_override.get("norm_type", config.norm_type) if name == "H" else config.norm_type
                     level.core.layers = nn.ModuleList(RoutedBlock(b, norm) for b in level.core.layers)

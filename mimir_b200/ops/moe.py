@@ -27,3 +27,180 @@ class MoEPlan:
 
 def moe_plan(weights: torch.Tensor) -> MoEPlan:
     return MoEPlan(weights)
+
+
+# ----------------------------------------------------------------------------------------
+# Grouped experts with an expert-parallel token exchange
+# ----------------------------------------------------------------------------------------
+def _swiglu_fwd(gu: torch.Tensor) -> torch.Tensor:
+    from mimir_b200.ops._ext import ext, kernels_enabled
+    if kernels_enabled(gu) and gu.shape[-1] % 16 == 0:
+        return ext().swiglu_fwd(gu)
+    gate, up = gu.chunk(2, dim=-1)
+    return torch.nn.functional.silu(gate) * up
+
+
+def _swiglu_bwd(gu: torch.Tensor, dp: torch.Tensor) -> torch.Tensor:
+    from mimir_b200.ops._ext import ext, kernels_enabled
+    if kernels_enabled(gu) and gu.shape[-1] % 16 == 0:
+        return ext().swiglu_bwd(dp.contiguous(), gu)
+    gate, up = gu.float().chunk(2, dim=-1)
+    sig = torch.sigmoid(gate)
+    dgate = dp.float() * up * sig * (1 + gate * (1 - sig))
+    dup = dp.float() * gate * sig
+    return torch.cat([dgate, dup], dim=-1).to(gu.dtype)
+
+
+class _Exchange:
+    """Moves token-slot rows between the source ranks and the expert owners for one plan.
+
+    CUDA: peer-memory kernels (``csrc/moe.cu``) into/out of ``PeerBuffer`` regions.
+    CPU: ``all_to_all_single`` plus the (source, expert) -> (expert, source) row permutation.
+    """
+
+    def __init__(self, ep, plan, T: int, k: int, d: int):
+        self.ep, self.plan, self.T, self.k, self.d = ep, plan, T, k, d
+        self.rows_in = sum(plan.expert_rows)
+        if not ep.cuda:
+            W, L = ep.size, ep.local
+            C = plan.counts.view(W, W, L)[:, ep.rank]            # [source, local expert]
+            src_start = torch.cumsum(C.sum(1), 0) - C.sum(1)     # where each source's rows land in the recv order
+            within = torch.cumsum(C, 1) - C                      # offset of each expert inside a source's chunk
+            pieces = [torch.arange(int(src_start[s] + within[s, e]), int(src_start[s] + within[s, e] + C[s, e]))
+                      for e in range(L) for s in range(W)]
+            self.perm = torch.cat(pieces) if pieces else torch.zeros(0, dtype=torch.long)  # buffer row -> recv row
+
+    # ---------------------------------------------------------------- CPU helpers
+    def _a2a(self, rows: torch.Tensor, send_counts, recv_counts) -> torch.Tensor:
+        if self.ep.size == 1:
+            return rows
+        import torch.distributed as dist
+        out = rows.new_empty((sum(recv_counts), rows.shape[1]))
+        dist.all_to_all_single(out, rows.contiguous(), recv_counts, send_counts, group=self.ep.group)
+        return out
+
+    def to_owner_cpu(self, slot_rows: torch.Tensor) -> torch.Tensor:
+        """[T*k, d] rows in slot order -> [rows_in, d] rows in this rank's buffer order."""
+        sent = slot_rows[self.plan.order]
+        recv = self._a2a(sent, self.plan.send_counts, self.plan.recv_counts)
+        return recv[self.perm]
+
+    def from_owner_cpu(self, buffer_rows: torch.Tensor) -> torch.Tensor:
+        """[rows_in, d] rows in buffer order -> [T*k, d] rows in slot order."""
+        recv = torch.empty_like(buffer_rows)
+        recv[self.perm] = buffer_rows
+        back = self._a2a(recv, self.plan.recv_counts, self.plan.send_counts)
+        out = torch.empty_like(back)
+        out[self.plan.order] = back
+        return out
+
+
+def _expert_forward(xp, expert_rows, weights, y=None):
+    """Per local expert: ``y = down(swiglu(x @ gate_up^T))`` on its contiguous rows."""
+    y = torch.empty_like(xp) if y is None else y
+    gus, s = [], 0
+    for i, n in enumerate(expert_rows):
+        gu_w, dn_w = weights[2 * i], weights[2 * i + 1]
+        if n:
+            gu = xp[s:s + n] @ gu_w.t()
+            torch.matmul(_swiglu_fwd(gu), dn_w.t(), out=y[s:s + n])
+        else:
+            gu = xp.new_empty((0, gu_w.shape[0]))
+        gus.append(gu)
+        s += n
+    return y, gus
+
+
+def _expert_backward(dy, xp, gus, expert_rows, weights, dxp):
+    grads, s = [], 0
+    for i, n in enumerate(expert_rows):
+        gu_w, dn_w = weights[2 * i], weights[2 * i + 1]
+        if n:
+            gu = gus[i]
+            d_dn = dy[s:s + n].t() @ _swiglu_fwd(gu)
+            dgu = _swiglu_bwd(gu, dy[s:s + n] @ dn_w)
+            d_gu = dgu.t() @ xp[s:s + n]
+            torch.matmul(dgu, gu_w, out=dxp[s:s + n])
+        else:  # every expert gets a gradient (zero) so all ranks update the same parameters
+            d_gu, d_dn = torch.zeros_like(gu_w), torch.zeros_like(dn_w)
+        grads += [d_gu.to(gu_w.dtype), d_dn.to(dn_w.dtype)]
+        s += n
+    return grads
+
+
+class _GroupedExpertsFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, topw, ep, plan, keep, *weights):
+        T, d = x.shape
+        k = topw.shape[1]
+        ex = _Exchange(ep, plan, T, k, d)
+        ctx.ex, ctx.weights_n = ex, len(weights)
+        w32 = topw.float().contiguous()
+        if ep.cuda:
+            from mimir_b200.ops._ext import ext
+            C = ext()
+            buf = ep.acquire(2 * plan.capacity, d)
+            C.moe_dispatch(x.contiguous(), plan.rows, plan.dst, buf.peer_ptrs(0, d), k)
+            ep.barrier()  # every rank's rows have landed in their owners' buffers
+            xp = buf.view(0, ex.rows_in, d)
+            _, gus = _expert_forward(xp, plan.expert_rows, weights, buf.view(plan.capacity, ex.rows_in, d))
+            ep.barrier()  # every owner's outputs are in place
+            out = C.moe_combine(buf.peer_ptrs(plan.capacity, d), plan.rows, plan.dst, w32, T, k, d)
+            if not keep:  # no backward: the next exchange's collective orders any reuse of the buffer
+                ep.release(buf)
+                return out
+            ctx.buf = buf
+            ctx.save_for_backward(w32, *weights)
+            ctx.xp, ctx.gus = xp, gus
+            return out
+        slots = x.repeat_interleave(k, dim=0) if k > 1 else x
+        xp = ex.to_owner_cpu(slots)
+        y, gus = _expert_forward(xp, plan.expert_rows, weights)
+        ys = ex.from_owner_cpu(y).view(T, k, d)
+        out = (ys.float() * w32.unsqueeze(-1)).sum(1).to(x.dtype)
+        ctx.save_for_backward(w32, *weights)
+        ctx.xp, ctx.gus, ctx.ys = xp, gus, ys
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        ex, plan, ep = ctx.ex, ctx.ex.plan, ctx.ex.ep
+        w32, *weights = ctx.saved_tensors
+        T, k, d = ex.T, ex.k, ex.d
+        dout = dout.contiguous()
+        if ep.cuda:
+            from mimir_b200.ops._ext import ext
+            C = ext()
+            gbuf = ep.acquire(2 * plan.capacity, d)
+            ep.barrier()  # every owner is done with the previous use of this buffer
+            dw = C.moe_combine_bwd(dout, w32, plan.rows, plan.dst, ctx.buf.peer_ptrs(plan.capacity, d),
+                                   gbuf.peer_ptrs(0, d), k)
+            ep.barrier()  # the scaled output gradients have reached their owners
+            dy = gbuf.view(0, ex.rows_in, d)
+            dxp = gbuf.view(plan.capacity, ex.rows_in, d)
+            grads = _expert_backward(dy, ctx.xp, ctx.gus, plan.expert_rows, weights, dxp)
+            ep.barrier()  # every owner's input gradients are in place
+            dx = C.moe_combine(gbuf.peer_ptrs(plan.capacity, d), plan.rows, plan.dst, None, T, k, d)
+            ep.release(gbuf)
+            ep.release(ctx.buf)
+        else:
+            dys = (dout.float().unsqueeze(1) * w32.unsqueeze(-1)).to(dout.dtype).reshape(T * k, d)
+            dw = (dout.float().unsqueeze(1) * ctx.ys.float()).sum(-1)
+            dy = ex.to_owner_cpu(dys)
+            dxp = torch.empty_like(ctx.xp)
+            grads = _expert_backward(dy, ctx.xp, ctx.gus, plan.expert_rows, weights, dxp)
+            dx = ex.from_owner_cpu(dxp).view(T, k, d).float().sum(1).to(dout.dtype)
+        ctx.xp = ctx.gus = ctx.ys = ctx.buf = None
+        return (dx, dw, None, None, None, *grads)
+
+
+def grouped_experts(x: torch.Tensor, topw: torch.Tensor, topi: torch.Tensor, ep, weights: list) -> torch.Tensor:
+    """``sum_j topw[t, j] * expert_{topi[t, j]}(x[t])`` with this rank's experts' weights
+    ``[gate_up_0, down_0, gate_up_1, down_1, ...]`` (experts ``ep.first ... ep.first + ep.local - 1``).
+
+    The rows of every expert are exchanged with its owner rank (``ep``); within an expert the
+    rows are in token order, as the reference's per-expert ``nonzero`` lists
+    (``src/mimir/model/expert_mixtures.py:92-104``)."""
+    plan = ep.plan(topi)
+    keep = torch.is_grad_enabled() and (x.requires_grad or topw.requires_grad or any(w.requires_grad for w in weights))
+    return _GroupedExpertsFn.apply(x, topw, ep, plan, keep, *weights)

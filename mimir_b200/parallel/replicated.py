@@ -38,6 +38,13 @@ from torch import Tensor, nn
 from torch.optim.optimizer import Optimizer
 
 _ALIGN = 8  # elements: 16 bytes of bf16, 32 bytes of fp32
+_LOCAL_FLAG = 256  # segment kind flag: rank-local parameter (csrc/dp_fused.cu kLocalFlag)
+
+
+def is_local(p: Tensor) -> bool:
+    """A rank-local parameter (an expert owned by this expert-parallel rank): its gradient is
+    complete on this rank, so it is neither reduced nor gathered."""
+    return bool(getattr(p, "_mimir_rank_local", False))
 
 
 def _align(n: int) -> int:
@@ -56,6 +63,7 @@ class ParamSlot:
     rows_mine: int         # owned rows (may be 0)
     shard: int             # element offset in the shard buffers
     trainable: bool
+    local: bool = False    # rank-local (expert-parallel) parameter: never reduced or gathered
 
     @property
     def shard_numel(self) -> int:
@@ -84,6 +92,8 @@ class ReplicatedEngine:
         self._broadcast_initial_state()
         self.slots = self._layout()
         self.total = self.slots[-1].flat + _align(self.slots[-1].numel) if self.slots else 0
+        # Replicated parameters come first (same offsets on every rank); rank-local ones follow.
+        self.replicated_total = min((s.flat for s in self.slots if s.local), default=self.total)
         self.shard_total = max((s.shard + _align(s.shard_numel) for s in self.slots), default=0)
         self._allocate()
         self.reduced: Optional[Tensor] = None
@@ -100,17 +110,18 @@ class ReplicatedEngine:
     def _broadcast_initial_state(self) -> None:
         if self.world == 1:
             return
-        for t in list(self.model.parameters()) + list(self.model.buffers()):
+        for t in [p for p in self.model.parameters() if not is_local(p)] + list(self.model.buffers()):
             dist.broadcast(t.data, src=dist.get_global_rank(self.group, 0) if self.group else 0, group=self.group)
 
     def _layout(self) -> list[ParamSlot]:
         slots, flat, shard = [], 0, 0
-        for fqn, p in self.model.named_parameters():
+        named = list(self.model.named_parameters())
+        for fqn, p in [x for x in named if not is_local(x[1])] + [x for x in named if is_local(x[1])]:
             rows = p.shape[0] if p.dim() > 0 else 1
-            chunk = math.ceil(rows / self.world)
-            row0 = min(rows, self.rank * chunk)
+            chunk = rows if is_local(p) else math.ceil(rows / self.world)
+            row0 = 0 if is_local(p) else min(rows, self.rank * chunk)
             mine = max(0, min(rows, row0 + chunk) - row0)
-            slot = ParamSlot(fqn, p, p.shape, flat, p.numel(), rows, row0, mine, shard, p.requires_grad)
+            slot = ParamSlot(fqn, p, p.shape, flat, p.numel(), rows, row0, mine, shard, p.requires_grad, is_local(p))
             slots.append(slot)
             flat += _align(p.numel())
             shard += _align(slot.shard_numel)
@@ -211,6 +222,7 @@ class ReplicatedEngine:
                 continue
             n = s.shard_numel
             kind, dst, dst_rank, has_m = (extra or {}).get(s.fqn, (0, 0, 0, 1))
+            kind |= _LOCAL_FLAG if s.local else 0
             vec = int(s.shard_flat % 8 == 0 and s.shard % 8 == 0 and n % 8 == 0 and dst % 8 == 0)
             rows.append((s.shard_flat, s.shard, n, block, lrs[s.fqn], wds[s.fqn], bc1[s.fqn], bc2_sqrt[s.fqn], vec,
                          kind, dst, dst_rank, has_m))
@@ -233,12 +245,10 @@ class ReplicatedEngine:
             table, blocks = self.segments(zero, zero, zero, zero)
             self.reduced = torch.empty(self.shard_total, dtype=torch.float32, device=self.device)
             partial = torch.empty(max(blocks, 1), dtype=torch.float32, device=self.device)
-            ext().dp_reduce(self.peer_grads, table, blocks, self.reduced, partial)
+            ext().dp_reduce(self.peer_grads, table, blocks, self.reduced, partial, self.rank)
             total = partial[:blocks].double().sum().reshape(1)
         else:
-            full = self.grads.to(torch.float32)
-            if self.world > 1:
-                dist.all_reduce(full, group=self.group)
+            full = self.summed_grads()
             self.reduced = torch.zeros(self.shard_total, dtype=torch.float32)
             for s in self.slots:
                 if s.trainable and s.shard_numel:
@@ -248,12 +258,19 @@ class ReplicatedEngine:
             dist.all_reduce(total, group=self.group)
         return total
 
+    def summed_grads(self) -> Tensor:
+        """fp32 gradients summed over the ranks (rank-local parameters keep their own)."""
+        full = self.grads.to(torch.float32)
+        if self.world > 1:
+            dist.all_reduce(full[:self.replicated_total], group=self.group)
+        return full
+
     @torch.no_grad()
     def gather_weights(self) -> None:
         """Rebuild every rank's replicated weights from the master shards (after a load)."""
         for s in self.slots:
             local = self.master[s.shard:s.shard + s.shard_numel].to(self.compute_dtype)
-            if self.world == 1:
+            if self.world == 1 or s.local:
                 self.weights[s.shard_flat:s.shard_flat + s.shard_numel] = local
                 continue
             chunk = math.ceil(s.rows / self.world) * (s.numel // s.rows)
@@ -273,8 +290,12 @@ class ReplicatedEngine:
         return self._mesh
 
     def shard_dtensor(self, s: ParamSlot, buffer: Tensor):
+        """The shard of ``s`` in ``buffer`` as a ``Shard(0)`` DTensor (a rank-local parameter: the plain
+        full tensor, which only its owner rank saves and loads)."""
         from torch.distributed.tensor import DTensor, Shard
         local = buffer[s.shard:s.shard + s.shard_numel].view(s.local_shape())
+        if s.local:
+            return local
         full_stride = torch.empty(s.shape, device="meta").stride()
         return DTensor.from_local(local, self.mesh(), [Shard(0)], run_check=False, shape=s.shape, stride=full_stride)
 
@@ -335,7 +356,7 @@ class ReplicatedAdamATan2(Optimizer):
             if eng.reduced is None:
                 eng.barrier()  # every rank's backward has finished writing its gradients
             ext().dp_step(eng.peer_grads, eng.peer_weights, table, blocks, eng.master, self.exp_avg, self.exp_avg_sq,
-                          self.ema, eng.reduced, self.grad_scale, b1, b2, ema if ema is not None else 0.0, [])
+                          self.ema, eng.reduced, self.grad_scale, b1, b2, ema if ema is not None else 0.0, [], eng.rank)
             eng.barrier()  # every rank's weight stores have landed
         else:
             self._step_cpu(lrs, wds, bc1, bc2_sqrt, b1, b2, ema)
@@ -345,9 +366,7 @@ class ReplicatedAdamATan2(Optimizer):
     def _step_cpu(self, lrs: dict, wds: dict, bc1: dict, bc2_sqrt: dict, b1, b2, ema) -> None:
         eng = self.engine
         if eng.reduced is None:
-            full = eng.grads.to(torch.float32)
-            if eng.world > 1:
-                dist.all_reduce(full, group=eng.group)
+            full = eng.summed_grads()
         scale = self.grad_scale if self.grad_scale is not None else None
         for s in eng.slots:
             if s.fqn not in lrs or s.shard_numel == 0:
@@ -441,6 +460,8 @@ class ReplicatedMuonAdamW(ReplicatedAdamATan2):
         from mimir_b200.optim.muon import matrix_splits
         if not 0 <= momentum < 1 or ns_steps < 1 or muon_lr_scale <= 0:
             raise ValueError("Invalid Muon momentum, iterations or LR scale")
+        if any(s.local for s in engine.slots):
+            raise ValueError("MuonAdamW on the replicated engine does not support expert-parallel parameters")
         super().__init__(engine, **kwargs)
         for group in self.param_groups:
             group.update(optimizer_kind="muon_adamw", muon_momentum=momentum, muon_ns_steps=ns_steps,
@@ -519,13 +540,13 @@ class ReplicatedMuonAdamW(ReplicatedAdamATan2):
                 eng.barrier()  # every rank's backward has finished writing its gradients
             table, blocks = eng.segments(first["lr"], first["wd"], first["bc1"], first["bc2"], first["extra"])
             C.dp_step(eng.peer_grads, eng.peer_weights, table, blocks, eng.master, self.exp_avg, self.exp_avg_sq,
-                      self.ema, eng.reduced, self.grad_scale, b1, b2, ema_decay, self.peer_work)
+                      self.ema, eng.reduced, self.grad_scale, b1, b2, ema_decay, self.peer_work, eng.rank)
             eng.barrier()  # every shard of every matrix has reached its owner
             self._orthogonalise(owned, group["muon_ns_steps"])
             eng.barrier()  # every owner has finished
             table, blocks = eng.segments(second["lr"], second["wd"], second["bc1"], second["bc2"], second["extra"])
             C.dp_step(eng.peer_grads, eng.peer_weights, table, blocks, eng.master, self.exp_avg, self.exp_avg_sq,
-                      self.ema, None, None, b1, b2, ema_decay, self.peer_work)
+                      self.ema, None, None, b1, b2, ema_decay, self.peer_work, eng.rank)
             eng.barrier()  # every rank's weight stores have landed
         eng.reduced = None
         self.grad_scale = None
@@ -551,9 +572,7 @@ class ReplicatedMuonAdamW(ReplicatedAdamATan2):
         b1, b2 = group["betas"]
         ema = group["ema"]
         if eng.reduced is None:
-            full = eng.grads.to(torch.float32)
-            if eng.world > 1:
-                dist.all_reduce(full, group=eng.group)
+            full = eng.summed_grads()
         for s in eng.slots:
             if s.fqn not in first["lr"]:
                 continue
