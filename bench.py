@@ -30,14 +30,34 @@ import torch.distributed as dist
 ROOT = os.path.dirname(os.path.abspath(__file__))
 SEQ_LEN, SEQS_PER_GPU, VOCAB = 4096, 4, 65536
 MODEL = dict(n_layers=24, hidden_size=2048, num_heads=16, num_key_value_heads=4, expansion=4.125)
+# BASELINE config 3 (``--config moe``): 16 layers, d 2048, 64 experts top-2 of FFN 1408 plus one
+# shared expert, expert parallelism over the GPUs, aux-loss-free routing balance, Zipf(1.1) tokens.
+MOE = dict(n_layers=16, experts=64, top_k=2, expert_ffn=1408, shared=1, zipf=1.1)
+CONFIG = {"name": "dense"}  # set from --config in main()
 METRIC = "train tokens/sec (box, device-timed, max over ranks) at 1/2/4/8 B200; MFU"
 BASELINE_VALUE = None  # the reference publishes no throughput number
+MODEL_LABEL = {"dense": "Mimir2 dense ~1.3B (24x2048, 16Q/4KV heads x128, SwiGLU 5632, vocab 65536)",
+               "moe": "Mimir2 MoE (16x2048, 16Q/4KV heads x128, 64 experts top-2 FFN 1408 + 1 shared expert, "
+                      "aux-loss-free routing balance, vocab 65536, Zipf(1.1) token ids)"}
 OPTIMIZER_LABEL = {"adam_atan2": "AdamATan2 + EMA",
                    "muon": "MuonAdamW + EMA (Muon on 2-D hidden matrices, 5 Newton-Schulz iterations in fp32, "
                            "momentum 0.95; Adam on the rest)"}
 
 
-def arch_dict(kv_heads=4):
+def arch_dict(kv_heads=4, reference=False):
+    if CONFIG["name"] == "moe":
+        base = _arch_base(kv_heads) | dict(n_layers=MOE["n_layers"], moe_num_experts=MOE["experts"],
+                                           moe_top_k=MOE["top_k"], moe_sparse=True, moe_aux_loss_free=True)
+        if reference:  # no expert width, shared experts or expert parallelism in the reference:
+            # its experts are dense-MLP copies; expansion 1.03125 gives 2048*1.03125*2/3 = 1408, which
+            # its multiple-of-256 rounding turns into 1536.
+            return base | dict(expansion=1.03125)
+        return base | dict(moe_expert_intermediate_size=MOE["expert_ffn"], moe_shared_experts=MOE["shared"],
+                           moe_dispatch="grouped", moe_expert_parallel=True)
+    return _arch_base(kv_heads)
+
+
+def _arch_base(kv_heads):
     return dict(name="mimir2", max_seq_len=SEQ_LEN, n_layers=MODEL["n_layers"], hidden_size=MODEL["hidden_size"],
                 num_heads=MODEL["num_heads"], num_key_value_heads=kv_heads, expansion=MODEL["expansion"],
                 init_type="lecun_normal", norm_type="pre", norm_eps=1e-6, pos_emb_type="rope", rope_theta=10000.0,
@@ -51,8 +71,14 @@ def synthetic_batch(rank: int, step: int):
     rng = np.random.default_rng(1_000_003 * rank + step)
     T = SEQ_LEN * SEQS_PER_GPU
     prefix = rng.integers(0, 2049, size=SEQS_PER_GPU).astype(np.int32)
-    inputs = rng.integers(0, VOCAB, size=T).astype(np.int32)
-    labels = rng.integers(0, VOCAB, size=T).astype(np.int32)
+    if CONFIG["name"] == "moe":  # Zipf(s) over the vocabulary skews the routing
+        p = np.arange(1, VOCAB + 1, dtype=np.float64) ** -MOE["zipf"]
+        p /= p.sum()
+        inputs = rng.choice(VOCAB, size=T, p=p).astype(np.int32)
+        labels = rng.choice(VOCAB, size=T, p=p).astype(np.int32)
+    else:
+        inputs = rng.integers(0, VOCAB, size=T).astype(np.int32)
+        labels = rng.integers(0, VOCAB, size=T).astype(np.int32)
     for s in range(SEQS_PER_GPU):
         labels[s * SEQ_LEN: s * SEQ_LEN + max(int(prefix[s]) - 1, 0)] = -100  # supervise the answer only
     positions = np.tile(np.arange(SEQ_LEN, dtype=np.int32), SEQS_PER_GPU)
@@ -80,11 +106,17 @@ def attention_pairs(host) -> int:
 
 def model_flops_per_step(host, kv_heads) -> float:
     d, H, hd, F = MODEL["hidden_size"], MODEL["num_heads"], 128, 5632
-    per_layer = d * (2 * H + 2 * kv_heads) * hd + H * hd * d + d * 2 * F + F * d
-    matmul_params = MODEL["n_layers"] * per_layer + d * VOCAB
+    layers = MODEL["n_layers"]
+    mlp = d * 2 * F + F * d
+    if CONFIG["name"] == "moe":  # active experts per token (top-k + shared) and the router
+        layers = MOE["n_layers"]
+        fe = CONFIG.get("expert_ffn", MOE["expert_ffn"])
+        mlp = CONFIG.get("active_experts", MOE["top_k"] + MOE["shared"]) * 3 * d * fe + d * MOE["experts"]
+    per_layer = d * (2 * H + 2 * kv_heads) * hd + H * hd * d + mlp
+    matmul_params = layers * per_layer + d * VOCAB
     T = SEQ_LEN * SEQS_PER_GPU
     dense = 6.0 * matmul_params * T
-    attn_fwd = 4.0 * hd * H * attention_pairs(host) * MODEL["n_layers"]
+    attn_fwd = 4.0 * hd * H * attention_pairs(host) * layers
     return dense + 3.0 * attn_fwd
 
 
@@ -192,7 +224,8 @@ def run_ours(args, rank, world, local):
     vocab = arch.pop("vocab_size")
     config = PretrainConfig(arch=arch, data=dict(path="synthetic"), global_batch_size=SEQ_LEN * SEQS_PER_GPU * world,
                             epochs=1, lr=3e-4, lr_warmup_steps=0, lr_min_ratio=1.0, weight_decay=0.1, beta1=0.9,
-                            beta2=0.95, ema=0.9999, distributed_strategy=args.dp, lr_auto=False,
+                            beta2=0.95, ema=None if CONFIG["name"] == "moe" else 0.9999,
+                            distributed_strategy=args.dp, lr_auto=False,
                             optimizer=args.optimizer, muon_momentum=0.95, muon_ns_steps=5)
     torch.manual_seed(0)
     model, carry, optim = create_model_and_optimizer(config, {"vocab_size": vocab, "max_seq_len": SEQ_LEN}, device)
@@ -237,6 +270,9 @@ def run_ours(args, rank, world, local):
     else:
         label = (f"dp{world}: replicated bf16 weights, fp32 master+AdamATan2 state sharded like FSDP2, one fused "
                  "NVLink reduce-scatter+update+all-gather kernel per step")
+    if CONFIG["name"] == "moe":
+        label += (f"; ep{world}: {MOE['experts'] // world} experts per GPU, token rows dispatched/combined over "
+                  "NVLink peer memory (route plan from all-gathered expert counts, no capacity factor)")
     return emit(args, world, seconds, e2e_seconds, h2d, 4, flops, clock_info, launches, impl="ours",
                 extra={"final_loss": losses[-1], "parallelism": label})
 
@@ -289,13 +325,13 @@ def run_reference(args, rank, world, local):
     # dense prefix-LM attention backend (accelerator "none") is the path that can run.
     set_accelerator_type("none")
     device = torch.device("cuda", local)
-    arch = arch_dict(kv_heads=None)  # the reference ties KV heads to Q heads
+    arch = arch_dict(kv_heads=None, reference=True)  # the reference ties KV heads to Q heads
     arch.pop("num_key_value_heads")
     vocab = arch.pop("vocab_size")
     compiled = os.environ.get("MIMIR_REF_COMPILE", "1") == "1"
     config = RefConfig(arch=arch, data=dict(path="synthetic"), global_batch_size=SEQ_LEN * SEQS_PER_GPU * world,
                        epochs=1, lr=3e-4, lr_warmup_steps=0, lr_min_ratio=1.0, weight_decay=0.1, beta1=0.9, beta2=0.95,
-                       ema=0.9999, distributed_strategy="fsdp", accelerator_type="sm100", lr_auto=False,
+                       ema=None if CONFIG["name"] == "moe" else 0.9999, distributed_strategy="fsdp", accelerator_type="sm100", lr_auto=False,
                        compile_train_batch=compiled)
     model_cfg = config.arch.model_dump() | {"vocab_size": vocab, "max_seq_len": SEQ_LEN} | config.data.model_dump() | {
         "fwd_bwd_dtype": "bfloat16", "activation_checkpointing": "none"}
@@ -312,7 +348,8 @@ def run_reference(args, rank, world, local):
         optim = RefMuon(model.named_parameters(), momentum=0.95, ns_steps=5, muon_lr_scale=1.0, lr=0.0,
                         betas=(0.9, 0.95), weight_decay=0.1, ema=0.9999)
     else:
-        optim = RefAdam(model.parameters(), lr=0.0, betas=(0.9, 0.95), weight_decay=0.1, ema=0.9999)
+        optim = RefAdam(model.parameters(), lr=0.0, betas=(0.9, 0.95), weight_decay=0.1,
+                        ema=None if CONFIG["name"] == "moe" else 0.9999)
     state = TrainState(model=model, carry=None, optim=optim, step=0, total_steps=10_000, fwd_bwd_dtype=torch.bfloat16,
                        use_cuda_autocast=False)
     hosts = [synthetic_batch(rank, i) for i in range(2)]
@@ -341,9 +378,15 @@ def run_reference(args, rank, world, local):
         (metrics["loss"][0] / metrics["loss"][1]).item()
     torch.cuda.synchronize()
     e2e_seconds = max_over_ranks(time.perf_counter() - t0)
+    if CONFIG["name"] == "moe":
+        CONFIG.update(expert_ffn=1536, active_experts=MOE["top_k"])
     flops = model_flops_per_step(hosts[0][0], MODEL["num_heads"])
     extra = {"attention_backend": "reference dense prefix-LM SDPA (FA4 unavailable offline)",
              "num_key_value_heads": MODEL["num_heads"], "torch_compile": compiled}
+    if CONFIG["name"] == "moe":
+        extra["moe_reference_limits"] = ("no expert FFN width option (experts are dense-MLP copies: FFN 1536, the "
+                                         "multiple of 256 nearest 1408), no shared expert, no expert parallelism "
+                                         "(all 64 experts on every rank)")
     return emit(args, world, seconds, e2e_seconds, h2d, 4, flops, clock_info, None, impl="reference", extra=extra)
 
 
@@ -364,12 +407,14 @@ def emit(args, world, seconds, e2e_seconds, h2d_bytes, d2h_bytes, flops_per_step
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": (value / BASELINE_VALUE) if BASELINE_VALUE else None, "dtype": "bf16",
-        "data": "synthetic uniform token ids, random-init weights",
-        "config": {"model": "Mimir2 dense ~1.3B (24x2048, 16Q/4KV heads x128, SwiGLU 5632, vocab 65536)",
+        "data": ("synthetic Zipf(1.1) token ids" if CONFIG["name"] == "moe" else "synthetic uniform token ids")
+                + ", random-init weights, 2 batches per rank alternated",
+        "config": {"model": MODEL_LABEL[CONFIG["name"]],
                    "global_batch": SEQ_LEN * SEQS_PER_GPU * world, "seq_len": SEQ_LEN, "micro_batch": SEQS_PER_GPU,
                    "parallelism": (extra or {}).pop("parallelism", f"fsdp{world}"),
                    "mask": "prefix-LM, prompt length uniform [0,2048]",
-                   "optimizer": OPTIMIZER_LABEL[args.optimizer], "l2": "inputs larger than L2 (weights+activations >> 126 MB)"},
+                   "optimizer": OPTIMIZER_LABEL[args.optimizer] + (" (no EMA)" if CONFIG["name"] == "moe" else ""),
+                   "l2": "inputs larger than L2 (weights+activations >> 126 MB)"},
         "mfu": round(achieved / 2.25e15, 4),
         "frac_of_measured_bf16": round(achieved / (peaks.get("bf16_tflops_sustained", 1422.4) * 1e12), 4),
         "clocks": clocks,
@@ -392,11 +437,14 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["dense", "moe"], default="dense",
+                    help="dense: the headline 1.3B config; moe: the 64-expert MoE config with expert parallelism")
     ap.add_argument("--optimizer", choices=["adam_atan2", "muon"], default="adam_atan2",
                     help="adam_atan2: the headline config; muon: the Muon variant of the same model")
     ap.add_argument("--dp", choices=["replicated", "fsdp"], default="replicated",
                     help="data-parallel engine of our arm (the reference arm always uses its FSDP2)")
     args = ap.parse_args()
+    CONFIG["name"] = args.config
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference" and not os.path.isdir(os.path.join(ROOT, "baseline", "_ref", "mimir")):

@@ -1,0 +1,136 @@
+"""MoE token-exchange kernels (csrc/moe.cu) and expert parallelism on B200s.
+
+* dispatch / combine / combine-backward kernels against PyTorch fp32 indexing arithmetic;
+* the grouped MoE path on one GPU against the per-expert ``index_add`` path;
+* expert parallelism over CUDA-IPC peer buffers on 2+ GPUs (spawned NCCL ranks) against one
+  process running every expert on the concatenated batch.
+"""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+D, F, E, K = 256, 384, 8, 2
+
+
+def test_exchange_kernels_match_torch():
+    from mimir_b200.ops._ext import ext
+    C = ext()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    T = 37
+    x = torch.randn(T, D, device=dev, generator=g).to(torch.bfloat16)
+    topi = torch.stack([torch.randperm(E, device=dev, generator=g)[:K] for _ in range(T)])
+    from mimir_b200.parallel.expert import expert_parallel
+    ep = expert_parallel(E, dev, distributed=False)
+    plan = ep.plan(topi)
+    buf = torch.zeros(T * K, D, device=dev, dtype=torch.bfloat16)
+    C.moe_dispatch(x, plan.rows, plan.dst, [buf.data_ptr()], K)
+    rows = plan.rows.long()
+    for j in range(K):
+        assert torch.equal(buf[rows[:, j]], x)
+    y = torch.randn(T * K, D, device=dev, generator=g).to(torch.bfloat16)
+    w = torch.rand(T, K, device=dev, generator=g)
+    out = C.moe_combine([y.data_ptr()], plan.rows, plan.dst, w, T, K, D)
+    want = (y[rows].float() * w.unsqueeze(-1)).sum(1)
+    torch.testing.assert_close(out.float(), want, rtol=1e-2, atol=1e-2)
+    dout = torch.randn(T, D, device=dev, generator=g).to(torch.bfloat16)
+    dy = torch.zeros_like(y)
+    dw = C.moe_combine_bwd(dout, w, plan.rows, plan.dst, [y.data_ptr()], [dy.data_ptr()], K)
+    torch.testing.assert_close(dw, (dout.float().unsqueeze(1) * y[rows].float()).sum(-1), rtol=1e-4, atol=1e-3)
+    for j in range(K):
+        torch.testing.assert_close(dy[rows[:, j]].float(), (w[:, j:j + 1] * dout.float()), rtol=1e-2, atol=1e-2)
+
+
+def _mixture(grouped, ep=False, shared=1, seed=0):
+    from mimir_b200.models.experts import MLPMixture
+    from mimir_b200.models.layers import SwiGLU
+    torch.manual_seed(seed)
+    m = MLPMixture(SwiGLU(D, F), D, E, K, sparse=True, grouped=grouped, expert_parallel=ep, shared_experts=shared,
+                   expert_intermediate_size=F)
+    with torch.no_grad():
+        for i, r in enumerate(m.router.rows):
+            r.copy_(torch.randn(D, generator=torch.Generator().manual_seed(10 + i)) * 0.5)
+    return m
+
+
+def _run(m, x, g):
+    x = x.clone().requires_grad_(True)
+    y = m(x)
+    (y.float() * g).sum().backward()
+    return y.detach().float(), x.grad.float(), {n: p.grad.float() for n, p in m.named_parameters()}
+
+
+def test_grouped_path_matches_index_path():
+    dev = torch.device("cuda", 0)
+    ref = _mixture(False).to(dev, torch.bfloat16)
+    grp = _mixture(True).to(dev, torch.bfloat16)
+    grp.load_state_dict(ref.state_dict())
+    gen = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(300, D, device=dev, generator=gen).to(torch.bfloat16)
+    g = torch.randn(300, D, device=dev, generator=gen)
+    a, b = _run(ref, x, g), _run(grp, x, g)
+    torch.testing.assert_close(b[0], a[0], rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(b[1], a[1], rtol=2e-2, atol=2e-2)
+    for n in a[2]:
+        scale = a[2][n].abs().max().clamp_min(1e-6)
+        assert (b[2][n] - a[2][n]).abs().max() / scale < 3e-2, n
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _ep_rank(rank, world, port, out):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        m = _mixture(True, ep=True).to(dev, torch.bfloat16)
+        gen = torch.Generator(device=dev).manual_seed(100 + rank)
+        x = torch.randn(200, D, device=dev, generator=gen).to(torch.bfloat16)
+        g = torch.randn(200, D, device=dev, generator=gen)
+        for _ in range(2):  # second pass reuses the pooled peer buffers
+            for p in m.parameters():
+                p.grad = None
+            y, dx, grads = _run(m, x, g)
+        torch.cuda.synchronize()
+        torch.save({"x": x.cpu(), "g": g.cpu(), "y": y.cpu(), "dx": dx.cpu(),
+                    "grads": {n: t.cpu() for n, t in grads.items()}}, f"{out}.{rank}.pt")
+        from mimir_b200.parallel.expert import expert_parallel
+        expert_parallel(E, dev).close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_expert_parallel_matches_single_process(tmp_path):
+    import torch.multiprocessing as mp
+    world = 2 if E % min(torch.cuda.device_count(), 8) else min(torch.cuda.device_count(), 8)
+    mp.spawn(_ep_rank, args=(world, _free_port(), str(tmp_path / "ep")), nprocs=world, join=True)
+    res = [torch.load(tmp_path / f"ep.{r}.pt") for r in range(world)]
+    dev = torch.device("cuda", 0)
+    full = _mixture(True).to(dev, torch.bfloat16)
+    x = torch.cat([r["x"] for r in res]).to(dev)
+    g = torch.cat([r["g"] for r in res]).to(dev)
+    y, dx, grads = _run(full, x, g)
+    T = res[0]["x"].shape[0]
+    for r in range(world):
+        torch.testing.assert_close(res[r]["y"], y[r * T:(r + 1) * T].cpu(), rtol=2e-2, atol=2e-2)
+        torch.testing.assert_close(res[r]["dx"], dx[r * T:(r + 1) * T].cpu(), rtol=2e-2, atol=2e-2)
+    local = E // world
+    for n, want in grads.items():
+        want = want.cpu()
+        if n.startswith("experts."):
+            got = res[int(n.split(".")[1]) // local]["grads"][n]
+        else:
+            got = sum(r["grads"][n] for r in res)
+        scale = want.abs().max().clamp_min(1e-6)
+        assert (got - want).abs().max() / scale < 3e-2, n
