@@ -325,6 +325,14 @@ def _save_unsharded_replicated(engine, train_state: TrainState, path: str, rank:
     model = {k: _full(v).cpu() for k, v in model_dcp_state(engine).items()}
     optim = train_state.optim.dcp_state()
     optim["state"] = {k: {n: _full(t).cpu() for n, t in slots.items()} for k, slots in optim["state"].items()}
+    local = [s.fqn for s in engine.slots if s.local]
+    if engine.world > 1 and local:  # expert-parallel parameters live on their owner rank only
+        mine = ({k: model[k] for k in local}, {k: optim["state"][k] for k in local if k in optim["state"]})
+        everyone = [None] * engine.world
+        dist.all_gather_object(everyone, mine, group=engine.group)
+        for m, o in everyone:
+            model.update(m)
+            optim["state"].update(o)
     if rank == 0:
         torch.save({"model": model, "optim": optim}, path)
 

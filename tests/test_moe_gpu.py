@@ -73,8 +73,10 @@ def test_grouped_path_matches_index_path():
     x = torch.randn(300, D, device=dev, generator=gen).to(torch.bfloat16)
     g = torch.randn(300, D, device=dev, generator=gen)
     a, b = _run(ref, x, g), _run(grp, x, g)
-    torch.testing.assert_close(b[0], a[0], rtol=2e-2, atol=2e-2)
-    torch.testing.assert_close(b[1], a[1], rtol=2e-2, atol=2e-2)
+    # bf16 sums in a different order (fp32 combine here, bf16 index_add there): compare against
+    # the tensor's scale
+    for name, u, v in (("y", b[0], a[0]), ("dx", b[1], a[1])):
+        assert (u - v).abs().max() / v.abs().max() < 2e-2, name
     for n in a[2]:
         scale = a[2][n].abs().max().clamp_min(1e-6)
         assert (b[2][n] - a[2][n]).abs().max() / scale < 3e-2, n
