@@ -33,6 +33,9 @@ MODEL = dict(n_layers=24, hidden_size=2048, num_heads=16, num_key_value_heads=4,
 # BASELINE config 3 (``--config moe``): 16 layers, d 2048, 64 experts top-2 of FFN 1408 plus one
 # shared expert, expert parallelism over the GPUs, aux-loss-free routing balance, Zipf(1.1) tokens.
 MOE = dict(n_layers=16, experts=64, top_k=2, expert_ffn=1408, shared=1, zipf=1.1)
+# Router rows are random-initialised in both arms (the reference's zero rows would send every
+# token to experts 0 and 1, whatever the data): normal with std 1/sqrt(d).
+ROUTER_STD = 2048 ** -0.5
 CONFIG = {"name": "dense"}  # set from --config in main()
 METRIC = "train tokens/sec (box, device-timed, max over ranks) at 1/2/4/8 B200; MFU"
 BASELINE_VALUE = None  # the reference publishes no throughput number
@@ -53,7 +56,7 @@ def arch_dict(kv_heads=4, reference=False):
             # its multiple-of-256 rounding turns into 1536.
             return base | dict(expansion=1.03125)
         return base | dict(moe_expert_intermediate_size=MOE["expert_ffn"], moe_shared_experts=MOE["shared"],
-                           moe_dispatch="grouped", moe_expert_parallel=True)
+                           moe_dispatch="grouped", moe_expert_parallel=True, moe_router_init_std=ROUTER_STD)
     return _arch_base(kv_heads)
 
 
@@ -338,6 +341,12 @@ def run_reference(args, rank, world, local):
     torch.manual_seed(0)
     with torch.device(device):
         model = RefHead(RefMimir2(model_cfg), model_cfg)
+    if CONFIG["name"] == "moe":  # random router rows, as in our arm (the reference initialises zeros)
+        gen = torch.Generator(device=device).manual_seed(1234)
+        with torch.no_grad():
+            for name, p in model.named_parameters():
+                if ".router.rows." in name:
+                    p.normal_(0.0, ROUTER_STD, generator=gen)
     for buf in model.buffers():
         dist.broadcast(buf, src=0)
     for module in fsdp_wrap_modules(model, "transformer_block"):

@@ -29,7 +29,7 @@ from mimir_b200.models.transformer import TransformerBlock
 
 class TopKRouter(nn.Module):
     def __init__(self, hidden_size, n, k, *, freeze_base=False, top1_straight_through=True,
-                 balance_enabled=False, balance_update_rate=0.001):
+                 balance_enabled=False, balance_update_rate=0.001, init_std=None):
         super().__init__()
         if not 1 <= k <= n:
             raise ValueError("Routing requires 1 <= k <= n")
@@ -43,6 +43,10 @@ class TopKRouter(nn.Module):
                                       for i in range(n)])
         self.biases = nn.ParameterList([nn.Parameter(torch.zeros(1), requires_grad=not (freeze_base and i == 0))
                                         for i in range(n)])
+        if init_std is not None:  # from-scratch MoE: random rows (zeros route every token to experts 0..k-1)
+            with torch.no_grad():
+                for row in self.rows:
+                    row.normal_(0.0, init_std)
         self.register_buffer("logit_bias", torch.zeros(n))
 
     def _apply(self, fn, recurse=True):
@@ -101,7 +105,7 @@ class MLPMixture(nn.Module):
 
     def __init__(self, mlp, hidden_size, n, k, *, freeze_base=False, top1_straight_through=True, sparse=False,
                  balance_enabled=False, balance_update_rate=0.001, expert_intermediate_size=None, shared_experts=0,
-                 grouped=False, expert_parallel=False):
+                 grouped=False, expert_parallel=False, router_init_std=None):
         super().__init__()
         if expert_intermediate_size is None:
             make = lambda i: mlp if i == 0 else copy.deepcopy(mlp)  # noqa: E731
@@ -110,7 +114,7 @@ class MLPMixture(nn.Module):
             make = lambda i: SwiGLU(hidden_size, expert_intermediate_size)  # noqa: E731
         self.router = TopKRouter(hidden_size, n, k, freeze_base=freeze_base,
                                  top1_straight_through=top1_straight_through, balance_enabled=balance_enabled,
-                                 balance_update_rate=balance_update_rate)
+                                 balance_update_rate=balance_update_rate, init_std=router_init_std)
         self.sparse, self.grouped, self.k, self.n = sparse, grouped or expert_parallel, k, n
         self.expert_parallel = expert_parallel
         if expert_parallel:

@@ -66,6 +66,7 @@ class Mimir2Config(RecurrentConfig):
     moe_expert_intermediate_size: Optional[int] = Field(default=None, ge=8)
     moe_shared_experts: int = Field(default=0, ge=0)
     moe_dispatch: Literal["index", "grouped"] = "index"
+    moe_router_init_std: Optional[float] = Field(default=None, gt=0)  # None: zero rows (reference init)
     moe_expert_parallel: bool = False
     mos_sparse: bool = False
     mos_sparse_routing: Literal["first_token", "prefix_mean"] = "first_token"
@@ -186,7 +187,8 @@ class Mimir2(RecurrentBackbone):
                                      balance_update_rate=config.routing_bias_update_rate,
                                      expert_intermediate_size=config.moe_expert_intermediate_size,
                                      shared_experts=config.moe_shared_experts, grouped=config.moe_dispatch == "grouped",
-                                     expert_parallel=config.moe_expert_parallel, **router_opts)
+                                     expert_parallel=config.moe_expert_parallel,
+                                     router_init_std=config.moe_router_init_std, **router_opts)
                 if config.moe_num_experts > 1:
                     norm = config.H_override.get("norm_type", config.norm_type) if name == "H" else config.norm_type
                     level.core.layers = nn.ModuleList(RoutedBlock(b, norm) for b in level.core.layers)

@@ -111,19 +111,33 @@ def _expert_forward(xp, expert_rows, weights, y=None):
     return y, gus
 
 
+def _weight_grad(w, a, b):
+    """Gradient ``a @ b`` of weight ``w``.  When the replicated engine owns ``w.grad`` (a view into
+    its flat buffer, with a ``_mimir_grad_sink`` callback), the GEMM accumulates into it in place
+    (one read of the old gradient instead of a temporary plus an add) and autograd gets None;
+    ``a is None`` means a zero gradient."""
+    sink = getattr(w, "_mimir_grad_sink", None)
+    if sink is not None and w.grad is not None:
+        if a is not None:
+            w.grad.addmm_(a, b)
+        sink(w)
+        return None
+    return torch.zeros_like(w) if a is None else (a @ b).to(w.dtype)
+
+
 def _expert_backward(dy, xp, gus, expert_rows, weights, dxp):
     grads, s = [], 0
     for i, n in enumerate(expert_rows):
         gu_w, dn_w = weights[2 * i], weights[2 * i + 1]
         if n:
             gu = gus[i]
-            d_dn = dy[s:s + n].t() @ _swiglu_fwd(gu)
+            d_dn = _weight_grad(dn_w, dy[s:s + n].t(), _swiglu_fwd(gu))
             dgu = _swiglu_bwd(gu, dy[s:s + n] @ dn_w)
-            d_gu = dgu.t() @ xp[s:s + n]
+            d_gu = _weight_grad(gu_w, dgu.t(), xp[s:s + n])
             torch.matmul(dgu, gu_w, out=dxp[s:s + n])
         else:  # every expert gets a gradient (zero) so all ranks update the same parameters
-            d_gu, d_dn = torch.zeros_like(gu_w), torch.zeros_like(dn_w)
-        grads += [d_gu.to(gu_w.dtype), d_dn.to(dn_w.dtype)]
+            d_gu, d_dn = _weight_grad(gu_w, None, None), _weight_grad(dn_w, None, None)
+        grads += [d_gu, d_dn]
         s += n
     return grads
 

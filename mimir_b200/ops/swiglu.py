@@ -24,7 +24,7 @@ class _SwiGLUFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dp):
         (gu2,) = ctx.saved_tensors
-        dgu = ext().swiglu_bwd(dp.reshape(gu2.shape[0], -1).contiguous(), gu2)
+        dgu = ext().swiglu_bwd(dp.reshape(gu2.shape[0], gu2.shape[1] // 2).contiguous(), gu2)
         return dgu.view(ctx.shape)
 
 

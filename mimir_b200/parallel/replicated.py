@@ -104,6 +104,8 @@ class ReplicatedEngine:
         for s in self.slots:
             if s.trainable:
                 s.param.register_post_accumulate_grad_hook(lambda _p, fqn=s.fqn: self.touched.add(fqn))
+                # Ops that accumulate straight into the gradient view report it here instead.
+                s.param._mimir_grad_sink = lambda _p, fqn=s.fqn: self.touched.add(fqn)
 
     # ------------------------------------------------------------------ setup
     @torch.no_grad()
