@@ -112,9 +112,6 @@ class MLPMixture(nn.Module):
         else:
             from mimir_b200.models.layers import SwiGLU
             make = lambda i: SwiGLU(hidden_size, expert_intermediate_size)  # noqa: E731
-        self.router = TopKRouter(hidden_size, n, k, freeze_base=freeze_base,
-                                 top1_straight_through=top1_straight_through, balance_enabled=balance_enabled,
-                                 balance_update_rate=balance_update_rate, init_std=router_init_std)
         self.sparse, self.grouped, self.k, self.n = sparse, grouped or expert_parallel, k, n
         self.expert_parallel = expert_parallel
         if expert_parallel:
@@ -133,6 +130,10 @@ class MLPMixture(nn.Module):
         else:
             self.experts = nn.ModuleList([make(i) for i in range(n)])
             self.expert_ids = list(range(n))
+        # registered after the experts: the reference's parameter (and state_dict) order
+        self.router = TopKRouter(hidden_size, n, k, freeze_base=freeze_base,
+                                 top1_straight_through=top1_straight_through, balance_enabled=balance_enabled,
+                                 balance_update_rate=balance_update_rate, init_std=router_init_std)
         width = expert_intermediate_size if expert_intermediate_size is not None else None
         if shared_experts:
             from mimir_b200.models.layers import SwiGLU
