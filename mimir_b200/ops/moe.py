@@ -7,6 +7,8 @@ per-expert counts in a single host transfer.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 
@@ -49,6 +51,14 @@ def _swiglu_bwd(gu: torch.Tensor, dp: torch.Tensor) -> torch.Tensor:
     dgate = dp.float() * up * sig * (1 + gate * (1 - sig))
     dup = dp.float() * gate * sig
     return torch.cat([dgate, dup], dim=-1).to(gu.dtype)
+
+
+def _split_rows(t, expert_rows):
+    out, s = [], 0
+    for n in expert_rows:
+        out.append(t[s:s + n])
+        s += n
+    return out
 
 
 class _Exchange:
@@ -95,9 +105,30 @@ class _Exchange:
         return out
 
 
-def _expert_forward(xp, expert_rows, weights, y=None):
-    """Per local expert: ``y = down(swiglu(x @ gate_up^T))`` on its contiguous rows."""
+def _grouped_kernel_ok(xp, weights) -> bool:
+    from mimir_b200.ops._ext import kernels_enabled
+    if not (kernels_enabled(xp) and xp.dtype == torch.bfloat16 and os.environ.get("MIMIR_MOE_CUBLAS") != "1"):
+        return False
+    gu, dn = weights[0], weights[1]
+    d, f2 = xp.shape[1], gu.shape[0]
+    return (d % 128 == 0 and f2 % 128 == 0 and (f2 // 2) % 64 == 0 and len(weights) // 2 <= 256
+            and all(w.is_contiguous() for w in weights))
+
+
+def _expert_forward(xp, expert_rows, weights, y=None, rows_dev=None):
+    """Per local expert: ``y = down(swiglu(x @ gate_up^T))`` on its contiguous rows.
+
+    CUDA: two launches of the tcgen05 grouped GEMM (``csrc/grouped_gemm.cu``) for all experts,
+    with the SwiGLU kernel in between; returns the packed ``[gate | up]`` projections of all rows
+    (one tensor).  Otherwise one GEMM pair per expert; returns the per-expert projections."""
     y = torch.empty_like(xp) if y is None else y
+    if rows_dev is not None and _grouped_kernel_ok(xp, weights):
+        from mimir_b200.ops._ext import ext
+        C = ext()
+        gu = torch.empty(xp.shape[0], weights[0].shape[0], dtype=xp.dtype, device=xp.device)
+        C.grouped_gemm(xp, list(weights[0::2]), rows_dev, gu, False)
+        C.grouped_gemm(ext().swiglu_fwd(gu), list(weights[1::2]), rows_dev, y, False)
+        return y, gu
     gus, s = [], 0
     for i, n in enumerate(expert_rows):
         gu_w, dn_w = weights[2 * i], weights[2 * i + 1]
@@ -125,7 +156,9 @@ def _weight_grad(w, a, b):
     return torch.zeros_like(w) if a is None else (a @ b).to(w.dtype)
 
 
-def _expert_backward(dy, xp, gus, expert_rows, weights, dxp):
+def _expert_backward(dy, xp, gus, expert_rows, weights, dxp, rows_dev=None):
+    if torch.is_tensor(gus):  # forward ran the grouped kernel: input gradients grouped too
+        return _expert_backward_grouped(dy, xp, gus, expert_rows, weights, dxp, rows_dev)
     grads, s = [], 0
     for i, n in enumerate(expert_rows):
         gu_w, dn_w = weights[2 * i], weights[2 * i + 1]
@@ -136,6 +169,30 @@ def _expert_backward(dy, xp, gus, expert_rows, weights, dxp):
             d_gu = _weight_grad(gu_w, dgu.t(), xp[s:s + n])
             torch.matmul(dgu, gu_w, out=dxp[s:s + n])
         else:  # every expert gets a gradient (zero) so all ranks update the same parameters
+            d_gu, d_dn = _weight_grad(gu_w, None, None), _weight_grad(dn_w, None, None)
+        grads += [d_gu, d_dn]
+        s += n
+    return grads
+
+
+def _expert_backward_grouped(dy, xp, gu, expert_rows, weights, dxp, rows_dev):
+    """Input gradients with the grouped kernel ("nn": ``dact = dy @ W_down``, ``dx = dgu @ W_gate_up``),
+    one SwiGLU-backward launch for all rows; weight gradients per expert (cuBLAS)."""
+    from mimir_b200.ops._ext import ext
+    C = ext()
+    rows = dy.shape[0]
+    dact = torch.empty(rows, gu.shape[1] // 2, dtype=dy.dtype, device=dy.device)
+    C.grouped_gemm(dy, list(weights[1::2]), rows_dev, dact, True)
+    dgu = C.swiglu_bwd(dact, gu)
+    C.grouped_gemm(dgu, list(weights[0::2]), rows_dev, dxp, True)
+    act = C.swiglu_fwd(gu)
+    grads, s = [], 0
+    for i, n in enumerate(expert_rows):
+        gu_w, dn_w = weights[2 * i], weights[2 * i + 1]
+        if n:
+            d_dn = _weight_grad(dn_w, dy[s:s + n].t(), act[s:s + n])
+            d_gu = _weight_grad(gu_w, dgu[s:s + n].t(), xp[s:s + n])
+        else:
             d_gu, d_dn = _weight_grad(gu_w, None, None), _weight_grad(dn_w, None, None)
         grads += [d_gu, d_dn]
         s += n
@@ -157,7 +214,8 @@ class _GroupedExpertsFn(torch.autograd.Function):
             C.moe_dispatch(x.contiguous(), plan.rows, plan.dst, buf.peer_ptrs(0, d), k)
             ep.barrier()  # every rank's rows have landed in their owners' buffers
             xp = buf.view(0, ex.rows_in, d)
-            _, gus = _expert_forward(xp, plan.expert_rows, weights, buf.view(plan.capacity, ex.rows_in, d))
+            _, gus = _expert_forward(xp, plan.expert_rows, weights, buf.view(plan.capacity, ex.rows_in, d),
+                                     plan.expert_rows_dev)
             ep.barrier()  # every owner's outputs are in place
             out = C.moe_combine(buf.peer_ptrs(plan.capacity, d), plan.rows, plan.dst, w32, T, k, d)
             if not keep:  # no backward: the next exchange's collective orders any reuse of the buffer
@@ -192,7 +250,7 @@ class _GroupedExpertsFn(torch.autograd.Function):
             ep.barrier()  # the scaled output gradients have reached their owners
             dy = gbuf.view(0, ex.rows_in, d)
             dxp = gbuf.view(plan.capacity, ex.rows_in, d)
-            grads = _expert_backward(dy, ctx.xp, ctx.gus, plan.expert_rows, weights, dxp)
+            grads = _expert_backward(dy, ctx.xp, ctx.gus, plan.expert_rows, weights, dxp, plan.expert_rows_dev)
             ep.barrier()  # every owner's input gradients are in place
             dx = C.moe_combine(gbuf.peer_ptrs(plan.capacity, d), plan.rows, plan.dst, None, T, k, d)
             ep.release(gbuf)

@@ -33,6 +33,7 @@ class RoutePlan:
     send_counts: list       # rows this rank sends to each rank
     recv_counts: list       # rows this rank receives from each rank
     expert_rows: list       # rows per local expert (receive side, in buffer order)
+    expert_rows_dev: Tensor  # the same, int32 on the device (for kernels that schedule on the device)
     capacity: int           # max rows any rank of the group receives
     order: Tensor           # token-slot indices sorted by (expert, token): the send order
     counts: Tensor          # host int64 [W, E]: rows every source rank routes to every expert
@@ -148,13 +149,14 @@ class ExpertParallel:
         within = torch.arange(flat.numel(), device=flat.device) - start[sorted_e]
         rows = torch.empty_like(flat)
         rows[order] = base[sorted_e] + src_off[sorted_e] + within
+        rows_dev = C.sum(0).view(W, L)[self.rank].to(torch.int32)
         host = C.cpu()
         recv_rows = host.sum(0).view(W, L)
         expert_rows = recv_rows[self.rank].tolist()
         send = host[self.rank].view(W, L).sum(1).tolist()
         recv = host.view(W, W, L)[:, self.rank].sum(1).tolist()
         return RoutePlan(rows=rows.view(T, k).to(torch.int32), dst=(flat // L).view(T, k).to(torch.int32),
-                         send_counts=send, recv_counts=recv, expert_rows=expert_rows,
+                         send_counts=send, recv_counts=recv, expert_rows=expert_rows, expert_rows_dev=rows_dev,
                          capacity=int(recv_rows.sum(1).max()), order=order, counts=host)
 
 

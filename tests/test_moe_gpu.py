@@ -136,3 +136,26 @@ def test_expert_parallel_matches_single_process(tmp_path):
             got = sum(r["grads"][n] for r in res)
         scale = want.abs().max().clamp_min(1e-6)
         assert (got - want).abs().max() / scale < 3e-2, n
+
+
+@pytest.mark.parametrize("b_kn", [False, True])
+@pytest.mark.parametrize("N,K", [(256, 128), (384, 192), (2816, 2048), (1408, 2048), (2048, 2816)])
+def test_grouped_gemm_matches_fp32(N, K, b_kn):
+    from mimir_b200.ops._ext import ext
+    C = ext()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(N + K)
+    counts = [130, 0, 1, 257, 64, 0, 300, 5]
+    R = sum(counts)
+    a = torch.randn(R, K, device=dev, generator=g).to(torch.bfloat16)
+    shape = (K, N) if b_kn else (N, K)
+    bs = [(torch.randn(*shape, device=dev, generator=g) / K ** 0.5).to(torch.bfloat16) for _ in counts]
+    out = torch.full((R, N), float("nan"), device=dev, dtype=torch.bfloat16)
+    C.grouped_gemm(a, bs, torch.tensor(counts, dtype=torch.int32, device=dev), out, b_kn)
+    torch.cuda.synchronize()
+    assert C.grouped_gemm_status(0) == 0
+    s = 0
+    for n, b in zip(counts, bs):
+        want = a[s:s + n].float() @ (b.float() if b_kn else b.float().t())
+        torch.testing.assert_close(out[s:s + n].float(), want, rtol=2e-2, atol=2e-2)
+        s += n
