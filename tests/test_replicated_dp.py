@@ -100,13 +100,14 @@ BASE = ["size@arch=XXS", "accelerator_type=cpu", "fwd_bwd_dtype=float32", "globa
         "arch.L_cycles=2", "dataloader_prefetch_factor=2"]
 
 
-def test_replicated_training_resumes_exactly_and_matches_plain(tmp_path):
+@pytest.mark.parametrize("optimizer", ["adam_atan2", "muon"])
+def test_replicated_training_resumes_exactly_and_matches_plain(tmp_path, optimizer):
     from mimir_b200.config.schema import load_config
     from mimir_b200.data.synthetic import write_corpus
     from mimir_b200.train.loop import launch
     from test_train_resume import _same_state, _tensors
     data = write_corpus(str(tmp_path / "d"), rows=64, seq_len=32, vocab=64)
-    common = BASE + [f"data.path={data}"]
+    common = BASE + [f"data.path={data}", f"optimizer={optimizer}"]
     launch(load_config(common + ["distributed_strategy=none", f"checkpoint_path={tmp_path / 'plain'}",
                                  "stop_after_step=6"]))
     launch(load_config(common + ["distributed_strategy=replicated", f"checkpoint_path={tmp_path / 'rep'}",
