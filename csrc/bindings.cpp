@@ -69,6 +69,7 @@ at::Tensor moe_combine(std::vector<int64_t> y, at::Tensor rows, at::Tensor dst, 
 at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::Tensor dst, std::vector<int64_t> y,
                            std::vector<int64_t> dy, int64_t k);
 void grouped_gemm(at::Tensor a, std::vector<at::Tensor> bs, at::Tensor counts, at::Tensor out, bool b_kn);
+void grouped_wgrad(at::Tensor a, at::Tensor b, std::vector<int64_t> rows, std::vector<at::Tensor> grads);
 int64_t grouped_gemm_status(int64_t device);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -106,6 +107,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine);
   m.def("moe_combine_bwd", &moe_combine_bwd);
   m.def("grouped_gemm", &grouped_gemm);
+  m.def("grouped_wgrad", &grouped_wgrad);
   m.def("grouped_gemm_status", &grouped_gemm_status);
   m.def("fmha_bwd", &fmha_bwd, py::arg("q_src"), py::arg("q_col"), py::arg("k_src"), py::arg("k_col"),
         py::arg("v_src"), py::arg("v_col"), py::arg("d_o"), py::arg("lse"), py::arg("delta"), py::arg("H"),

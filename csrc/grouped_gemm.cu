@@ -28,6 +28,7 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -290,6 +291,158 @@ void launch(const CUtensorMap& ma, const at::Tensor& maps, const at::Tensor& cou
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ---------------------------------------------------------------------------------------------
+// Weight gradients: for every group g,  W_g[m, n] += sum_{r in g} A[r, m] * B[r, n]
+// (A = the output gradient rows of the group, B = the input rows).  The reduction runs over the
+// group's rows, so each group has its own pair of TMA maps whose row extent is the group's row
+// count: the tail k-block reads zeros past the group's end (TMA out-of-bounds fill) instead of
+// the next group's rows.  Both operands are MN-major tiles ([64 rows x 64 columns] chunks); the
+// epilogue adds the fp32 accumulator to the bf16 weight gradient in place.
+struct WgradGroup {
+  CUtensorMap a;     // [rows_g, M] window of A
+  CUtensorMap b;     // [rows_g, N] window of B
+  uint64_t out;      // W_g gradient, contiguous bf16 [M, N]
+  int32_t kblocks;   // ceil(rows_g / 64)
+  int32_t pad[13];
+};
+static_assert(sizeof(WgradGroup) % 64 == 0, "tensor maps must stay 64-byte aligned");
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) grouped_wgrad_kernel(const WgradGroup* __restrict__ groups, int G,
+                                                                      int M, int N, int* status) {
+  using CF = Cfg<BN>;
+  constexpr int kABytes = kBK * kBM * 2;  // [64 rows x 128 m] as two 64-column chunks
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ Bars bars;
+  Bars* bar = &bars;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < CF::kStages; ++s) {
+      mbar_init(&bar->full[s], 1);
+      mbar_init(&bar->empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->acc_full[i], 1);
+      mbar_init(&bar->acc_empty[i], 4);
+    }
+    mbar_init(&bar->done, 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bar->tmem_base, CF::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+  const int ntm = M / kBM, ntn = N / BN;
+  const int per_group = ntm * ntn;
+  const int total = G * per_group;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        const WgradGroup* gr = groups + t / per_group;
+        const int m0 = ((t % per_group) / ntn) * kBM, n0 = (t % ntn) * BN;
+        for (int kb = 0; kb < gr->kblocks; ++kb, ++it) {
+          const int s = it % CF::kStages;
+          if (it >= CF::kStages &&
+              !mbar_wait(&bar->empty[s], ((it / CF::kStages) - 1) & 1, status, kStatusTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * CF::kStageBytes;
+          mbar_arrive_expect_tx(&bar->full[s], CF::kStageBytes);
+#pragma unroll
+          for (int c = 0; c < kBM / 64; ++c) tma_load_2d(sa + c * (kBK * 128), &gr->a, &bar->full[s], m0 + c * 64, kb * kBK);
+#pragma unroll
+          for (int c = 0; c < BN / 64; ++c)
+            tma_load_2d(sa + kABytes + c * (kBK * 128), &gr->b, &bar->full[s], n0 + c * 64, kb * kBK);
+        }
+      }
+      for (int j = max(0, it - CF::kStages); j < it; ++j)
+        mbar_wait(&bar->full[j % CF::kStages], (j / CF::kStages) & 1, status, kStatusTimeoutKV);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kBM, BN, 1, 1);
+      int it = 0, i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++i) {
+        const int buf = i & 1;
+        const int nkb = groups[t / per_group].kblocks;
+        if (i >= 2 && !mbar_wait(&bar->acc_empty[buf], ((i >> 1) - 1) & 1, status, kStatusTimeoutO)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * BN;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % CF::kStages;
+          if (!mbar_wait(&bar->full[s], (it / CF::kStages) & 1, status, kStatusTimeoutKV)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * CF::kStageBytes);
+          const uint32_t sb = sa + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_bf16_ss(acc, smem_desc(sa + kk * 2048, kBK * 128, 1024, kLayoutSW128),
+                        smem_desc(sb + kk * 2048, kBK * 128, 1024, kLayoutSW128), idesc, (kb | kk) != 0 ? 1u : 0u);
+          mma_commit(&bar->empty[s]);
+        }
+        if (ok) mma_commit(&bar->acc_full[buf]);
+      }
+      mma_commit(&bar->done);
+      mbar_wait(&bar->done, 0, status, kStatusTimeoutOther);
+    }
+  } else {
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    int i = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
+      const int buf = i & 1;
+      if (!warp_wait(&bar->acc_full[buf], (i >> 1) & 1, status, kStatusTimeoutS)) break;
+      tc_fence_after();
+      const WgradGroup* gr = groups + t / per_group;
+      const int m0 = ((t % per_group) / ntn) * kBM, n0 = (t % ntn) * BN;
+      __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(gr->out) + int64_t(m0 + r) * N + n0;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem + lane_off + buf * BN + c * 32, v);
+        uint4* dst = reinterpret_cast<uint4*>(row + c * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 old = dst[q];
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&old);
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            o[2 * e] = f.x + v[8 * q + 2 * e];
+            o[2 * e + 1] = f.y + v[8 * q + 2 * e + 1];
+          }
+          dst[q] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                              pack_bf16x2(o[6], o[7]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->acc_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, CF::kTmemCols);
+  }
+}
+
 }  // namespace
 
 // out[rows, :N] = a[rows, :K] @ b_g^T ("nt": b_g is [N, K]) or a[rows, :K] @ b_g ("nn": b_g is
@@ -326,6 +479,63 @@ void grouped_gemm(at::Tensor a, std::vector<at::Tensor> bs, at::Tensor counts, a
     if (b_kn) launch<128, true>(ma, maps, counts, G, out, N, K, status, st, sms);
     else launch<128, false>(ma, maps, counts, G, out, N, K, status, st, sms);
   }
+}
+
+
+// grads[g] += a_g^T @ b_g for the row blocks given by the host list `rows` (a: [R, M], b: [R, N],
+// bf16, rows grouped in order; grads: contiguous bf16 [M, N]).  Groups without rows are skipped.
+void grouped_wgrad(at::Tensor a, at::Tensor b, std::vector<int64_t> rows, std::vector<at::Tensor> grads) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.dtype() == at::kBFloat16 && b.dtype() == at::kBFloat16 && a.dim() == 2 &&
+                  b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1 && a.size(0) == b.size(0),
+              "a, b: bf16 [R, M], [R, N] with unit column stride");
+  TORCH_CHECK(rows.size() == grads.size(), "one row count per gradient");
+  const int64_t M = a.size(1), N = b.size(1);
+  TORCH_CHECK(M % kBM == 0 && N % 128 == 0, "M must be a multiple of 128 and N of 128");
+  TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0, "row strides must be 16-byte multiples");
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int BN = N % 256 == 0 ? 256 : 128;
+  std::vector<WgradGroup> host;
+  int64_t row = 0;
+  for (size_t g = 0; g < rows.size(); ++g) {
+    const auto& w = grads[g];
+    TORCH_CHECK(w.is_cuda() && w.dtype() == at::kBFloat16 && w.is_contiguous() && w.size(0) == M && w.size(1) == N,
+                "gradient ", g, ": contiguous bf16 [M, N]");
+    const int64_t n = rows[g];
+    if (n > 0) {
+      WgradGroup gr{};
+      const auto* ab = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr()) + row * a.stride(0);
+      const auto* bb = reinterpret_cast<const __nv_bfloat16*>(b.data_ptr()) + row * b.stride(0);
+      gr.a = make_tmap_bf16_2d(ab, n, M, a.stride(0), 64, kBK);
+      gr.b = make_tmap_bf16_2d(bb, n, N, b.stride(0), 64, kBK);
+      gr.out = reinterpret_cast<uint64_t>(w.data_ptr());
+      gr.kblocks = static_cast<int32_t>((n + kBK - 1) / kBK);
+      host.push_back(gr);
+    }
+    row += n;
+  }
+  TORCH_CHECK(row <= a.size(0), "row counts exceed the buffers");
+  if (host.empty()) return;
+  const int64_t nbytes = static_cast<int64_t>(host.size() * sizeof(WgradGroup));
+  at::Tensor pinned = at::empty({nbytes}, at::TensorOptions().dtype(at::kByte).pinned_memory(true));
+  std::memcpy(pinned.data_ptr(), host.data(), nbytes);
+  at::Tensor dev = pinned.to(at::TensorOptions().device(a.device()), /*non_blocking=*/true);
+  int sms = 0;
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, a.device().index()));
+  auto st = at::cuda::getCurrentCUDAStream();
+  int* status = status_word(a.device());
+  const int G = static_cast<int>(host.size());
+  auto go = [&](auto kernel, int smem) {
+    static bool attr = false;
+    if (!attr) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      attr = true;
+    }
+    kernel<<<sms, kThreads, smem, st>>>(reinterpret_cast<const WgradGroup*>(dev.data_ptr()), G,
+                                        static_cast<int>(M), static_cast<int>(N), status);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  };
+  if (BN == 256) go(grouped_wgrad_kernel<256>, Cfg<256>::kSmem);
+  else go(grouped_wgrad_kernel<128>, Cfg<128>::kSmem);
 }
 
 int64_t grouped_gemm_status(int64_t device) {

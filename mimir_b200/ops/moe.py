@@ -177,7 +177,8 @@ def _expert_backward(dy, xp, gus, expert_rows, weights, dxp, rows_dev=None):
 
 def _expert_backward_grouped(dy, xp, gu, expert_rows, weights, dxp, rows_dev):
     """Input gradients with the grouped kernel ("nn": ``dact = dy @ W_down``, ``dx = dgu @ W_gate_up``),
-    one SwiGLU-backward launch for all rows; weight gradients per expert (cuBLAS)."""
+    one SwiGLU-backward launch for all rows, and the weight gradients with the grouped
+    weight-gradient kernel (reduction over each expert's rows)."""
     from mimir_b200.ops._ext import ext
     C = ext()
     rows = dy.shape[0]
@@ -186,17 +187,22 @@ def _expert_backward_grouped(dy, xp, gu, expert_rows, weights, dxp, rows_dev):
     dgu = C.swiglu_bwd(dact, gu)
     C.grouped_gemm(dgu, list(weights[0::2]), rows_dev, dxp, True)
     act = C.swiglu_fwd(gu)
-    grads, s = [], 0
-    for i, n in enumerate(expert_rows):
-        gu_w, dn_w = weights[2 * i], weights[2 * i + 1]
-        if n:
-            d_dn = _weight_grad(dn_w, dy[s:s + n].t(), act[s:s + n])
-            d_gu = _weight_grad(gu_w, dgu[s:s + n].t(), xp[s:s + n])
+    # Weight gradients, one grouped launch per projection, accumulated in place: into the
+    # engine's gradient views when it owns them, else into fresh zero tensors handed to autograd.
+    targets, out = [], []
+    for w in weights:
+        sink = getattr(w, "_mimir_grad_sink", None)
+        if sink is not None and w.grad is not None:
+            sink(w)
+            targets.append(w.grad)
+            out.append(None)
         else:
-            d_gu, d_dn = _weight_grad(gu_w, None, None), _weight_grad(dn_w, None, None)
-        grads += [d_gu, d_dn]
-        s += n
-    return grads
+            z = torch.zeros_like(w)
+            targets.append(z)
+            out.append(z)
+    C.grouped_wgrad(dy, act, list(expert_rows), targets[1::2])
+    C.grouped_wgrad(dgu, xp, list(expert_rows), targets[0::2])
+    return out
 
 
 class _GroupedExpertsFn(torch.autograd.Function):

@@ -159,3 +159,25 @@ def test_grouped_gemm_matches_fp32(N, K, b_kn):
         want = a[s:s + n].float() @ (b.float() if b_kn else b.float().t())
         torch.testing.assert_close(out[s:s + n].float(), want, rtol=2e-2, atol=2e-2)
         s += n
+
+
+@pytest.mark.parametrize("M,N", [(256, 128), (2816, 2048), (2048, 1408)])
+def test_grouped_wgrad_accumulates_fp32_products(M, N):
+    from mimir_b200.ops._ext import ext
+    C = ext()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(M + N)
+    rows = [70, 0, 129, 1, 64, 200]
+    R = sum(rows) + 17  # trailing rows that belong to no group
+    a = torch.randn(R, M, device=dev, generator=g).to(torch.bfloat16)
+    b = torch.randn(R, N, device=dev, generator=g).to(torch.bfloat16)
+    grads = [torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16) for _ in rows]
+    before = [w.float().clone() for w in grads]
+    C.grouped_wgrad(a, b, rows, grads)
+    torch.cuda.synchronize()
+    assert C.grouped_gemm_status(0) == 0
+    s = 0
+    for n, w, w0 in zip(rows, grads, before):
+        want = w0 + a[s:s + n].float().t() @ b[s:s + n].float()
+        assert (w.float() - want).abs().max() / want.abs().max() < 1e-2
+        s += n
