@@ -178,3 +178,46 @@ def test_replicated_engine_keeps_expert_parallel_parameters_local(tmp_path):
     for e in range(E):
         torch.testing.assert_close(full[f"model.mix.experts.{e}.down_proj.weight"],
                                    want[f"mix.experts.{e}.down_proj.weight"], rtol=1e-5, atol=1e-6)
+
+
+# ------------------------------------------------------------------ EP training: checkpoint + exact resume
+def _launch_worker(rank, world, port, overrides):
+    import os
+    os.environ.update(RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE=str(world), LOCAL_WORLD_SIZE=str(world),
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from mimir_b200.config.schema import load_config
+    from mimir_b200.train.loop import launch
+    try:
+        launch(load_config(overrides))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _free_port():
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_expert_parallel_training_resumes_exactly(tmp_path):
+    from mimir_b200.data.synthetic import write_corpus
+    from test_replicated_dp import BASE
+    from test_train_resume import _same_state, _tensors
+    data = write_corpus(str(tmp_path / "d"), rows=64, seq_len=32, vocab=64)
+    common = BASE + [f"data.path={data}", "distributed_strategy=replicated", "arch.moe_num_experts=4",
+                     "arch.moe_top_k=2", "arch.moe_sparse=true", "arch.moe_dispatch=grouped",
+                     "arch.moe_expert_parallel=true", "arch.moe_expert_intermediate_size=32",
+                     "arch.moe_shared_experts=1", "arch.moe_aux_loss_free=true", "arch.moe_router_init_std=0.1"]
+    runs = [(tmp_path / "full", ["checkpoint_step_interval=3", "stop_after_step=6"]),
+            (tmp_path / "resumed", ["stop_after_step=6", f"resume_checkpoint_path={tmp_path / 'full'}",
+                                    "resume_checkpoint_tag=step_3"])]
+    for run, extra in runs:
+        mp.spawn(_launch_worker, args=(2, _free_port(), common + [f"checkpoint_path={run}", *extra]), nprocs=2,
+                 join=True)
+    _same_state(tmp_path / "full", tmp_path / "resumed", "step_6")
+    keys = set(_tensors(tmp_path / "full" / "step_6", "step_6"))
+    experts = {k for k in keys if ".mlp.experts." in k and k.startswith("model.")}
+    assert {k.split(".mlp.experts.")[1].split(".")[0] for k in experts} == {"0", "1", "2", "3"}
+    assert any(".mlp.shared_experts.0." in k for k in keys)
