@@ -288,12 +288,7 @@ def load_sharded_train_state(config, train_state: TrainState, tag: str) -> None:
     # DCP loads the requested subset only: refuse sources with modules this run disabled.
     stored = {k.removeprefix("model.") for k in dcp.FileSystemReader(ckpt).read_metadata().state_dict_metadata
               if k.startswith("model.")}
-    known = set(model_state)
-    if engine.world > 1 and any(s.local for s in engine.slots):  # other ranks own the other experts
-        everyone = [None] * engine.world
-        dist.all_gather_object(everyone, sorted(known), group=engine.group)
-        known = set().union(*map(set, everyone))
-    unexpected = stored - known
+    unexpected = stored - set(model_state)
     if unexpected:
         raise ValueError("Checkpoint contains disabled or mismatched v2 features; enable the original "
                          f"gates/experts/residual branches explicitly. Unexpected model keys: {sorted(unexpected)}")
