@@ -443,6 +443,21 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_wgrad_kernel(const WgradG
   }
 }
 
+// One launch of the weight-gradient kernel; the shared-memory attribute is set once per
+// instantiation (each BN has its own flag).
+template <int BN>
+void launch_wgrad(const WgradGroup* groups, int G, int64_t M, int64_t N, int* status, cudaStream_t st, int sms) {
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(grouped_wgrad_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Cfg<BN>::kSmem));
+    attr = true;
+  }
+  grouped_wgrad_kernel<BN><<<sms, kThreads, Cfg<BN>::kSmem, st>>>(groups, G, static_cast<int>(M), static_cast<int>(N),
+                                                                  status);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace
 
 // out[rows, :N] = a[rows, :K] @ b_g^T ("nt": b_g is [N, K]) or a[rows, :K] @ b_g ("nn": b_g is
@@ -524,18 +539,9 @@ void grouped_wgrad(at::Tensor a, at::Tensor b, std::vector<int64_t> rows, std::v
   auto st = at::cuda::getCurrentCUDAStream();
   int* status = status_word(a.device());
   const int G = static_cast<int>(host.size());
-  auto go = [&](auto kernel, int smem) {
-    static bool attr = false;
-    if (!attr) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      attr = true;
-    }
-    kernel<<<sms, kThreads, smem, st>>>(reinterpret_cast<const WgradGroup*>(dev.data_ptr()), G,
-                                        static_cast<int>(M), static_cast<int>(N), status);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-  };
-  if (BN == 256) go(grouped_wgrad_kernel<256>, Cfg<256>::kSmem);
-  else go(grouped_wgrad_kernel<128>, Cfg<128>::kSmem);
+  const auto* groups = reinterpret_cast<const WgradGroup*>(dev.data_ptr());
+  if (BN == 256) launch_wgrad<256>(groups, G, M, N, status, st, sms);
+  else launch_wgrad<128>(groups, G, M, N, status, st, sms);
 }
 
 int64_t grouped_gemm_status(int64_t device) {
