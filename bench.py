@@ -422,7 +422,8 @@ def emit(args, world, seconds, e2e_seconds, h2d_bytes, d2h_bytes, flops_per_step
                    "global_batch": SEQ_LEN * SEQS_PER_GPU * world, "seq_len": SEQ_LEN, "micro_batch": SEQS_PER_GPU,
                    "parallelism": (extra or {}).pop("parallelism", f"fsdp{world}"),
                    "mask": "prefix-LM, prompt length uniform [0,2048]",
-                   "optimizer": OPTIMIZER_LABEL[args.optimizer] + (" (no EMA)" if CONFIG["name"] == "moe" else ""),
+                   "optimizer": (OPTIMIZER_LABEL[args.optimizer].replace(" + EMA", "") + " (no EMA)") if CONFIG["name"] == "moe"
+                   else OPTIMIZER_LABEL[args.optimizer],
                    "l2": "inputs larger than L2 (weights+activations >> 126 MB)"},
         "mfu": round(achieved / 2.25e15, 4),
         "frac_of_measured_bf16": round(achieved / (peaks.get("bf16_tflops_sustained", 1422.4) * 1e12), 4),
