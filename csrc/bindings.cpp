@@ -71,6 +71,7 @@ at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::T
 void grouped_gemm(at::Tensor a, std::vector<at::Tensor> bs, at::Tensor counts, at::Tensor out, bool b_kn);
 void grouped_wgrad(at::Tensor a, at::Tensor b, std::vector<int64_t> rows, std::vector<at::Tensor> grads);
 int64_t grouped_gemm_status(int64_t device);
+at::Tensor router_topk(at::Tensor scores, int64_t k, c10::optional<at::Tensor> load);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mimir_b200 hand-written sm_100a kernels";
@@ -109,6 +110,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm", &grouped_gemm);
   m.def("grouped_wgrad", &grouped_wgrad);
   m.def("grouped_gemm_status", &grouped_gemm_status);
+  m.def("router_topk", &router_topk);
   m.def("fmha_bwd", &fmha_bwd, py::arg("q_src"), py::arg("q_col"), py::arg("k_src"), py::arg("k_col"),
         py::arg("v_src"), py::arg("v_col"), py::arg("d_o"), py::arg("lse"), py::arg("delta"), py::arg("H"),
         py::arg("KV"), py::arg("is_causal"), py::arg("cu_seqlens"), py::arg("prefix_lens"), py::arg("numseqs"),

@@ -66,7 +66,19 @@ class TopKRouter(nn.Module):
             s = s + logit_bias.float()
         return s
 
-    def forward(self, x, logit_bias=None):
+    def _select(self, selection):
+        """Top-k experts per token (stable: ties go to the lower index).  CUDA: one kernel that also
+        adds this forward's selections to the routing-balance counts (``csrc/router.cu``)."""
+        from mimir_b200.ops._ext import kernels_enabled
+        if kernels_enabled(selection) and self.n <= 256:
+            from mimir_b200.ops._ext import ext
+            from mimir_b200.optim.routing_balance import load_counter
+            load = load_counter(self) if self.balance_enabled else None
+            flat = selection.detach().reshape(-1, self.n).float().contiguous()
+            return ext().router_topk(flat, self.k, load).view(*selection.shape[:-1], self.k), True
+        return selection.argsort(dim=-1, descending=True, stable=True)[..., :self.k], False
+
+    def forward(self, x, logit_bias=None, return_indices=False):
         scores = self.scores(x, logit_bias)
         tiny = torch.finfo(torch.float32).tiny
         if self.balance_enabled:
@@ -74,9 +86,9 @@ class TopKRouter(nn.Module):
             selection = affinity + self.selection_bias.float()
         else:
             affinity = selection = scores
-        chosen = selection.argsort(dim=-1, descending=True, stable=True)[..., :self.k]
+        chosen, counted = self._select(selection)
         mask = torch.zeros_like(scores, dtype=torch.bool).scatter(-1, chosen, True)
-        if self.balance_enabled:
+        if self.balance_enabled and not counted:
             from mimir_b200.optim.routing_balance import record_load
             record_load(self, mask)
             weights = affinity * mask
@@ -88,7 +100,7 @@ class TopKRouter(nn.Module):
                 else scores.softmax(-1)
             surrogate = probs * mask
             weights = weights + (surrogate - surrogate.detach())
-        return weights
+        return (weights, chosen) if return_indices else weights
 
 
 class MLPMixture(nn.Module):
@@ -154,10 +166,10 @@ class MLPMixture(nn.Module):
         return out
 
     def forward(self, x, stability_diagnostics=None, stability_scope=None, routing_bias=None):
-        weights = self.router(x, routing_bias)
+        weights, chosen = self.router(x, routing_bias, return_indices=True)
         shared = self._shared(x, stability_diagnostics, stability_scope)
         if self.grouped and (stability_diagnostics is None or self.expert_parallel):
-            out = self._grouped(x, weights)
+            out = self._grouped(x, weights, chosen)
         elif self.sparse:
             out = self._dispatch(x, weights, stability_diagnostics, stability_scope)
         else:
@@ -169,12 +181,12 @@ class MLPMixture(nn.Module):
         return out if shared is None else out + shared
 
     @torch.compiler.disable
-    def _grouped(self, x, weights):
+    def _grouped(self, x, weights, chosen):
         from mimir_b200.ops.moe import grouped_experts
         from mimir_b200.parallel.expert import expert_parallel
         flat = x.reshape(-1, x.shape[-1])
-        w = weights.reshape(-1, self.n)
-        topw, topi = w.topk(self.k, dim=-1)
+        topi = chosen.reshape(-1, self.k)
+        topw = weights.reshape(-1, self.n).gather(-1, topi)
         ep = expert_parallel(self.n if self.expert_parallel else self.n, flat.device,
                              distributed=self.expert_parallel)
         params = []

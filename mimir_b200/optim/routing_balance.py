@@ -26,6 +26,15 @@ def record_load(router, mask):
         session.counts[router].add_(mask.detach().reshape(-1, router.n).sum(0))
 
 
+def load_counter(router):
+    """The int64 [n] count buffer a fused selection kernel may add this forward's selections to, or
+    None when nothing is being recorded (no balance step, eval mode, or an activation replay)."""
+    session = _ACTIVE.get()
+    if session is not None and router.training and torch._C._current_graph_task_id() == -1:
+        return session.counts[router]
+    return None
+
+
 class BalanceStep:
     def __init__(self, model):
         self.counts = {m: torch.zeros(m.n, dtype=torch.int64, device=m.selection_bias.device)

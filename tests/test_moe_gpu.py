@@ -181,3 +181,17 @@ def test_grouped_wgrad_accumulates_fp32_products(M, N):
         want = w0 + a[s:s + n].float().t() @ b[s:s + n].float()
         assert (w.float() - want).abs().max() / want.abs().max() < 1e-2
         s += n
+
+
+@pytest.mark.parametrize("E,k", [(8, 2), (64, 2), (64, 8), (256, 1)])
+def test_router_topk_matches_stable_argsort_and_counts(E, k):
+    from mimir_b200.ops._ext import ext
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(E * 10 + k)
+    sel = torch.randn(1000, E, device=dev, generator=g)
+    sel[::7, : E // 2] = 0.25  # exact ties: the lower expert index must win, as in a stable argsort
+    load = torch.full((E,), 5, dtype=torch.int64, device=dev)
+    chosen = ext().router_topk(sel, k, load)
+    want = sel.argsort(dim=-1, descending=True, stable=True)[:, :k]
+    assert torch.equal(chosen, want)
+    assert torch.equal(load - 5, torch.bincount(want.reshape(-1), minlength=E))
