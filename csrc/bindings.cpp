@@ -65,8 +65,8 @@ void ipc_close(int64_t ptr, int64_t device);
 bool peer_access_possible(int64_t device, int64_t peer);
 void moe_dispatch(at::Tensor x, at::Tensor rows, at::Tensor dst, std::vector<int64_t> recv, int64_t k);
 at::Tensor moe_combine(std::vector<int64_t> y, at::Tensor rows, at::Tensor dst, c10::optional<at::Tensor> w,
-                       int64_t T, int64_t k, int64_t d);
-at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::Tensor dst, std::vector<int64_t> y,
+                       int64_t T, int64_t k, int64_t d, c10::optional<at::Tensor> ys);
+at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::Tensor dst, at::Tensor ys,
                            std::vector<int64_t> dy, int64_t k);
 void grouped_gemm(at::Tensor a, std::vector<at::Tensor> bs, at::Tensor counts, at::Tensor out, bool b_kn);
 void grouped_wgrad(at::Tensor a, at::Tensor b, std::vector<int64_t> rows, std::vector<at::Tensor> grads);

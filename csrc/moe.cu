@@ -8,9 +8,10 @@
 // The receive buffers are CUDA-IPC mappings, so the exchange is plain loads and stores:
 //
 //   dispatch      recv[dst][row(t,j)]  = x[t]                       (one load of x[t], k peer stores)
-//   combine       out[t] = sum_j w[t,j] * y[dst][row(t,j)]          (peer loads, fp32 accumulate)
+//   combine       out[t] = sum_j w[t,j] * y[dst][row(t,j)]          (peer loads, fp32 accumulate;
+//                 optionally the loaded rows are kept:  ys[t*k+j] = y[dst][row(t,j)])
 //   combine_bwd   dy[dst][row(t,j)] = w[t,j] * dout[t]              (peer stores)
-//                 dw[t,j] = <dout[t], y[dst][row(t,j)]>             (peer loads, fp32)
+//                 dw[t,j] = <dout[t], ys[t*k+j]>                    (local rows kept by the forward)
 //   gather_sum    dx[t] = sum_j dxp[dst][row(t,j)]                  (combine with unit weights)
 //
 // One warp per token walks the hidden dimension in 16-byte vectors.  With W = 1 the same
@@ -83,7 +84,8 @@ __global__ void __launch_bounds__(kWarps * 32) moe_combine_kernel(const __grid_c
                                                                    const int32_t* __restrict__ rows,
                                                                    const int32_t* __restrict__ dst,
                                                                    const float* __restrict__ w,
-                                                                   __nv_bfloat16* __restrict__ out, int64_t T, int k,
+                                                                   __nv_bfloat16* __restrict__ out,
+                                                                   __nv_bfloat16* __restrict__ ys, int64_t T, int k,
                                                                    int64_t d) {
   const int64_t t = int64_t(blockIdx.x) * kWarps + threadIdx.x / 32;
   if (t >= T) return;
@@ -103,6 +105,7 @@ __global__ void __launch_bounds__(kWarps * 32) moe_combine_kernel(const __grid_c
 #pragma unroll
     for (int j = 0; j < kMaxTopK; ++j) {
       if (j < k) {
+        if (ys != nullptr) reinterpret_cast<uint4*>(ys + (t * k + j) * d)[v] = raw[j];
         float f[8];
         unpack8(raw[j], f);
 #pragma unroll
@@ -113,12 +116,12 @@ __global__ void __launch_bounds__(kWarps * 32) moe_combine_kernel(const __grid_c
   }
 }
 
-// dy[dst][row] = bf16(w[t,j] * dout[t]);  dw[t,j] = <dout[t], y[dst][row]>
+// dy[dst][row] = bf16(w[t,j] * dout[t]);  dw[t,j] = <dout[t], ys[t*k+j]>
 __global__ void __launch_bounds__(kWarps * 32) moe_combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout,
                                                                        const float* __restrict__ w,
                                                                        const int32_t* __restrict__ rows,
                                                                        const int32_t* __restrict__ dst,
-                                                                       const __grid_constant__ PeerRows y,
+                                                                       const __nv_bfloat16* __restrict__ ys,
                                                                        const __grid_constant__ PeerRows dy,
                                                                        float* __restrict__ dw, int64_t T, int k,
                                                                        int64_t d) {
@@ -138,7 +141,7 @@ __global__ void __launch_bounds__(kWarps * 32) moe_combine_bwd_kernel(const __nv
     for (int j = 0; j < kMaxTopK; ++j) {
       if (j < k) {
         float yf[8], s[8];
-        unpack8(row_ptr(y, q[j], r[j], d)[v], yf);
+        unpack8(reinterpret_cast<const uint4*>(ys + (t * k + j) * d)[v], yf);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           dot[j] += gf[e] * yf[e];
@@ -195,22 +198,25 @@ void moe_dispatch(at::Tensor x, at::Tensor rows, at::Tensor dst, std::vector<int
 }
 
 at::Tensor moe_combine(std::vector<int64_t> y, at::Tensor rows, at::Tensor dst, c10::optional<at::Tensor> w,
-                       int64_t T, int64_t k, int64_t d) {
+                       int64_t T, int64_t k, int64_t d, c10::optional<at::Tensor> ys) {
   TORCH_CHECK(d % 8 == 0, "hidden size must be a multiple of 8");
   check_routes(rows, dst, T, k);
   if (w) TORCH_CHECK(w->is_cuda() && w->dtype() == at::kFloat && w->is_contiguous() && w->numel() == T * k,
                      "weights: fp32 [T, k]");
+  if (ys) TORCH_CHECK(ys->is_cuda() && ys->dtype() == at::kBFloat16 && ys->is_contiguous() && ys->numel() == T * k * d,
+                      "ys: contiguous bf16 [T * k, d]");
   const c10::cuda::CUDAGuard guard(rows.device());
   at::Tensor out = at::empty({T, d}, rows.options().dtype(at::kBFloat16));
   if (T == 0) return out;
   moe_combine_kernel<<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
       make_rows(y), rows.data_ptr<int32_t>(), dst.data_ptr<int32_t>(), w ? w->data_ptr<float>() : nullptr,
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), T, static_cast<int>(k), d);
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+      ys ? reinterpret_cast<__nv_bfloat16*>(ys->data_ptr()) : nullptr, T, static_cast<int>(k), d);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }
 
-at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::Tensor dst, std::vector<int64_t> y,
+at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::Tensor dst, at::Tensor ys,
                            std::vector<int64_t> dy, int64_t k) {
   TORCH_CHECK(dout.is_cuda() && dout.dtype() == at::kBFloat16 && dout.is_contiguous() && dout.dim() == 2,
               "dout: bf16 [T, d]");
@@ -219,13 +225,15 @@ at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::T
   check_routes(rows, dst, T, k);
   TORCH_CHECK(w.is_cuda() && w.dtype() == at::kFloat && w.is_contiguous() && w.numel() == T * k,
               "weights: fp32 [T, k]");
-  TORCH_CHECK(y.size() == dy.size(), "one y and one dy buffer per rank");
+  TORCH_CHECK(ys.is_cuda() && ys.dtype() == at::kBFloat16 && ys.is_contiguous() && ys.numel() == T * k * d,
+              "ys: contiguous bf16 [T * k, d] (the rows the forward combine loaded)");
   const c10::cuda::CUDAGuard guard(dout.device());
   at::Tensor dw = at::empty({T, k}, w.options());
   if (T == 0) return dw;
   moe_combine_bwd_kernel<<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), w.data_ptr<float>(), rows.data_ptr<int32_t>(),
-      dst.data_ptr<int32_t>(), make_rows(y), make_rows(dy), dw.data_ptr<float>(), T, static_cast<int>(k), d);
+      dst.data_ptr<int32_t>(), reinterpret_cast<const __nv_bfloat16*>(ys.data_ptr()), make_rows(dy),
+      dw.data_ptr<float>(), T, static_cast<int>(k), d);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dw;
 }

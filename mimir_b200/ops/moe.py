@@ -206,12 +206,18 @@ def _expert_backward_grouped(dy, xp, gu, expert_rows, weights, dxp, rows_dev):
 
 
 class _GroupedExpertsFn(torch.autograd.Function):
+    """Saved for backward (through ``save_for_backward``, so activation checkpointing can drop and
+    recompute them): the owner-side input rows ``xp``, the gate/up projections, and ``ys``, the
+    expert outputs of this rank's token-slots as the forward combine loaded them.  No peer buffer
+    is held from the forward to the backward: each exchange's buffer goes back to the pool as soon
+    as its last kernel is issued (the next exchange's collective orders any reuse)."""
+
     @staticmethod
     def forward(ctx, x, topw, ep, plan, keep, *weights):
         T, d = x.shape
         k = topw.shape[1]
         ex = _Exchange(ep, plan, T, k, d)
-        ctx.ex, ctx.weights_n = ex, len(weights)
+        ctx.ex, ctx.n_weights = ex, len(weights)
         w32 = topw.float().contiguous()
         if ep.cuda:
             from mimir_b200.ops._ext import ext
@@ -223,27 +229,32 @@ class _GroupedExpertsFn(torch.autograd.Function):
             _, gus = _expert_forward(xp, plan.expert_rows, weights, buf.view(plan.capacity, ex.rows_in, d),
                                      plan.expert_rows_dev)
             ep.barrier()  # every owner's outputs are in place
-            out = C.moe_combine(buf.peer_ptrs(plan.capacity, d), plan.rows, plan.dst, w32, T, k, d)
-            if not keep:  # no backward: the next exchange's collective orders any reuse of the buffer
-                ep.release(buf)
-                return out
-            ctx.buf = buf
-            ctx.save_for_backward(w32, *weights)
-            ctx.xp, ctx.gus = xp, gus
-            return out
-        slots = x.repeat_interleave(k, dim=0) if k > 1 else x
-        xp = ex.to_owner_cpu(slots)
-        y, gus = _expert_forward(xp, plan.expert_rows, weights)
-        ys = ex.from_owner_cpu(y).view(T, k, d)
-        out = (ys.float() * w32.unsqueeze(-1)).sum(1).to(x.dtype)
-        ctx.save_for_backward(w32, *weights)
-        ctx.xp, ctx.gus, ctx.ys = xp, gus, ys
+            ys = torch.empty(T * k, d, dtype=x.dtype, device=x.device) if keep else None
+            out = C.moe_combine(buf.peer_ptrs(plan.capacity, d), plan.rows, plan.dst, w32, T, k, d, ys)
+            if keep:
+                xp = xp.clone()
+            ep.release(buf)
+        else:
+            slots = x.repeat_interleave(k, dim=0) if k > 1 else x
+            xp = ex.to_owner_cpu(slots)
+            y, gus = _expert_forward(xp, plan.expert_rows, weights)
+            ys = ex.from_owner_cpu(y)
+            out = (ys.view(T, k, d).float() * w32.unsqueeze(-1)).sum(1).to(x.dtype)
+        if keep:
+            ctx.gus_is_tensor = torch.is_tensor(gus)
+            gus = [gus] if ctx.gus_is_tensor else list(gus)
+            ctx.n_gus = len(gus)
+            ctx.save_for_backward(w32, xp, ys, *gus, *weights)
         return out
 
     @staticmethod
     def backward(ctx, dout):
         ex, plan, ep = ctx.ex, ctx.ex.plan, ctx.ex.ep
-        w32, *weights = ctx.saved_tensors
+        saved = ctx.saved_tensors
+        w32, xp, ys = saved[:3]
+        gus = saved[3:3 + ctx.n_gus]
+        weights = saved[3 + ctx.n_gus:]
+        gus = gus[0] if ctx.gus_is_tensor else list(gus)
         T, k, d = ex.T, ex.k, ex.d
         dout = dout.contiguous()
         if ep.cuda:
@@ -251,24 +262,21 @@ class _GroupedExpertsFn(torch.autograd.Function):
             C = ext()
             gbuf = ep.acquire(2 * plan.capacity, d)
             ep.barrier()  # every owner is done with the previous use of this buffer
-            dw = C.moe_combine_bwd(dout, w32, plan.rows, plan.dst, ctx.buf.peer_ptrs(plan.capacity, d),
-                                   gbuf.peer_ptrs(0, d), k)
+            dw = C.moe_combine_bwd(dout, w32, plan.rows, plan.dst, ys, gbuf.peer_ptrs(0, d), k)
             ep.barrier()  # the scaled output gradients have reached their owners
             dy = gbuf.view(0, ex.rows_in, d)
             dxp = gbuf.view(plan.capacity, ex.rows_in, d)
-            grads = _expert_backward(dy, ctx.xp, ctx.gus, plan.expert_rows, weights, dxp, plan.expert_rows_dev)
+            grads = _expert_backward(dy, xp, gus, plan.expert_rows, weights, dxp, plan.expert_rows_dev)
             ep.barrier()  # every owner's input gradients are in place
-            dx = C.moe_combine(gbuf.peer_ptrs(plan.capacity, d), plan.rows, plan.dst, None, T, k, d)
+            dx = C.moe_combine(gbuf.peer_ptrs(plan.capacity, d), plan.rows, plan.dst, None, T, k, d, None)
             ep.release(gbuf)
-            ep.release(ctx.buf)
         else:
             dys = (dout.float().unsqueeze(1) * w32.unsqueeze(-1)).to(dout.dtype).reshape(T * k, d)
-            dw = (dout.float().unsqueeze(1) * ctx.ys.float()).sum(-1)
+            dw = (dout.float().unsqueeze(1) * ys.view(T, k, d).float()).sum(-1)
             dy = ex.to_owner_cpu(dys)
-            dxp = torch.empty_like(ctx.xp)
-            grads = _expert_backward(dy, ctx.xp, ctx.gus, plan.expert_rows, weights, dxp)
+            dxp = torch.empty_like(xp)
+            grads = _expert_backward(dy, xp, gus, plan.expert_rows, weights, dxp)
             dx = ex.from_owner_cpu(dxp).view(T, k, d).float().sum(1).to(dout.dtype)
-        ctx.xp = ctx.gus = ctx.ys = ctx.buf = None
         return (dx, dw, None, None, None, *grads)
 
 

@@ -34,12 +34,14 @@ def test_exchange_kernels_match_torch():
         assert torch.equal(buf[rows[:, j]], x)
     y = torch.randn(T * K, D, device=dev, generator=g).to(torch.bfloat16)
     w = torch.rand(T, K, device=dev, generator=g)
-    out = C.moe_combine([y.data_ptr()], plan.rows, plan.dst, w, T, K, D)
+    ys = torch.empty(T * K, D, device=dev, dtype=torch.bfloat16)
+    out = C.moe_combine([y.data_ptr()], plan.rows, plan.dst, w, T, K, D, ys)
     want = (y[rows].float() * w.unsqueeze(-1)).sum(1)
     torch.testing.assert_close(out.float(), want, rtol=1e-2, atol=1e-2)
+    assert torch.equal(ys.view(T, K, D), y[rows])  # the loaded rows are kept for the backward
     dout = torch.randn(T, D, device=dev, generator=g).to(torch.bfloat16)
     dy = torch.zeros_like(y)
-    dw = C.moe_combine_bwd(dout, w, plan.rows, plan.dst, [y.data_ptr()], [dy.data_ptr()], K)
+    dw = C.moe_combine_bwd(dout, w, plan.rows, plan.dst, ys, [dy.data_ptr()], K)
     torch.testing.assert_close(dw, (dout.float().unsqueeze(1) * y[rows].float()).sum(-1), rtol=1e-4, atol=1e-3)
     for j in range(K):
         torch.testing.assert_close(dy[rows[:, j]].float(), (w[:, j:j + 1] * dout.float()), rtol=1e-2, atol=1e-2)
@@ -195,3 +197,18 @@ def test_router_topk_matches_stable_argsort_and_counts(E, k):
     want = sel.argsort(dim=-1, descending=True, stable=True)[:, :k]
     assert torch.equal(chosen, want)
     assert torch.equal(load - 5, torch.bincount(want.reshape(-1), minlength=E))
+
+
+def test_grouped_path_under_activation_checkpointing_returns_every_buffer():
+    from torch.utils.checkpoint import checkpoint
+    from mimir_b200.parallel.expert import expert_parallel
+    dev = torch.device("cuda", 0)
+    m = _mixture(True).to(dev, torch.bfloat16)
+    ep = expert_parallel(E, dev, distributed=False)
+    x = torch.randn(300, D, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    sizes = []
+    for _ in range(3):
+        checkpoint(m, x, use_reentrant=False).float().square().sum().backward()
+        assert not ep._busy  # nothing held after the backward
+        sizes.append(len(ep._pool))
+    assert sizes[1] == sizes[2]  # the pool stops growing: buffers are reused
