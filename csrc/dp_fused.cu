@@ -216,33 +216,6 @@ __device__ __forceinline__ void update8(const float (&gin)[8], float scale, int6
   if (a.ema != nullptr) st8(a.ema + sh, e);
 }
 
-// Bulk L2 prefetch of a contiguous range (16-byte aligned address and size); no data reaches the
-// CTA, so nothing has to be waited for.
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
-               : "memory");
-}
-
-// One thread of the CTA asks L2 for the fp32 optimizer slots (and this rank's gradients) of the
-// CTA's next chunk while the current one is being updated, so the chunk's loads find their
-// sectors in L2 instead of waiting on HBM with only a few loads in flight per thread.
-__device__ __forceinline__ void prefetch_chunk(const Peers& peers, const StepArgs& a, int64_t chunk) {
-  const Segment s = a.segs[find_segment(a.segs, a.nsegs, chunk)];
-  const int kind = s.kind & ~kLocalFlag;
-  if (!s.vec || (kind != kAdamATan2 && kind != kAdamEps)) return;
-  const int64_t start = (chunk - s.block_start) * kChunk;
-  const int64_t n = min(start + int64_t(kChunk), s.n) - start;
-  if (n <= 0) return;
-  const uint32_t fbytes = static_cast<uint32_t>(n * 4);
-  const int64_t sh = s.shard + start;
-  prefetch_l2(a.master + sh, fbytes);
-  prefetch_l2(a.exp_avg_sq + sh, fbytes);
-  if (a.exp_avg != nullptr) prefetch_l2(a.exp_avg + sh, fbytes);
-  if (a.ema != nullptr) prefetch_l2(a.ema + sh, fbytes);
-  prefetch_l2(reinterpret_cast<const __nv_bfloat16*>(peers.grad[a.rank]) + s.flat + start,
-              static_cast<uint32_t>(n * 2));
-}
-
 // Persistent: CTA b handles chunks b, b + gridDim.x, ...  Within a chunk each thread walks its
 // 8-element groups with the next group's gradient loads (peer loads over NVLink) issued before
 // the current group is updated, so NVLink latency overlaps the HBM traffic of the update.
@@ -250,9 +223,7 @@ template <bool kFromPeers>
 __global__ void __launch_bounds__(kThreads, 2) dp_update_kernel(const __grid_constant__ Peers peers,
                                                                    const StepArgs a, int64_t nchunks) {
   const float scale = a.grad_scale != nullptr ? *a.grad_scale : 1.f;
-  if (threadIdx.x == 0 && blockIdx.x < nchunks) prefetch_chunk(peers, a, blockIdx.x);
   for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
-    if (threadIdx.x == 0 && chunk + gridDim.x < nchunks) prefetch_chunk(peers, a, chunk + gridDim.x);
     const Segment s = a.segs[find_segment(a.segs, a.nsegs, chunk)];
     const int64_t start = (chunk - s.block_start) * kChunk;
     const int64_t end = min(start + int64_t(kChunk), s.n);
