@@ -340,6 +340,7 @@ class ReplicatedAdamATan2(Optimizer):
         (group,) = self.param_groups
         b1, b2 = group["betas"]
         lrs, wds, bc1, bc2_sqrt = {}, {}, {}, {}
+        corrections: dict = {}  # step value -> (bc1, sqrt(bc2)); parameters almost always share one
         for s in eng.slots:
             if not s.trainable or s.fqn not in eng.touched:
                 continue
@@ -347,9 +348,12 @@ class ReplicatedAdamATan2(Optimizer):
             st["step"] += 1
             lrs[s.fqn] = self._lr(group, s.param)
             wds[s.fqn] = float(group["weight_decay"])
-            # bias corrections exactly as the per-parameter optimizer forms them (fp32 tensors)
-            bc1[s.fqn] = (1 - b1 ** st["step"]) if self.exp_avg is not None else torch.tensor(1.0)
-            bc2_sqrt[s.fqn] = (1 - b2 ** st["step"]).sqrt()
+            key = float(st["step"])
+            if key not in corrections:
+                # bias corrections exactly as the per-parameter optimizer forms them (fp32 tensors)
+                corrections[key] = ((1 - b1 ** st["step"]) if self.exp_avg is not None else torch.tensor(1.0),
+                                    (1 - b2 ** st["step"]).sqrt())
+            bc1[s.fqn], bc2_sqrt[s.fqn] = corrections[key]
         ema = group["ema"]
         if eng.cuda:
             from mimir_b200.ops._ext import ext
@@ -510,7 +514,7 @@ class ReplicatedMuonAdamW(ReplicatedAdamATan2):
         beta, wd = float(group["muon_momentum"]), float(group["weight_decay"])
         first = {"lr": {}, "wd": {}, "bc1": {}, "bc2": {}, "extra": {}}
         second = {"lr": {}, "wd": {}, "bc1": {}, "bc2": {}, "extra": {}}
-        owned = []
+        owned, corrections = [], {}
         for s in eng.slots:
             if not s.trainable or s.fqn not in eng.touched:
                 continue
@@ -528,8 +532,11 @@ class ReplicatedMuonAdamW(ReplicatedAdamATan2):
                     owned.append(s)
             else:
                 first["lr"][s.fqn], first["wd"][s.fqn] = lr, wd
-                first["bc1"][s.fqn] = float(1 - b1 ** st["step"]) if self.has_m else 1.0
-                first["bc2"][s.fqn] = float(1 - b2 ** st["step"])
+                key = float(st["step"])
+                if key not in corrections:
+                    corrections[key] = (float(1 - b1 ** st["step"]) if self.has_m else 1.0,
+                                        float(1 - b2 ** st["step"]))
+                first["bc1"][s.fqn], first["bc2"][s.fqn] = corrections[key]
                 first["extra"][s.fqn] = (1, 0, 0, int(self.has_m))
         ema = group["ema"]
         if not eng.cuda:
