@@ -56,7 +56,7 @@ def main():
     loss.backward()
     del w, hid
 
-    ng = NGramMemory(d, orders=(2, 3), buckets=args.buckets, heads=1).to(dev, torch.bfloat16)
+    ng = NGramMemory(256, orders=(2, 3), buckets=args.buckets, heads=1).to(dev, torch.bfloat16)  # config 5: 256 dims
     ids = torch.randint(0, 65536, (1, T), device=dev)
     pos = torch.arange(T, device=dev).remainder(4096).unsqueeze(0)
     ng.lookup(ids, pos, torch.bfloat16).float().sum().backward()
