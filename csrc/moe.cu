@@ -14,13 +14,16 @@
 //                 dw[t,j] = <dout[t], ys[t*k+j]>                    (local rows kept by the forward)
 //   gather_sum    dx[t] = sum_j dxp[dst][row(t,j)]                  (combine with unit weights)
 //
-// One warp per token walks the hidden dimension in 16-byte vectors.  With W = 1 the same
+// One warp per token walks the hidden dimension in 16-byte vectors, kUnroll vectors per lane at a
+// time (loads first, then the arithmetic and stores).  With W = 1 the same
 // kernels are the local permutation and un-permutation.  Nothing here waits on a peer: the
 // caller orders each exchange with the other ranks by a collective before and after it.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cuda_runtime.h>
 #include <torch/extension.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -57,110 +60,155 @@ __device__ __forceinline__ uint4* row_ptr_mut(const PeerRows& p, int rank, int64
   return reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.ptr[rank]) + row * d);
 }
 
+// Every lane first loads kUnroll 16-byte vectors (of each of the K rows) and only then uses them,
+// so a warp keeps several loads in flight per lane: the copies are latency-bound otherwise.
+constexpr int kUnroll = 4;
+
+template <int K>
 __global__ void __launch_bounds__(kWarps * 32) moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x,
                                                                     const int32_t* __restrict__ rows,
                                                                     const int32_t* __restrict__ dst,
                                                                     const __grid_constant__ PeerRows recv, int64_t T,
-                                                                    int k, int64_t d) {
+                                                                    int64_t d) {
   const int64_t t = int64_t(blockIdx.x) * kWarps + threadIdx.x / 32;
   if (t >= T) return;
   const int lane = threadIdx.x & 31;
-  int r[kMaxTopK], q[kMaxTopK];
+  int r[K], q[K];
 #pragma unroll
-  for (int j = 0; j < kMaxTopK; ++j)
-    if (j < k) r[j] = rows[t * k + j], q[j] = dst[t * k + j];
+  for (int j = 0; j < K; ++j) r[j] = rows[t * K + j], q[j] = dst[t * K + j];
   const uint4* src = reinterpret_cast<const uint4*>(x + t * d);
-  for (int64_t v = lane; v < d / 8; v += 32) {
-    const uint4 val = src[v];
+  const int64_t nv = d / 8;
+  for (int64_t v0 = lane; v0 < nv; v0 += 32 * kUnroll) {
+    uint4 val[kUnroll];
 #pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j)
-      if (j < k) row_ptr_mut(recv, q[j], r[j], d)[v] = val;
+    for (int u = 0; u < kUnroll; ++u)
+      if (v0 + 32 * u < nv) val[u] = src[v0 + 32 * u];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (v0 + 32 * u < nv) {
+#pragma unroll
+        for (int j = 0; j < K; ++j) row_ptr_mut(recv, q[j], r[j], d)[v0 + 32 * u] = val[u];
+      }
+    }
   }
   __threadfence_system();  // this thread's peer stores are visible before the closing collective
 }
 
-// out[t] = sum_j w[t,j] * y[dst][row]   (w == nullptr: unit weights)
+// out[t] = sum_j w[t,j] * y[dst][row]   (w == nullptr: unit weights); ys[t*K+j] = the loaded rows
+template <int K>
 __global__ void __launch_bounds__(kWarps * 32) moe_combine_kernel(const __grid_constant__ PeerRows y,
                                                                    const int32_t* __restrict__ rows,
                                                                    const int32_t* __restrict__ dst,
                                                                    const float* __restrict__ w,
                                                                    __nv_bfloat16* __restrict__ out,
-                                                                   __nv_bfloat16* __restrict__ ys, int64_t T, int k,
+                                                                   __nv_bfloat16* __restrict__ ys, int64_t T,
                                                                    int64_t d) {
   const int64_t t = int64_t(blockIdx.x) * kWarps + threadIdx.x / 32;
   if (t >= T) return;
   const int lane = threadIdx.x & 31;
-  int r[kMaxTopK], q[kMaxTopK];
-  float wt[kMaxTopK];
+  int r[K], q[K];
+  float wt[K];
 #pragma unroll
-  for (int j = 0; j < kMaxTopK; ++j)
-    if (j < k) r[j] = rows[t * k + j], q[j] = dst[t * k + j], wt[j] = w != nullptr ? w[t * k + j] : 1.f;
+  for (int j = 0; j < K; ++j)
+    r[j] = rows[t * K + j], q[j] = dst[t * K + j], wt[j] = w != nullptr ? w[t * K + j] : 1.f;
   uint4* o = reinterpret_cast<uint4*>(out + t * d);
-  for (int64_t v = lane; v < d / 8; v += 32) {
-    uint4 raw[kMaxTopK];
+  const int64_t nv = d / 8;
+  for (int64_t v0 = lane; v0 < nv; v0 += 32 * kUnroll) {
+    uint4 raw[kUnroll][K];
 #pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j)
-      if (j < k) raw[j] = row_ptr(y, q[j], r[j], d)[v];
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int u = 0; u < kUnroll; ++u)
+      if (v0 + 32 * u < nv) {
 #pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j) {
-      if (j < k) {
-        if (ys != nullptr) reinterpret_cast<uint4*>(ys + (t * k + j) * d)[v] = raw[j];
+        for (int j = 0; j < K; ++j) raw[u][j] = row_ptr(y, q[j], r[j], d)[v0 + 32 * u];
+      }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = v0 + 32 * u;
+      if (v >= nv) continue;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        if (ys != nullptr) reinterpret_cast<uint4*>(ys + (t * K + j) * d)[v] = raw[u][j];
         float f[8];
-        unpack8(raw[j], f);
+        unpack8(raw[u][j], f);
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[e] += wt[j] * f[e];
       }
+      o[v] = pack8(acc);
     }
-    o[v] = pack8(acc);
   }
 }
 
-// dy[dst][row] = bf16(w[t,j] * dout[t]);  dw[t,j] = <dout[t], ys[t*k+j]>
+// dy[dst][row] = bf16(w[t,j] * dout[t]);  dw[t,j] = <dout[t], ys[t*K+j]>
+template <int K>
 __global__ void __launch_bounds__(kWarps * 32) moe_combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout,
                                                                        const float* __restrict__ w,
                                                                        const int32_t* __restrict__ rows,
                                                                        const int32_t* __restrict__ dst,
                                                                        const __nv_bfloat16* __restrict__ ys,
                                                                        const __grid_constant__ PeerRows dy,
-                                                                       float* __restrict__ dw, int64_t T, int k,
-                                                                       int64_t d) {
+                                                                       float* __restrict__ dw, int64_t T, int64_t d) {
   const int64_t t = int64_t(blockIdx.x) * kWarps + threadIdx.x / 32;
   if (t >= T) return;
   const int lane = threadIdx.x & 31;
-  int r[kMaxTopK], q[kMaxTopK];
-  float wt[kMaxTopK], dot[kMaxTopK];
+  int r[K], q[K];
+  float wt[K], dot[K];
 #pragma unroll
-  for (int j = 0; j < kMaxTopK; ++j)
-    if (j < k) r[j] = rows[t * k + j], q[j] = dst[t * k + j], wt[j] = w[t * k + j], dot[j] = 0.f;
+  for (int j = 0; j < K; ++j) r[j] = rows[t * K + j], q[j] = dst[t * K + j], wt[j] = w[t * K + j], dot[j] = 0.f;
   const uint4* g = reinterpret_cast<const uint4*>(dout + t * d);
-  for (int64_t v = lane; v < d / 8; v += 32) {
-    float gf[8];
-    unpack8(g[v], gf);
+  const int64_t nv = d / 8;
+  for (int64_t v0 = lane; v0 < nv; v0 += 32 * kUnroll) {
+    uint4 gr[kUnroll], yr[kUnroll][K];
 #pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j) {
-      if (j < k) {
-        float yf[8], s[8];
-        unpack8(reinterpret_cast<const uint4*>(ys + (t * k + j) * d)[v], yf);
+    for (int u = 0; u < kUnroll; ++u)
+      if (v0 + 32 * u < nv) {
+        gr[u] = g[v0 + 32 * u];
+#pragma unroll
+        for (int j = 0; j < K; ++j) yr[u][j] = reinterpret_cast<const uint4*>(ys + (t * K + j) * d)[v0 + 32 * u];
+      }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = v0 + 32 * u;
+      if (v >= nv) continue;
+      float gf[8];
+      unpack8(gr[u], gf);
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        float yf[8], sc[8];
+        unpack8(yr[u][j], yf);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           dot[j] += gf[e] * yf[e];
-          s[e] = wt[j] * gf[e];
+          sc[e] = wt[j] * gf[e];
         }
-        row_ptr_mut(dy, q[j], r[j], d)[v] = pack8(s);
+        row_ptr_mut(dy, q[j], r[j], d)[v] = pack8(sc);
       }
     }
   }
 #pragma unroll
-  for (int j = 0; j < kMaxTopK; ++j) {
-    if (j < k) {
-      float s = dot[j];
+  for (int j = 0; j < K; ++j) {
+    float sm = dot[j];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) dw[t * k + j] = s;
-    }
+    for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+    if (lane == 0) dw[t * K + j] = sm;
   }
   __threadfence_system();
+}
+
+// Calls `launch(std::integral_constant<int, K>{})` for the top-k in use (1..kMaxTopK).
+template <typename F>
+void with_topk(int64_t k, F&& launch) {
+  switch (k) {
+    case 1: launch(std::integral_constant<int, 1>{}); break;
+    case 2: launch(std::integral_constant<int, 2>{}); break;
+    case 3: launch(std::integral_constant<int, 3>{}); break;
+    case 4: launch(std::integral_constant<int, 4>{}); break;
+    case 5: launch(std::integral_constant<int, 5>{}); break;
+    case 6: launch(std::integral_constant<int, 6>{}); break;
+    case 7: launch(std::integral_constant<int, 7>{}); break;
+    case 8: launch(std::integral_constant<int, 8>{}); break;
+    default: TORCH_CHECK(false, "top-k must be in [1, ", kMaxTopK, "]");
+  }
 }
 
 PeerRows make_rows(const std::vector<int64_t>& ptrs) {
@@ -191,9 +239,11 @@ void moe_dispatch(at::Tensor x, at::Tensor rows, at::Tensor dst, std::vector<int
   check_routes(rows, dst, T, k);
   const c10::cuda::CUDAGuard guard(x.device());
   if (T == 0) return;
-  moe_dispatch_kernel<<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), rows.data_ptr<int32_t>(), dst.data_ptr<int32_t>(),
-      make_rows(recv), T, static_cast<int>(k), d);
+  with_topk(k, [&](auto kk) {
+    moe_dispatch_kernel<decltype(kk)::value><<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), rows.data_ptr<int32_t>(), dst.data_ptr<int32_t>(),
+        make_rows(recv), T, d);
+  });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -208,10 +258,12 @@ at::Tensor moe_combine(std::vector<int64_t> y, at::Tensor rows, at::Tensor dst, 
   const c10::cuda::CUDAGuard guard(rows.device());
   at::Tensor out = at::empty({T, d}, rows.options().dtype(at::kBFloat16));
   if (T == 0) return out;
-  moe_combine_kernel<<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
-      make_rows(y), rows.data_ptr<int32_t>(), dst.data_ptr<int32_t>(), w ? w->data_ptr<float>() : nullptr,
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-      ys ? reinterpret_cast<__nv_bfloat16*>(ys->data_ptr()) : nullptr, T, static_cast<int>(k), d);
+  with_topk(k, [&](auto kk) {
+    moe_combine_kernel<decltype(kk)::value><<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+        make_rows(y), rows.data_ptr<int32_t>(), dst.data_ptr<int32_t>(), w ? w->data_ptr<float>() : nullptr,
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+        ys ? reinterpret_cast<__nv_bfloat16*>(ys->data_ptr()) : nullptr, T, d);
+  });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }
@@ -230,10 +282,12 @@ at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::T
   const c10::cuda::CUDAGuard guard(dout.device());
   at::Tensor dw = at::empty({T, k}, w.options());
   if (T == 0) return dw;
-  moe_combine_bwd_kernel<<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), w.data_ptr<float>(), rows.data_ptr<int32_t>(),
-      dst.data_ptr<int32_t>(), reinterpret_cast<const __nv_bfloat16*>(ys.data_ptr()), make_rows(dy),
-      dw.data_ptr<float>(), T, static_cast<int>(k), d);
+  with_topk(k, [&](auto kk) {
+    moe_combine_bwd_kernel<decltype(kk)::value><<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), w.data_ptr<float>(), rows.data_ptr<int32_t>(),
+        dst.data_ptr<int32_t>(), reinterpret_cast<const __nv_bfloat16*>(ys.data_ptr()), make_rows(dy),
+        dw.data_ptr<float>(), T, d);
+  });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dw;
 }
