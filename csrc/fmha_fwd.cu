@@ -25,6 +25,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "fmha_noalloc.h"
 #include "tma.cuh"
@@ -534,7 +536,9 @@ int64_t fmha_status(at::Device dev) {
 // cudaGetSymbolAddress returns for the current device.
 namespace {
 static __device__ __align__(256) int2 g_noalloc_tiles[MIMIR_FMHA_NOALLOC_MAX_TILES];
-static __device__ __align__(256) int g_noalloc_words[64];  // [0] tile count, [1] kernel status
+// [0] tile count (rewritten by every call's schedule kernel), [1] kernel status: the first
+// bounded-wait timeout of any call since the last mimir_fmha_noalloc_status() read.
+static __device__ __align__(256) int g_noalloc_words[64];
 
 struct NoAllocScratch {
   int2* tiles = nullptr;
@@ -542,17 +546,25 @@ struct NoAllocScratch {
   bool ready = false;
 };
 NoAllocScratch g_scratch[64];
+std::mutex g_noalloc_setup_mu;  // two host threads making their first call at once
 
+// Once per device, with that device current: look up the scratch addresses and raise the
+// kernel's dynamic shared-memory limit.
 int noalloc_setup(int device) {
   if (device < 0 || device >= 64) return MIMIR_NOALLOC_ERR_ARGS;
+  std::lock_guard<std::mutex> lock(g_noalloc_setup_mu);
   NoAllocScratch& s = g_scratch[device];
   if (s.ready) return MIMIR_NOALLOC_OK;
-  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.tiles), g_noalloc_tiles) != cudaSuccess)
+  int2* tiles = nullptr;
+  int* words = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&tiles), g_noalloc_tiles) != cudaSuccess)
     return MIMIR_NOALLOC_ERR_CUDA;
-  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.words), g_noalloc_words) != cudaSuccess)
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&words), g_noalloc_words) != cudaSuccess)
     return MIMIR_NOALLOC_ERR_CUDA;
   if (cudaFuncSetAttribute(fmha_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
     return MIMIR_NOALLOC_ERR_CUDA;
+  s.tiles = tiles;
+  s.words = words;
   s.ready = true;
   return MIMIR_NOALLOC_OK;
 }
@@ -584,6 +596,11 @@ extern "C" int mimir_fmha_fwd_noalloc(const void* q, int64_t q_ld, const void* k
       q_ld < (int64_t)num_heads * kHeadDim || k_ld < (int64_t)num_kv_heads * kHeadDim ||
       v_ld < (int64_t)num_kv_heads * kHeadDim)
     return MIMIR_NOALLOC_ERR_ARGS;
+  // The kernel stores `out` in 16-byte vectors and `lse` as fp32; the schedule reads int32.
+  if (reinterpret_cast<uintptr_t>(out) % 16 != 0 || reinterpret_cast<uintptr_t>(lse) % 4 != 0 ||
+      reinterpret_cast<uintptr_t>(cu_seqlens) % 4 != 0 ||
+      (prefix_lens != nullptr && reinterpret_cast<uintptr_t>(prefix_lens) % 4 != 0))
+    return MIMIR_NOALLOC_ERR_ARGS;
   if (total_tokens == 0 || numseqs == 0) return MIMIR_NOALLOC_OK;
   const int64_t max_tiles = (total_tokens + kTile - 1) / kTile + numseqs;
   if (max_tiles > MIMIR_FMHA_NOALLOC_MAX_TILES || max_tiles > 65535) return MIMIR_NOALLOC_ERR_TOO_LARGE;
@@ -596,8 +613,8 @@ extern "C" int mimir_fmha_fwd_noalloc(const void* q, int64_t q_ld, const void* k
   if (!make_tmap_noexcept(&mq, q, total_tokens, q_ld, q_ld) || !make_tmap_noexcept(&mk, k, total_tokens, k_ld, k_ld) ||
       !make_tmap_noexcept(&mv, v, total_tokens, v_ld, v_ld))
     return MIMIR_NOALLOC_ERR_ARGS;
-  // The status word must start at zero; the tile count is rewritten by the schedule kernel.
-  if (cudaMemsetAsync(s.words + 1, 0, sizeof(int), stream) != cudaSuccess) return MIMIR_NOALLOC_ERR_CUDA;
+  // The tile count (words[0]) is rewritten by the schedule kernel; the status word keeps
+  // collecting failures until mimir_fmha_noalloc_status() reads and clears it.
   // A causal call never reads prefix_lens; the schedule kernel gets the cu_seqlens pointer as a
   // harmless stand-in so it never dereferences a null pointer.
   const int* prefix = is_causal ? cu_seqlens : prefix_lens;
@@ -619,4 +636,20 @@ extern "C" int mimir_fmha_fwd_noalloc(const void* q, int64_t q_ld, const void* k
   dim3 grid((unsigned)num_heads, (unsigned)max_tiles);
   fmha_fwd_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, prm);
   return cudaGetLastError() == cudaSuccess ? MIMIR_NOALLOC_OK : MIMIR_NOALLOC_ERR_CUDA;
+}
+
+extern "C" int mimir_fmha_noalloc_status(cudaStream_t stream, int* status_out) {
+  if (status_out == nullptr) return MIMIR_NOALLOC_ERR_ARGS;
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess) return MIMIR_NOALLOC_ERR_CUDA;
+  const int rc = noalloc_setup(device);
+  if (rc != MIMIR_NOALLOC_OK) return rc;
+  int* word = g_scratch[device].words + 1;
+  // Pageable destination: the copy is staged by the driver, so it is complete once the
+  // stream has synchronised.
+  if (cudaMemcpyAsync(status_out, word, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return MIMIR_NOALLOC_ERR_CUDA;
+  if (*status_out != 0 && cudaMemsetAsync(word, 0, sizeof(int), stream) != cudaSuccess) return MIMIR_NOALLOC_ERR_CUDA;
+  return MIMIR_NOALLOC_OK;
 }
