@@ -212,18 +212,31 @@ def timed_loop(run_step, batches, steps: int):
 
 
 # ---------------------------------------------------------------------------------------- our arm
-def run_ours(args, rank, world, local):
-    sys.path.insert(0, ROOT)
+def heldout_loss(model_call, device, wrap) -> float:
+    """Forward-only loss on a batch no step has seen (step index 10**6).  The timed loop alternates
+    two batches, so its training loss falls towards zero as the 1.3B model memorises their random
+    labels; on unseen uniform labels the loss must stay near ln(65536) = 11.09."""
+    host, scalars = synthetic_batch(dist.get_rank(), 10 ** 6)
+    with torch.no_grad():
+        metrics = model_call(device_batch(host, scalars, device, wrap))
+    return float((metrics["loss"][0] / metrics["loss"][1]).item())
+
+
+def measure_ours(args, rank, world, local, kv_heads):
+    """Build our model with `kv_heads` KV heads, warm up, then time K steps on the device and K
+    steps end to end.  Releases the model and its peer buffers before returning."""
+    import gc
+
     from mimir_b200.config.schema import PretrainConfig
     from mimir_b200.models.common import wrap_tensor
-    from mimir_b200.ops._ext import ext, launch_count
+    from mimir_b200.ops._ext import launch_count
     from mimir_b200.optim.schedules import update_lr
+    from mimir_b200.parallel.replicated import engine_of
     from mimir_b200.train.setup import create_model_and_optimizer, make_train_state
     from mimir_b200.train.steps import train_accumulated_batches
 
-    ext()  # fail loudly if the extension is missing
     device = torch.device("cuda", local)
-    arch = arch_dict(kv_heads=MODEL["num_key_value_heads"])
+    arch = arch_dict(kv_heads=kv_heads)
     vocab = arch.pop("vocab_size")
     config = PretrainConfig(arch=arch, data=dict(path="synthetic"), global_batch_size=SEQ_LEN * SEQS_PER_GPU * world,
                             epochs=1, lr=3e-4, lr_warmup_steps=0, lr_min_ratio=1.0, weight_decay=0.1, beta1=0.9,
@@ -263,7 +276,25 @@ def run_ours(args, rank, world, local):
         losses.append((metrics["loss"][0] / metrics["loss"][1]).item())
     torch.cuda.synchronize()
     e2e_seconds = max_over_ranks(time.perf_counter() - t0)
-    flops = model_flops_per_step(hosts[0][0], MODEL["num_key_value_heads"])
+    unseen = heldout_loss(lambda b: state.model(batch=b, carry=state.carry, bp_steps=2)[2], device, wrap_tensor)
+    flops = model_flops_per_step(hosts[0][0], kv_heads)
+    engine = engine_of(model)
+    if engine is not None:
+        dist.barrier()
+        engine.close()
+    del state, model, carry, optim, dev_batches
+    gc.collect()
+    torch.cuda.empty_cache()
+    return dict(seconds=seconds, e2e_seconds=e2e_seconds, h2d=h2d, flops=flops, clocks=clock_info,
+                launches=launches, final_loss=losses[-1], heldout_loss=unseen)
+
+
+def run_ours(args, rank, world, local):
+    sys.path.insert(0, ROOT)
+    from mimir_b200.ops._ext import ext
+
+    ext()  # fail loudly if the extension is missing
+    r = measure_ours(args, rank, world, local, args.kv_heads)
     if args.dp != "replicated":
         label = f"fsdp{world}"
     elif args.optimizer == "muon":
@@ -276,8 +307,22 @@ def run_ours(args, rank, world, local):
     if CONFIG["name"] == "moe":
         label += (f"; ep{world}: {MOE['experts'] // world} experts per GPU, token rows dispatched/combined over "
                   "NVLink peer memory (route plan from all-gathered expert counts, no capacity factor)")
-    return emit(args, world, seconds, e2e_seconds, h2d, 4, flops, clock_info, launches, impl="ours",
-                extra={"final_loss": losses[-1], "parallelism": label})
+    extra = {"final_loss": r["final_loss"], "heldout_loss": r["heldout_loss"], "parallelism": label,
+             "num_key_value_heads": args.kv_heads}
+    if CONFIG["name"] == "dense" and args.same_config and args.kv_heads != MODEL["num_heads"]:
+        # The reference ties KV heads to Q heads, so its arm can only run 16 KV heads; measure our
+        # arm on that exact architecture too.
+        same = measure_ours(args, rank, world, local, MODEL["num_heads"])
+        tokens = SEQ_LEN * SEQS_PER_GPU * world * args.steps
+        extra["same_config"] = {
+            "num_key_value_heads": MODEL["num_heads"], "value": round(tokens / same["seconds"], 1),
+            "ms_per_step": round(same["seconds"] / args.steps * 1000.0, 3),
+            "e2e": {"value": round(tokens / same["e2e_seconds"], 1), "unit": "tokens/s"},
+            "final_loss": same["final_loss"], "heldout_loss": same["heldout_loss"], "clocks": same["clocks"],
+            "gpu_launches": same["launches"],
+            "note": "the reference arm's architecture (KV heads = Q heads, its transformer.py:78)"}
+    return emit(args, world, r["seconds"], r["e2e_seconds"], r["h2d"], 4, r["flops"], r["clocks"], r["launches"],
+                impl="ours", extra=extra)
 
 
 # ---------------------------------------------------------------------------------------- reference arm
@@ -381,17 +426,20 @@ def run_reference(args, rank, world, local):
     dist.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
+    losses = []
     for i in range(args.steps):
         host, scalars = hosts[i % 2]
         metrics = step(device_batch(host, scalars, device, wrap_tensor))
-        (metrics["loss"][0] / metrics["loss"][1]).item()
+        losses.append((metrics["loss"][0] / metrics["loss"][1]).item())
     torch.cuda.synchronize()
     e2e_seconds = max_over_ranks(time.perf_counter() - t0)
+    unseen = heldout_loss(lambda b: state.model(batch=b, carry=state.carry, bp_steps=2)[2], device, wrap_tensor)
     if CONFIG["name"] == "moe":
         CONFIG.update(expert_ffn=1536, active_experts=MOE["top_k"])
     flops = model_flops_per_step(hosts[0][0], MODEL["num_heads"])
     extra = {"attention_backend": "reference dense prefix-LM SDPA (FA4 unavailable offline)",
-             "num_key_value_heads": MODEL["num_heads"], "torch_compile": compiled}
+             "num_key_value_heads": MODEL["num_heads"], "torch_compile": compiled, "final_loss": losses[-1],
+             "heldout_loss": unseen}
     if CONFIG["name"] == "moe":
         extra["moe_reference_limits"] = ("no expert FFN width option (experts are dense-MLP copies: FFN 1536, the "
                                          "multiple of 256 nearest 1408), no shared expert, no expert parallelism "
@@ -451,6 +499,10 @@ def main():
                     help="dense: the headline 1.3B config; moe: the 64-expert MoE config with expert parallelism")
     ap.add_argument("--optimizer", choices=["adam_atan2", "muon"], default="adam_atan2",
                     help="adam_atan2: the headline config; muon: the Muon variant of the same model")
+    ap.add_argument("--kv-heads", type=int, default=MODEL["num_key_value_heads"],
+                    help="KV heads of our arm's dense model (BASELINE config 2: 4)")
+    ap.add_argument("--no-same-config", dest="same_config", action="store_false",
+                    help="skip the extra measurement of our arm at the reference's 16 KV heads")
     ap.add_argument("--dp", choices=["replicated", "fsdp"], default="replicated",
                     help="data-parallel engine of our arm (the reference arm always uses its FSDP2)")
     args = ap.parse_args()
