@@ -50,6 +50,7 @@ def main():
     ap.add_argument("--kv-heads", type=int, default=4)
     ap.add_argument("--only", default=None, help="comma-separated projection names")
     ap.add_argument("--check", action="store_true", help="compare ours against cuBLAS")
+    ap.add_argument("--fused", action="store_true", help="also time the fused SwiGLU / accumulate epilogues")
     args = ap.parse_args()
     peaks = {}
     try:
@@ -95,6 +96,35 @@ def main():
     if len(impls) == 2:
         tot = {i: sum(r[f"{i}_ms"] for r in rows) for i in impls}
         print(json.dumps({"total_ms": tot}))
+    if args.fused and "ours" in impls:
+        fused_rows(T, args.iters, flush, peak)
+
+
+def fused_rows(T, iters, flush, peak):
+    """The fused epilogues as the model uses them, against cuBLAS plus the separate kernels."""
+    from mimir_b200 import ops
+    C = ops.ext()
+    d, F = 2048, 5632
+    x = torch.randn(T, d, device="cuda", dtype=torch.bfloat16)
+    w_gu = torch.randn(2 * F, d, device="cuda", dtype=torch.bfloat16) * d ** -0.5
+    w_dn = torch.randn(d, F, device="cuda", dtype=torch.bfloat16) * F ** -0.5
+    dy = torch.randn(T, d, device="cuda", dtype=torch.bfloat16)
+    gu = torch.mm(x, w_gu.t())
+    grad = torch.zeros(2 * F, d, device="cuda", dtype=torch.bfloat16)
+    dgu = torch.randn(T, 2 * F, device="cuda", dtype=torch.bfloat16)
+    cases = [
+        ("swiglu_forward (gate_up GEMM + SwiGLU)", 2.0 * T * 2 * F * d,
+         lambda: C.gemm_swiglu(x, w_gu), lambda: C.swiglu_fwd(torch.mm(x, w_gu.t()))),
+        ("swiglu_backward (down input-grad GEMM + SwiGLU bwd)", 2.0 * T * F * d,
+         lambda: C.gemm_swiglu_bwd(dy, w_dn, gu), lambda: C.swiglu_bwd(torch.mm(dy, w_dn), gu)),
+        ("gate_up weight grad accumulated in place (bf16)", 2.0 * T * 2 * F * d,
+         lambda: C.gemm(dgu, True, x, True, grad, grad, 1.0, 1.0), lambda: grad.add_(torch.mm(dgu.t(), x))),
+    ]
+    for name, flops, ours, ref in cases:
+        o, r = _time(ours, flush, iters), _time(ref, flush, iters)
+        print(json.dumps({"fused": name, "ours_ms": round(o, 4), "cublas_plus_kernel_ms": round(r, 4),
+                          "ours_tflops": round(flops / o / 1e9, 1),
+                          "ours_frac_of_measured": round(flops / o / 1e9 / peak, 3)}), flush=True)
 
 
 if __name__ == "__main__":

@@ -72,6 +72,13 @@ void grouped_gemm(at::Tensor a, std::vector<at::Tensor> bs, at::Tensor counts, a
 void grouped_wgrad(at::Tensor a, at::Tensor b, std::vector<int64_t> rows, std::vector<at::Tensor> grads);
 int64_t grouped_gemm_status(int64_t device);
 at::Tensor router_topk(at::Tensor scores, int64_t k, c10::optional<at::Tensor> load);
+// gemm.cu
+at::Tensor gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, c10::optional<at::Tensor> out,
+                c10::optional<at::Tensor> add, double alpha, double beta, int64_t bn, int64_t group_m,
+                int64_t wait_ns, int64_t inject);
+std::vector<at::Tensor> gemm_swiglu(at::Tensor x, at::Tensor w_gu, int64_t group_m);
+at::Tensor gemm_swiglu_bwd(at::Tensor dy, at::Tensor w_down, at::Tensor gu, int64_t group_m);
+int64_t gemm_status(int64_t device);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mimir_b200 hand-written sm_100a kernels";
@@ -111,6 +118,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_wgrad", &grouped_wgrad);
   m.def("grouped_gemm_status", &grouped_gemm_status);
   m.def("router_topk", &router_topk);
+  m.def("gemm", &gemm, py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"), py::arg("out") = py::none(),
+        py::arg("add") = py::none(), py::arg("alpha") = 1.0, py::arg("beta") = 0.0, py::arg("bn") = 256,
+        py::arg("group_m") = 8, py::arg("wait_ns") = 0, py::arg("inject") = 0);
+  m.def("gemm_swiglu", &gemm_swiglu, py::arg("x"), py::arg("w_gu"), py::arg("group_m") = 8);
+  m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd, py::arg("dy"), py::arg("w_down"), py::arg("gu"), py::arg("group_m") = 8);
+  m.def("gemm_status", &gemm_status);
   m.def("fmha_bwd", &fmha_bwd, py::arg("q_src"), py::arg("q_col"), py::arg("k_src"), py::arg("k_col"),
         py::arg("v_src"), py::arg("v_col"), py::arg("d_o"), py::arg("lse"), py::arg("delta"), py::arg("H"),
         py::arg("KV"), py::arg("is_causal"), py::arg("cu_seqlens"), py::arg("prefix_lens"), py::arg("numseqs"),

@@ -571,6 +571,7 @@ int noalloc_setup(int device) {
 
 bool make_tmap_noexcept(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld) {
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0 || (ld * 2) % 16 != 0) return false;
+  bind_device_context();  // the encoder needs a current context (first call on a new host thread)
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
   cuuint32_t box[2] = {64, (cuuint32_t)kTile};

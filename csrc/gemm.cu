@@ -1,0 +1,586 @@
+// Dense GEMM on the 5th-generation tensor cores, one CTA pair per 256-row output tile.
+//
+//   C[M, N] = alpha * sum_k A[m, k] * B[n, k]  (+ beta * D[M, N])
+//
+// A is K-major ([M, K] row-major) or M-major ([K, M] row-major, i.e. the transpose is stored);
+// B is K-major ([N, K]) or N-major ([K, N]).  The three GEMMs of a linear layer Y = X W^T are
+//   forward         Y  = X  W^T   A = X  [T, in]  K-major, B = W [out, in] K-major   ("nt")
+//   input gradient  dX = dY W     A = dY [T, out] K-major, B = W [out, in] N-major   ("nn")
+//   weight gradient dW = dY^T X   A = dY [T, out] M-major, B = X [T, in]   N-major   ("tn")
+// so no operand is ever transposed in memory.
+//
+// Tiling: a cluster of two CTAs (an SM pair) owns a 256 x BN output tile.  Each CTA stages its
+// 128 rows of A and BN/2 rows of B per 64-deep k-block with TMA (128-byte swizzle, no
+// multicast), and the even CTA issues tcgen05.mma.cta_group::2 (M = 256, N = BN, K = 16), which
+// reads both CTAs' shared memory and writes each CTA's 128 accumulator rows into its own TMEM.
+// Per SM that is half the shared-memory operand traffic of a one-CTA 128 x BN tile.
+//
+// Persistent kernel, one CTA per SM, 6 warps per CTA:
+//   warp 0      TMA producer (both CTAs): ring of kStages stages; every stage's bytes from both
+//               CTAs complete on the even CTA's `full` barrier.
+//   warp 1      MMA issuer (even CTA only): 4 MMAs per k-block into one of two TMEM
+//               accumulators; commits release the stage in both CTAs (`empty`) and hand the
+//               finished accumulator to both CTAs' epilogues (`acc_full`).
+//   warps 2-5   epilogue (both CTAs): tcgen05.ld of the CTA's 128 rows (one row per thread),
+//               the fused epilogue, 16-byte global stores; the 8 epilogue warps of the pair
+//               release the accumulator on the even CTA's `acc_empty` barrier.
+// Tiles are visited in groups of `group_m` 256-row blocks (all column blocks of a group before
+// the next group) so that the clusters running at the same time share A and B panels in L2.
+//
+// Fused epilogues: plain (alpha/beta with an optional bf16 or fp32 addend, which may alias the
+// output: in-place gradient accumulation), SwiGLU forward (the CTA pair loads matching gate and
+// up weight rows, writes gate|up for the backward and silu(gate) * up), and SwiGLU backward
+// (the down projection's input gradient turned into d[gate|up] from the saved gate|up).
+//
+// Every mbarrier wait is bounded by a run-time limit (default 2 s); on a timeout the kernel
+// records a status code, stops issuing work, waits (bounded) for its copies and MMAs, frees
+// TMEM and returns.  `inject` = 1 is a test hook: one epilogue warp withholds its first
+// accumulator release, so the MMA issuer's wait runs out (the timeout path without a GPU fault).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "tma.cuh"
+
+using namespace mimir;
+
+namespace {
+
+constexpr int kBM = 128;  // A rows per CTA (256 per pair)
+constexpr int kBK = 64;   // k per stage: one 128-byte swizzle row of bf16
+constexpr int kThreads = 192;
+constexpr int kEpiWarps = 4;
+
+enum EpiKind : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiSwiGLUBwd = 2 };
+
+struct GemmParams {
+  void* out;  // [M, N] bf16, or fp32 when the kernel's kOutF32 is set
+  int64_t ldo;
+  const void* add;  // optional addend of the output's dtype and shape (may alias `out`)
+  int64_t ldd;
+  float alpha, beta;
+  void* aux;  // SwiGLU: gate|up [M, 2F] bf16 (written by the forward, read by the backward)
+  int64_t ldx;
+  int ffn;  // SwiGLU: F
+  int M, N, K;
+  int tiles_m, tiles_n, group_m;
+  int* status;
+  unsigned long long wait_ns;
+  int inject;
+};
+
+template <int BN>
+struct PairCfg {
+  static constexpr int kBHalf = BN / 2;             // B rows staged per CTA
+  static constexpr int kABytes = kBM * kBK * 2;     // 16 KB
+  static constexpr int kBBytes = kBHalf * kBK * 2;  // 16 KB (BN 256) or 8 KB (BN 128)
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = 196608 / kStageBytes;  // 6 or 8 stages, 192 KB
+  static constexpr int kSmem = kStages * kStageBytes + 1024;
+  static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
+  static_assert(kStages <= 8, "barrier arrays hold 8 stages");
+};
+
+struct PairBars {
+  uint64_t full[8];
+  uint64_t empty[8];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t done;
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mt, int& nt) {
+  const int per_group = p.group_m * p.tiles_n;
+  const int g = t / per_group;
+  const int first = g * p.group_m;
+  const int gsize = min(p.group_m, p.tiles_m - first);
+  const int r = t - g * per_group;
+  mt = first + r % gsize;
+  nt = r / gsize;
+}
+
+__device__ __forceinline__ float silu_ref(float g) { return g / (1.f + __expf(-g)); }
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    d[q] = make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                      pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v)[32]) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 w = s[q];
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&words[e]));
+      v[8 * q + 2 * e] = f.x;
+      v[8 * q + 2 * e + 1] = f.y;
+    }
+  }
+}
+
+template <int BN, bool kAMn, bool kBMn, int kEpi, bool kOutF32>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                     const GemmParams p) {
+  using CF = PairCfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ PairBars bars;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  const int total = p.tiles_m * p.tiles_n;
+  const int nkb = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < CF::kStages; ++s) {
+      mbar_init(&bars.full[s], 1);
+      mbar_init(&bars.empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars.acc_full[i], 1);
+      mbar_init(&bars.acc_empty[i], 2 * kEpiWarps);
+    }
+    mbar_init(&bars.done, 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&bars.tmem_base, CF::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem = bars.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = cid; ok && t < total; t += ncl) {
+        int mt, nt;
+        tile_coords(t, p, mt, nt);
+        const int am = mt * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int bn = kEpi == kEpiSwiGLU ? nt * CF::kBHalf + (rank ? p.ffn : 0)  // gate rows | up rows
+                                          : nt * BN + static_cast<int>(rank) * CF::kBHalf;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % CF::kStages;
+          if (it >= CF::kStages && !mbar_wait_ns(&bars.empty[s], ((it / CF::kStages) - 1) & 1, p.status,
+                                                 kStatusTimeoutEmpty, p.wait_ns)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = smem_u32(smem + s * CF::kStageBytes);
+          const uint32_t sb = sa + CF::kABytes;
+          const uint32_t fb = mapa_shared(smem_u32(&bars.full[s]), 0);
+          if (leader) mbar_arrive_expect_tx(&bars.full[s], 2 * CF::kStageBytes);
+          const int k0 = kb * kBK;
+          if (kAMn) {
+#pragma unroll
+            for (int c = 0; c < kBM / 64; ++c) tma_load_2d_pair(sa + c * (kBK * 128), &map_a, fb, am + c * 64, k0);
+          } else {
+            tma_load_2d_pair(sa, &map_a, fb, k0, am);
+          }
+          if (kBMn) {
+#pragma unroll
+            for (int c = 0; c < CF::kBHalf / 64; ++c)
+              tma_load_2d_pair(sb + c * (kBK * 128), &map_b, fb, bn + c * 64, k0);
+          } else {
+            tma_load_2d_pair(sb, &map_b, fb, k0, bn);
+          }
+        }
+      }
+      // Tail: the last stages are released once the pair's MMAs have read them, which also
+      // means their copies have landed.
+      // After a timeout nothing releases the stages any more: give the copies in flight a fixed
+      // millisecond to land instead.
+      for (int j = max(0, it - CF::kStages); j < it; ++j) {
+        if (!mbar_wait_ns(&bars.empty[j % CF::kStages], (j / CF::kStages) & 1, p.status, kStatusTimeoutKV,
+                          p.wait_ns)) {
+          spin_ns(1000000ull);
+          break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(2 * kBM, BN, kAMn ? 1 : 0, kBMn ? 1 : 0);
+      int it = 0, i = 0;
+      bool ok = true;
+      for (int t = cid; ok && t < total; t += ncl, ++i) {
+        const int buf = i & 1;
+        if (i >= 2 &&
+            !mbar_wait_ns(&bars.acc_empty[buf], ((i >> 1) - 1) & 1, p.status, kStatusTimeoutO, p.wait_ns))
+          break;
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * BN;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % CF::kStages;
+          if (!mbar_wait_ns(&bars.full[s], (it / CF::kStages) & 1, p.status, kStatusTimeoutKV, p.wait_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * CF::kStageBytes);
+          const uint32_t sb = sa + CF::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // K-major: 16 k = 32 bytes along the swizzled row.  MN-major: 16 k-rows = 2048 bytes;
+            // the 64-wide column chunks sit kBK * 128 bytes apart (leading byte offset).
+            const uint64_t ad = kAMn ? smem_desc(sa + kk * 2048, kBK * 128, 1024, kLayoutSW128)
+                                     : smem_desc(sa + kk * 32, 16, 1024, kLayoutSW128);
+            const uint64_t bd = kBMn ? smem_desc(sb + kk * 2048, kBK * 128, 1024, kLayoutSW128)
+                                     : smem_desc(sb + kk * 32, 16, 1024, kLayoutSW128);
+            mma_bf16_pair(acc, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair(&bars.empty[s], 0x3);  // the stage is free in both CTAs once read
+        }
+        if (ok) mma_commit_pair(&bars.acc_full[buf], 0x3);
+      }
+      mma_commit_pair(&bars.done, 0x3);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int wq = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    int i = 0;
+    for (int t = cid; t < total; t += ncl, ++i) {
+      const int buf = i & 1;
+      if (!warp_wait_ns(&bars.acc_full[buf], (i >> 1) & 1, p.status, kStatusTimeoutS, p.wait_ns)) break;
+      tc_fence_after();
+      int mt, nt;
+      tile_coords(t, p, mt, nt);
+      const int row = mt * 2 * kBM + static_cast<int>(rank) * kBM + wq * 32 + lane;
+      const bool valid = row < p.M;
+      const uint32_t tacc = tmem + lane_off + buf * BN;
+      if (kEpi == kEpiStore) {
+        const int n0 = nt * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tacc + c * 32, v);
+          const int col = n0 + c * 32;
+          if (valid && col < p.N) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] *= p.alpha;
+            if (kOutF32) {
+              float* dst = reinterpret_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + col;
+              if (p.add != nullptr) {
+                const float4* src =
+                    reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.add) + static_cast<int64_t>(row) * p.ldd + col);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  const float4 a = src[q];
+                  v[4 * q] += p.beta * a.x;
+                  v[4 * q + 1] += p.beta * a.y;
+                  v[4 * q + 2] += p.beta * a.z;
+                  v[4 * q + 3] += p.beta * a.w;
+                }
+              }
+              float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            } else {
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + col;
+              if (p.add != nullptr) {
+                float a[32];
+                load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(p.add) + static_cast<int64_t>(row) * p.ldd + col, a);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) v[e] += p.beta * a[e];
+              }
+              store_bf16x32(dst, v);
+            }
+          }
+        }
+      } else if (kEpi == kEpiSwiGLU) {
+        // Columns [0, BN/2) of the accumulator are gate rows, [BN/2, BN) the matching up rows.
+        const int h0 = nt * CF::kBHalf;
+        __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(p.aux) + static_cast<int64_t>(row) * p.ldx;
+        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo;
+#pragma unroll 1
+        for (int c = 0; c < CF::kBHalf / 32; ++c) {
+          float g[32], u[32];
+          tmem_ld32(tacc + c * 32, g);
+          tmem_ld32(tacc + CF::kBHalf + c * 32, u);
+          if (valid) {
+            const int col = h0 + c * 32;
+            store_bf16x32(gu + col, g);
+            store_bf16x32(gu + p.ffn + col, u);
+            // The backward reads the bf16 gate|up, so the product is formed from the rounded values.
+#pragma unroll
+            for (int e = 0; e < 32; ++e) g[e] = silu_ref(bf16_round(g[e])) * bf16_round(u[e]);
+            store_bf16x32(h + col, g);
+          }
+        }
+      } else {  // kEpiSwiGLUBwd: accumulator = d(silu(gate) * up) for columns n0 .. n0 + BN of F
+        const int n0 = nt * BN;
+        const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(p.aux) + static_cast<int64_t>(row) * p.ldx;
+        __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float d[32];
+          tmem_ld32(tacc + c * 32, d);
+          const int col = n0 + c * 32;
+          if (valid && col < p.N) {
+            float g[32], u[32];
+            load_bf16x32(gu + col, g);
+            load_bf16x32(gu + p.ffn + col, u);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float de = bf16_round(d[e]);
+              const float s = 1.f / (1.f + __expf(-g[e]));
+              const float du = de * g[e] * s;
+              g[e] = de * u[e] * s * (1.f + g[e] * (1.f - s));
+              u[e] = du;
+            }
+            store_bf16x32(dgu + col, g);
+            store_bf16x32(dgu + p.ffn + col, u);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      const bool withhold = p.inject == 1 && i == 0 && leader && wq == 0;
+      if (lane == 0 && !withhold) mbar_arrive_remote(mapa_shared(smem_u32(&bars.acc_empty[buf]), 0));
+    }
+    // Every MMA that writes this CTA's TMEM has completed before TMEM is freed (the last
+    // accumulator was just read, so in a normal run this wait is short).
+    if (warp == 2 && lane == 0) mbar_wait_ns(&bars.done, 0, p.status, kStatusTimeoutOther, p.wait_ns);
+    __syncwarp();
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, CF::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------ host side
+int* status_word(int device) {
+  static int* words[64] = {nullptr};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (words[device] == nullptr) {
+    C10_CUDA_CHECK(cudaMalloc(&words[device], sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(words[device], 0, sizeof(int)));
+  }
+  return words[device];
+}
+
+// Number of CTA pairs that can be resident at once (the persistent grid), per device.
+int resident_pairs(int device, const void* kernel, int smem) {
+  static int cached[64] = {0};
+  if (cached[device] > 0) return cached[device];
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  int sms = 0;
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  cfg.gridDim = dim3(sms & ~1);
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters <= 0) {
+    (void)cudaGetLastError();
+    clusters = sms / 2;
+  }
+  cached[device] = clusters;
+  return clusters;
+}
+
+template <int BN, bool kAMn, bool kBMn, int kEpi, bool kOutF32>
+void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int device, cudaStream_t st) {
+  using CF = PairCfg<BN>;
+  auto kernel = gemm_pair_kernel<BN, kAMn, kBMn, kEpi, kOutF32>;
+  static bool attr[64] = {false};
+  if (!attr[device]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kSmem));
+    attr[device] = true;
+  }
+  const int pairs = std::min(resident_pairs(device, reinterpret_cast<const void*>(kernel), CF::kSmem),
+                             p.tiles_m * p.tiles_n);
+  kernel<<<2 * pairs, kThreads, CF::kSmem, st>>>(ma, mb, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void check_operand(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.stride(1) == 1, name,
+              ": bf16 CUDA matrix with unit column stride");
+  TORCH_CHECK((t.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name,
+              ": 16-byte aligned base and row stride");
+}
+
+template <int BN>
+void dispatch_store(bool a_mn, bool b_mn, bool f32, const CUtensorMap& ma, const CUtensorMap& mb,
+                    const GemmParams& p, int dev, cudaStream_t st) {
+  const int code = (a_mn ? 4 : 0) | (b_mn ? 2 : 0) | (f32 ? 1 : 0);
+  switch (code) {
+    case 0: launch_pair<BN, false, false, kEpiStore, false>(ma, mb, p, dev, st); break;
+    case 1: launch_pair<BN, false, false, kEpiStore, true>(ma, mb, p, dev, st); break;
+    case 2: launch_pair<BN, false, true, kEpiStore, false>(ma, mb, p, dev, st); break;
+    case 3: launch_pair<BN, false, true, kEpiStore, true>(ma, mb, p, dev, st); break;
+    case 6: launch_pair<BN, true, true, kEpiStore, false>(ma, mb, p, dev, st); break;
+    case 7: launch_pair<BN, true, true, kEpiStore, true>(ma, mb, p, dev, st); break;
+    default: TORCH_CHECK(false, "unsupported operand layout: an M-major A needs an N-major B");
+  }
+}
+
+GemmParams base_params(int M, int N, int K, int BN, int64_t group_m, int64_t wait_ns, int64_t inject, int device) {
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.alpha = 1.f;
+  p.beta = 0.f;
+  p.tiles_m = (M + 2 * kBM - 1) / (2 * kBM);
+  p.tiles_n = (N + BN - 1) / BN;
+  p.group_m = static_cast<int>(std::max<int64_t>(1, group_m));
+  p.status = status_word(device);
+  p.wait_ns = wait_ns > 0 ? static_cast<unsigned long long>(wait_ns) : 2000000000ull;
+  p.inject = static_cast<int>(inject);
+  return p;
+}
+
+}  // namespace
+
+// out[M, N] = alpha * op(a) @ op(b)^T (+ beta * add).  a: [M, K] (a_mn = false) or [K, M] (a_mn =
+// true); b: [N, K] (b_mn = false) or [K, N] (b_mn = true).  `out` (bf16 or fp32) is allocated as
+// bf16 when absent; `add` has out's dtype and may be `out` itself (in-place accumulation).
+at::Tensor gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, c10::optional<at::Tensor> out,
+                c10::optional<at::Tensor> add, double alpha, double beta, int64_t bn, int64_t group_m,
+                int64_t wait_ns, int64_t inject) {
+  check_operand(a, "a");
+  check_operand(b, "b");
+  const int64_t M = a_mn ? a.size(1) : a.size(0), K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "inner dimensions differ");
+  TORCH_CHECK(!a_mn || b_mn, "an M-major A needs an N-major B");
+  TORCH_CHECK(N % 32 == 0, "N must be a multiple of 32");  // inner extents are checked by the TMA maps
+  TORCH_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "dimensions must fit in int32");
+  const c10::cuda::CUDAGuard guard(a.device());
+  at::Tensor o = out.has_value() ? *out : at::empty({M, N}, a.options());
+  TORCH_CHECK(o.is_cuda() && o.dim() == 2 && o.size(0) == M && o.size(1) == N && o.stride(1) == 1 &&
+                  (o.scalar_type() == at::kBFloat16 || o.scalar_type() == at::kFloat),
+              "out: [M, N] bf16 or fp32 with unit column stride");
+  const bool f32 = o.scalar_type() == at::kFloat;
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(o.data_ptr()) % 16 == 0 && (o.stride(0) * o.element_size()) % 16 == 0,
+              "out: 16-byte aligned base and row stride");
+  if (M == 0 || N == 0) return o;
+  const int BN = bn == 128 ? 128 : 256;
+  const int dev = a.device().index();
+  GemmParams p = base_params(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), BN, group_m, wait_ns,
+                             inject, dev);
+  p.out = o.data_ptr();
+  p.ldo = o.stride(0);
+  p.alpha = static_cast<float>(alpha);
+  if (add.has_value() && beta != 0.0) {
+    const auto& d = *add;
+    TORCH_CHECK(d.scalar_type() == o.scalar_type() && d.dim() == 2 && d.size(0) == M && d.size(1) == N &&
+                    d.stride(1) == 1 && reinterpret_cast<uintptr_t>(d.data_ptr()) % 16 == 0 &&
+                    (d.stride(0) * d.element_size()) % 16 == 0,
+                "add: same dtype and shape as out, 16-byte aligned");
+    p.add = d.data_ptr();
+    p.ldd = d.stride(0);
+    p.beta = static_cast<float>(beta);
+  }
+  if (K == 0) {  // no products: the result is the scaled addend (or zero)
+    if (p.add != nullptr) o.copy_(add->mul(beta));
+    else o.zero_();
+    return o;
+  }
+  const CUtensorMap ma = a_mn ? make_tmap_bf16_2d(a.data_ptr(), K, M, a.stride(0), 64, kBK)
+                              : make_tmap_bf16_2d(a.data_ptr(), M, K, a.stride(0), kBK, kBM);
+  const CUtensorMap mb = b_mn ? make_tmap_bf16_2d(b.data_ptr(), K, N, b.stride(0), 64, kBK)
+                              : make_tmap_bf16_2d(b.data_ptr(), N, K, b.stride(0), kBK, BN / 2);
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (BN == 256) dispatch_store<256>(a_mn, b_mn, f32, ma, mb, p, dev, st);
+  else dispatch_store<128>(a_mn, b_mn, f32, ma, mb, p, dev, st);
+  return o;
+}
+
+// Forward of a SwiGLU MLP's first projection: gu = x @ w_gu^T (w_gu = [gate rows; up rows],
+// [2F, K]) and h = silu(gate) * up, both bf16.  Returns {h [M, F], gu [M, 2F]}.
+std::vector<at::Tensor> gemm_swiglu(at::Tensor x, at::Tensor w_gu, int64_t group_m) {
+  check_operand(x, "x");
+  check_operand(w_gu, "w_gu");
+  const int64_t M = x.size(0), K = x.size(1), F = w_gu.size(0) / 2;
+  TORCH_CHECK(w_gu.size(1) == K && w_gu.size(0) == 2 * F, "w_gu: [2F, K]");
+  TORCH_CHECK(F % 128 == 0, "F must be a multiple of 128");
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor h = at::empty({M, F}, x.options());
+  at::Tensor gu = at::empty({M, 2 * F}, x.options());
+  if (M == 0) return {h, gu};
+  constexpr int BN = 256;  // 128 gate + 128 up columns per tile: 128 columns of h
+  const int dev = x.device().index();
+  GemmParams p = base_params(static_cast<int>(M), static_cast<int>(F), static_cast<int>(K), BN, group_m, 0, 0, dev);
+  p.tiles_n = static_cast<int>(F / (BN / 2));
+  p.out = h.data_ptr();
+  p.ldo = h.stride(0);
+  p.aux = gu.data_ptr();
+  p.ldx = gu.stride(0);
+  p.ffn = static_cast<int>(F);
+  const CUtensorMap ma = make_tmap_bf16_2d(x.data_ptr(), M, K, x.stride(0), kBK, kBM);
+  const CUtensorMap mb = make_tmap_bf16_2d(w_gu.data_ptr(), 2 * F, K, w_gu.stride(0), kBK, BN / 2);
+  launch_pair<256, false, false, kEpiSwiGLU, false>(ma, mb, p, dev, at::cuda::getCurrentCUDAStream());
+  return {h, gu};
+}
+
+// Input gradient of a SwiGLU MLP's down projection fused with the SwiGLU backward:
+// dh = dy @ w_down (w_down = [D, F]), then d[gate|up] from the saved bf16 gate|up.  Returns
+// dgu [M, 2F] bf16.
+at::Tensor gemm_swiglu_bwd(at::Tensor dy, at::Tensor w_down, at::Tensor gu, int64_t group_m) {
+  check_operand(dy, "dy");
+  check_operand(w_down, "w_down");
+  check_operand(gu, "gu");
+  const int64_t M = dy.size(0), D = dy.size(1), F = w_down.size(1);
+  TORCH_CHECK(w_down.size(0) == D && gu.size(0) == M && gu.size(1) == 2 * F, "shapes: dy [M, D], w_down [D, F], gu [M, 2F]");
+  TORCH_CHECK(F % 32 == 0, "F must be a multiple of 32");
+  const c10::cuda::CUDAGuard guard(dy.device());
+  at::Tensor dgu = at::empty({M, 2 * F}, dy.options());
+  if (M == 0) return dgu;
+  const int dev = dy.device().index();
+  GemmParams p = base_params(static_cast<int>(M), static_cast<int>(F), static_cast<int>(D), 256, group_m, 0, 0, dev);
+  p.out = dgu.data_ptr();
+  p.ldo = dgu.stride(0);
+  p.aux = gu.data_ptr();
+  p.ldx = gu.stride(0);
+  p.ffn = static_cast<int>(F);
+  const CUtensorMap ma = make_tmap_bf16_2d(dy.data_ptr(), M, D, dy.stride(0), kBK, kBM);
+  const CUtensorMap mb = make_tmap_bf16_2d(w_down.data_ptr(), D, F, w_down.stride(0), 64, kBK);
+  launch_pair<256, false, true, kEpiSwiGLUBwd, false>(ma, mb, p, dev, at::cuda::getCurrentCUDAStream());
+  return dgu;
+}
+
+// Reads and clears the dense GEMM kernels' status word of `device` (0 = every wait completed).
+int64_t gemm_status(int64_t device) {
+  int* w = status_word(static_cast<int>(device));
+  int host = 0;
+  C10_CUDA_CHECK(cudaMemcpy(&host, w, sizeof(int), cudaMemcpyDeviceToHost));
+  if (host != 0) C10_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
+  return host;
+}

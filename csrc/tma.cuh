@@ -22,12 +22,24 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
+// The driver-level encoder needs a current CUDA context.  A host thread that has made no CUDA
+// runtime call yet (the autograd engine's worker thread, a Python thread) has none, and
+// c10::cuda::CUDAGuard does not create one when the device index already matches; cudaSetDevice
+// binds the device's primary context to the calling thread.  Once per thread and device.
+inline void bind_device_context() {
+  thread_local int bound = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  if (bound != dev && cudaSetDevice(dev) == cudaSuccess) bound = dev;
+}
+
 // Row-major bf16 matrix [rows, cols] with leading dimension `ld` (elements); box is
 // {box_cols (inner), box_rows}.  base must be 16-byte aligned, ld*2 a multiple of 16.
 inline CUtensorMap make_tmap_bf16_2d(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_cols,
                                      int box_rows, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
   TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  bind_device_context();
   CUtensorMap map;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
@@ -46,6 +58,7 @@ inline CUtensorMap make_tmap_f32_2d(const void* base, int64_t rows, int64_t cols
                                     int box_rows) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
   TORCH_CHECK((ld * 4) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  bind_device_context();
   CUtensorMap map;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};

@@ -6,8 +6,10 @@ attention ``:118-253``, ``SwiGLU`` ``:256-287``).  Parameter names and shapes ar
 identical so DCP checkpoints are interchangeable.
 
 On CUDA the training path of :class:`Attention` and :class:`SwiGLU` runs through the
-hand-written sm_100a kernels in :mod:`mimir_b200.ops` (RoPE, single-pass prefix-LM
-attention with the ``sigmoid(gate)`` epilogue fused, SwiGLU).  On CPU, and for cached
+hand-written sm_100a kernels in :mod:`mimir_b200.ops`: every projection is the tcgen05
+CTA-pair GEMM (``ops.linear``), the SwiGLU MLP is two fused GEMMs per direction
+(``ops.swiglu_mlp``), and attention is the single-pass prefix-LM kernel with RoPE and the
+``sigmoid(gate)`` epilogue fused.  On CPU, and for cached
 decode or stability diagnostics, the plain PyTorch formulation below is used; it is also
 the numerical oracle for the kernels.
 """
@@ -69,7 +71,7 @@ class LinearInit(nn.Module):
         self.bias = nn.Parameter(torch.zeros((rows,), **kwargs)) if bias else None
 
     def forward(self, x: Tensor) -> Tensor:
-        return F.linear(x, self.weight, self.bias)
+        return ops.linear(x, self.weight, self.bias)
 
 
 class ScaledEmbeddingInit(nn.Module):
@@ -208,6 +210,9 @@ class SwiGLU(nn.Module):
         self.down_proj = LinearInit(intermediate_size, hidden_size, bias=False, init_std=init_std_out, **kwargs)
 
     def forward(self, x, stability_diagnostics=None, stability_scope=None):
+        if stability_diagnostics is None and ops.swiglu_mlp_supported(x, self.gate_up_proj.weight,
+                                                                      self.down_proj.weight):
+            return ops.swiglu_mlp(x, self.gate_up_proj.weight, self.down_proj.weight)
         gu = self.gate_up_proj(x)
         if stability_diagnostics is None:
             return self.down_proj(ops.swiglu(gu))

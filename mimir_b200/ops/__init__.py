@@ -13,3 +13,4 @@ from mimir_b200.ops.loss import linear_cross_entropy, linear_cross_entropy_refer
 from mimir_b200.ops.moe import moe_plan  # noqa: F401
 from mimir_b200.ops.ngram import ngram_lookup  # noqa: F401
 from mimir_b200.ops.embedding import scaled_embedding  # noqa: F401
+from mimir_b200.ops.gemm import linear, swiglu_mlp, swiglu_mlp_supported  # noqa: F401
