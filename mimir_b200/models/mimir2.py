@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import copy
 import math
+from dataclasses import dataclass
 from typing import Optional, Literal
 
 import torch
@@ -89,67 +90,156 @@ class Mimir2Config(RecurrentConfig):
 
     @model_validator(mode="after")
     def _validate(self):
-        h_layers = self.H_override.get("n_layers", self.n_layers)
-        looped = self.recurrence_mode == "looped"
-        if self.moe_aux_loss_free and self.moe_num_experts < 2:
-            raise ValueError("MoE balancing requires multiple MoE experts")
-        if self.mos_aux_loss_free and self.mos_num_experts < 2:
-            raise ValueError("MoS balancing requires multiple MoS experts")
-        if self.n_layers < 1 or h_layers < 0:
-            raise ValueError("L requires positive layers and H requires nonnegative layers")
-        if h_layers == 0 and not looped:
-            raise ValueError("Zero-layer H requires looped recurrence")
-        if self.h_residual_persistence or self.h_branch_l_mixing:
-            if (looped or h_layers == 0 or self.residual_branches < 2 or self.residual_levels not in ("H", "both")):
-                raise ValueError("H stream options require hierarchical recurrence and multiple H residual branches")
-            if self.h_memory_branches > 1:
-                raise ValueError("H stream options cannot be combined with H recurrent memory")
-            if self.gate_initialize_from_v1:
-                raise ValueError("H stream options require explicit upcycling, not gate-only migration")
-        if self.h_branch_l_mixing and (self.mos_num_experts < 2 or self.l_memory_branches > 1):
-            raise ValueError("Branch-specific L mixing requires MoS and no L recurrent memory")
-        if looped and (self.gates_enabled or self.h_memory_branches > 1 or self.l_memory_branches > 1
-                       or self.mos_state_mode != "shared"):
-            raise ValueError("Looped recurrence requires shared MoS state, no invocation gates, "
-                             "and no recurrent memory branches; residual branches are supported")
-        if self.mos_sparse and self.mos_sparse_routing == "prefix_mean" and self.attn_type != "prefixlm":
-            raise ValueError("Prefix-mean routing requires PrefixLM prompt visibility")
-        for rows, count in ((self.moe_metadata_bias, self.moe_num_experts), (self.mos_metadata_bias, self.mos_num_experts)):
-            if any(len(r) != count or not all(math.isfinite(v) for v in r) for r in rows):
-                raise ValueError("Metadata bias rows must contain one finite logit per expert")
-        if self.routing_bias_decay_end and self.routing_bias_decay_end <= self.routing_bias_decay_start:
-            raise ValueError("Routing bias decay end must follow start")
-        if self.specialist_training and not self.expert_freeze_base:
-            raise ValueError("Specialist training requires a frozen reference expert")
-        if self.mos_state_mode == "separate" and self.l_memory_branches > 1:
-            raise ValueError("Choose expert-specific L states or general L memory branches, not both")
-        if self.upcycle_from_dense and self.gate_initialize_from_v1:
-            raise ValueError("Use only one migration mode")
-        if self.gate_initialize_from_v1 and not self.gates_enabled:
-            raise ValueError("gate_initialize_from_v1 requires gates_enabled=true")
-        if (self.moe_dispatch == "grouped" or self.moe_expert_parallel) and not (self.moe_sparse
-                                                                               and self.moe_num_experts > 1):
-            raise ValueError("The grouped MoE dispatch and expert parallelism need moe_sparse with several experts")
-        if self.moe_expert_parallel and self.moe_dispatch != "grouped":
-            raise ValueError("moe_expert_parallel requires moe_dispatch=grouped")
-        if self.upcycle_from_dense and (self.moe_expert_intermediate_size is not None or self.moe_shared_experts):
-            raise ValueError("Upcycling copies the dense MLP: it needs the dense expert width and no shared experts")
-        if self.moe_expert_parallel and (self.specialist_training or self.expert_freeze_base):
-            raise ValueError("Expert parallelism does not support specialist training or a frozen base expert")
-        if self.moe_top_k > self.moe_num_experts or self.mos_top_k > self.mos_num_experts:
-            raise ValueError("Expert top_k must not exceed num_experts")
-        if self.gate_initialize_from_v1 and (self.moe_num_experts > 1 or self.mos_num_experts > 1
-                                             or self.residual_branches > 1):
-            raise ValueError("Expert/branch upcycling requires upcycle_from_dense; "
-                             "gate_initialize_from_v1 only migrates gates")
-        if self.residual_branches > 1:
-            for level in ("L", "H"):
-                norm = self.H_override.get("norm_type", self.norm_type) if level == "H" else self.norm_type
-                if self.residual_levels in (level, "both") and norm != "pre":
-                    raise ValueError("Multiple residual branches currently require pre-norm")
-        if self.expert_freeze_base and self.moe_num_experts == self.mos_num_experts == 1:
-            raise ValueError("expert_freeze_base requires an expert mixture")
+        derived = _Derived(self)
+        for broken, message in _CONFIG_RULES:
+            if broken(self, derived):
+                raise ValueError(message)
         return self
+
+
+class _Derived:
+    """Quantities several configuration rules share."""
+
+    def __init__(self, cfg):
+        self.h_layers = cfg.H_override.get("n_layers", cfg.n_layers)
+        self.looped = cfg.recurrence_mode == "looped"
+        self.h_stream_options = cfg.h_residual_persistence or cfg.h_branch_l_mixing
+        self.norms = {"L": cfg.norm_type, "H": cfg.H_override.get("norm_type", cfg.norm_type)}
+
+
+def _bad_metadata_rows(cfg) -> bool:
+    tables = ((cfg.moe_metadata_bias, cfg.moe_num_experts), (cfg.mos_metadata_bias, cfg.mos_num_experts))
+    return any(len(row) != count or not all(math.isfinite(v) for v in row) for rows, count in tables for row in rows)
+
+
+def _non_prenorm_branches(cfg, d: _Derived) -> bool:
+    return cfg.residual_branches > 1 and any(
+        cfg.residual_levels in (level, "both") and d.norms[level] != "pre" for level in ("L", "H"))
+
+
+# (rule violated?, message) in the order they are checked; the messages are the user interface.
+_CONFIG_RULES = (
+    (lambda c, d: c.moe_aux_loss_free and c.moe_num_experts < 2, "MoE balancing requires multiple MoE experts"),
+    (lambda c, d: c.mos_aux_loss_free and c.mos_num_experts < 2, "MoS balancing requires multiple MoS experts"),
+    (lambda c, d: c.n_layers < 1 or d.h_layers < 0, "L requires positive layers and H requires nonnegative layers"),
+    (lambda c, d: d.h_layers == 0 and not d.looped, "Zero-layer H requires looped recurrence"),
+    (lambda c, d: d.h_stream_options and (d.looped or d.h_layers == 0 or c.residual_branches < 2
+                                          or c.residual_levels not in ("H", "both")),
+     "H stream options require hierarchical recurrence and multiple H residual branches"),
+    (lambda c, d: d.h_stream_options and c.h_memory_branches > 1,
+     "H stream options cannot be combined with H recurrent memory"),
+    (lambda c, d: d.h_stream_options and c.gate_initialize_from_v1,
+     "H stream options require explicit upcycling, not gate-only migration"),
+    (lambda c, d: c.h_branch_l_mixing and (c.mos_num_experts < 2 or c.l_memory_branches > 1),
+     "Branch-specific L mixing requires MoS and no L recurrent memory"),
+    (lambda c, d: d.looped and (c.gates_enabled or c.h_memory_branches > 1 or c.l_memory_branches > 1
+                                or c.mos_state_mode != "shared"),
+     "Looped recurrence requires shared MoS state, no invocation gates, and no recurrent memory branches; "
+     "residual branches are supported"),
+    (lambda c, d: c.mos_sparse and c.mos_sparse_routing == "prefix_mean" and c.attn_type != "prefixlm",
+     "Prefix-mean routing requires PrefixLM prompt visibility"),
+    (lambda c, d: _bad_metadata_rows(c), "Metadata bias rows must contain one finite logit per expert"),
+    (lambda c, d: bool(c.routing_bias_decay_end) and c.routing_bias_decay_end <= c.routing_bias_decay_start,
+     "Routing bias decay end must follow start"),
+    (lambda c, d: c.specialist_training and not c.expert_freeze_base,
+     "Specialist training requires a frozen reference expert"),
+    (lambda c, d: c.mos_state_mode == "separate" and c.l_memory_branches > 1,
+     "Choose expert-specific L states or general L memory branches, not both"),
+    (lambda c, d: c.upcycle_from_dense and c.gate_initialize_from_v1, "Use only one migration mode"),
+    (lambda c, d: c.gate_initialize_from_v1 and not c.gates_enabled,
+     "gate_initialize_from_v1 requires gates_enabled=true"),
+    (lambda c, d: (c.moe_dispatch == "grouped" or c.moe_expert_parallel)
+     and not (c.moe_sparse and c.moe_num_experts > 1),
+     "The grouped MoE dispatch and expert parallelism need moe_sparse with several experts"),
+    (lambda c, d: c.moe_expert_parallel and c.moe_dispatch != "grouped",
+     "moe_expert_parallel requires moe_dispatch=grouped"),
+    (lambda c, d: c.upcycle_from_dense and (c.moe_expert_intermediate_size is not None or c.moe_shared_experts),
+     "Upcycling copies the dense MLP: it needs the dense expert width and no shared experts"),
+    (lambda c, d: c.moe_expert_parallel and (c.specialist_training or c.expert_freeze_base),
+     "Expert parallelism does not support specialist training or a frozen base expert"),
+    (lambda c, d: c.moe_top_k > c.moe_num_experts or c.mos_top_k > c.mos_num_experts,
+     "Expert top_k must not exceed num_experts"),
+    (lambda c, d: c.gate_initialize_from_v1 and (c.moe_num_experts > 1 or c.mos_num_experts > 1
+                                                 or c.residual_branches > 1),
+     "Expert/branch upcycling requires upcycle_from_dense; gate_initialize_from_v1 only migrates gates"),
+    (lambda c, d: _non_prenorm_branches(c, d), "Multiple residual branches currently require pre-norm"),
+    (lambda c, d: c.expert_freeze_base and c.moe_num_experts == c.mos_num_experts == 1,
+     "expert_freeze_base requires an expert mixture"),
+)
+
+
+@dataclass(frozen=True)
+class _Call:
+    level: str   # "L" or "H"
+    slot: int    # invocation index within the level (gate and cache slot)
+    grad: bool   # inside the truncated-BPTT window
+
+
+def _schedule(h_cycles: int, l_cycles: int, h_window: int, l_window: int) -> list[_Call]:
+    """Per H cycle: its L invocations, then its H invocation.  The last ``l_window`` L calls and
+    the last ``h_window`` H calls record autograd state."""
+    l_total = h_cycles * l_cycles
+    calls = []
+    for i in range(h_cycles):
+        calls.extend(_Call("L", k, k >= l_total - l_window) for k in range(i * l_cycles, (i + 1) * l_cycles))
+        calls.append(_Call("H", i, i >= h_cycles - h_window))
+    return calls
+
+
+class _Pass:
+    """State of one v2 forward: the two stack states, recurrent memories, MoS expert states and
+    routes, per-level extra inputs (routing biases) and the current cycle's L context."""
+
+    def __init__(self, model, x, cache, diagnostics, seq_info, category):
+        cfg = model.gate_config
+        self.model, self.cache, self.diagnostics = model, cache, diagnostics
+        self.looped = cfg.recurrence_mode == "looped"
+        self.mixture = cfg.mos_num_experts > 1
+        self.z_H, self.z_L = x, model.zL_init
+        self.h_streams = model.H_level.core.initialize_streams(x) if cfg.h_residual_persistence else None
+        self.memory_modules, self.memories = {}, {}
+        for name, start in (("H", self.z_H), ("L", self.z_L)):
+            memory = getattr(getattr(model, f"{name}_level"), "memory", None)
+            if memory is not None:
+                self.memory_modules[name] = memory
+                self.memories[name] = memory.initialize(start.expand_as(x))
+        moe_bias = model._metadata_bias(category, "moe")
+        self.mos_bias = model._metadata_bias(category, "mos")
+        self.info = {}
+        for name in ("L", "H"):
+            self.info[name] = dict(seq_info)
+            if moe_bias is not None and cfg.moe_levels in (name, "both"):
+                self.info[name]["routing_bias"] = moe_bias
+        self.routes = None
+        if self.mixture and cfg.mos_sparse:
+            from mimir_b200.models.sparse_stacks import cached_sequence_routes, sequence_routes
+            self.routes = (sequence_routes(model.L_level.stack_router, x, seq_info, self.mos_bias,
+                                           cfg.mos_sparse_routing) if cache is None
+                           else cached_sequence_routes(model, x, cache, seq_info, self.mos_bias))
+        separate = self.mixture and cfg.mos_state_mode == "separate"
+        self.states = [model.zL_init] * cfg.mos_num_experts if separate else None
+        self.context = None
+        self.collect = None
+
+    def begin_cycle(self) -> None:
+        """Start of an H cycle: looped recurrence restarts L from H and gives it no H context
+        (None stands for a zero context)."""
+        if self.looped:
+            self.z_L = self.z_H
+        self.context = None if self.looped else self.z_H
+
+    def _attr(self, level: str) -> str:
+        return "z_H" if level == "H" else "z_L"
+
+    def read_memory(self, level: str) -> None:
+        if level in self.memories:
+            setattr(self, self._attr(level), self.memory_modules[level].read_state(self.memories[level]))
+
+    def write_memory(self, level: str) -> None:
+        if level in self.memories:
+            memory = self.memory_modules[level]
+            self.memories[level] = memory.update(self.memories[level], getattr(self, self._attr(level)))
+            setattr(self, self._attr(level), memory.read_state(self.memories[level]))
 
 
 class InvocationGate(nn.Module):
@@ -168,6 +258,11 @@ class InvocationGate(nn.Module):
 
 
 class Mimir2(RecurrentBackbone):
+    """The v1 backbone plus the opt-in v2 features.  Features are installed in a fixed order (per
+    level L then H: MLP mixtures, routed blocks, residual branches; then the H branch mixer, MoS
+    stacks, invocation gates, recurrent memories, routing-bias scale, n-gram memory): the order
+    fixes RNG consumption and parameter names, which checkpoints depend on."""
+
     def __init__(self, config_dict):
         config = Mimir2Config(**config_dict)
         if config.H_cycles < 1 or config.L_cycles < 1:
@@ -175,36 +270,15 @@ class Mimir2(RecurrentBackbone):
         super().__init__(config_dict)
         self.gate_config = config
         self.has_h_stack = config.H_override.get("n_layers", config.n_layers) > 0
-        router_opts = dict(freeze_base=config.expert_freeze_base,
-                           top1_straight_through=config.router_top1_straight_through)
+        self._router_options = dict(freeze_base=config.expert_freeze_base,
+                                    top1_straight_through=config.router_top1_straight_through)
         for name in ("L", "H"):
-            level = getattr(self, f"{name}_level")
-            if name == "H" and not self.has_h_stack:
-                continue
-            if config.moe_levels in (name, "both"):
-                install_mlp_mixtures(level.core, self.hidden_size, config.moe_num_experts, config.moe_top_k,
-                                     sparse=config.moe_sparse, balance_enabled=config.moe_aux_loss_free,
-                                     balance_update_rate=config.routing_bias_update_rate,
-                                     expert_intermediate_size=config.moe_expert_intermediate_size,
-                                     shared_experts=config.moe_shared_experts, grouped=config.moe_dispatch == "grouped",
-                                     expert_parallel=config.moe_expert_parallel,
-                                     router_init_std=config.moe_router_init_std, **router_opts)
-                if config.moe_num_experts > 1:
-                    norm = config.H_override.get("norm_type", config.norm_type) if name == "H" else config.norm_type
-                    level.core.layers = nn.ModuleList(RoutedBlock(b, norm) for b in level.core.layers)
-            if config.residual_branches > 1 and config.residual_levels in (name, "both"):
-                level.core = BranchedTransformer(level.core, config.residual_branches, config.residual_write_init_scale,
-                                                 config.residual_input_dependent)
+            if name == "L" or self.has_h_stack:
+                self._install_level(name, getattr(self, f"{name}_level"))
         if config.h_branch_l_mixing:
             self.H_level.l_branch_mixer = BranchExpertMixer(config.residual_branches, config.mos_num_experts)
         if config.mos_num_experts > 1:
-            self.L_level.stack_experts = nn.ModuleList(copy.deepcopy(self.L_level.core)
-                                                       for _ in range(config.mos_num_experts - 1))
-            self.L_level.stack_router = TopKRouter(self.hidden_size, config.mos_num_experts, config.mos_top_k,
-                                                   balance_enabled=config.mos_aux_loss_free,
-                                                   balance_update_rate=config.routing_bias_update_rate, **router_opts)
-            if config.expert_freeze_base:
-                self.L_level.core.requires_grad_(False)
+            self._install_stack_mixture()
         if config.gates_enabled:
             self.H_level.invocation_gates = nn.ModuleList(InvocationGate(self.hidden_size) for _ in range(self.H_cycles))
             self.L_level.invocation_gates = nn.ModuleList(InvocationGate(self.hidden_size)
@@ -219,12 +293,48 @@ class Mimir2(RecurrentBackbone):
         if self.ngram_enabled:
             self.ngram = NGramMemory(self.hidden_size, config.ngram_orders, config.ngram_buckets, config.ngram_heads,
                                      config.ngram_contextual_gate)
-        if (config.ngram_orders or config.h_memory_branches > 1 or config.l_memory_branches > 1 or config.moe_sparse
-                or config.mos_sparse or config.residual_input_dependent or config.h_residual_persistence
-                or config.h_branch_l_mixing):
+        if self._needs_explicit_checkpoint(config):
             for m in self.modules():
                 if isinstance(m, TransformerBlock):
                     m._v2_explicit_checkpoint = True
+
+    def _install_level(self, name, level):
+        """MLP mixtures (and routed blocks), then residual branches, on one level's stack."""
+        cfg = self.gate_config
+        if cfg.moe_levels in (name, "both"):
+            install_mlp_mixtures(level.core, self.hidden_size, cfg.moe_num_experts, cfg.moe_top_k,
+                                 sparse=cfg.moe_sparse, balance_enabled=cfg.moe_aux_loss_free,
+                                 balance_update_rate=cfg.routing_bias_update_rate,
+                                 expert_intermediate_size=cfg.moe_expert_intermediate_size,
+                                 shared_experts=cfg.moe_shared_experts, grouped=cfg.moe_dispatch == "grouped",
+                                 expert_parallel=cfg.moe_expert_parallel, router_init_std=cfg.moe_router_init_std,
+                                 **self._router_options)
+            if cfg.moe_num_experts > 1:
+                norm = cfg.H_override.get("norm_type", cfg.norm_type) if name == "H" else cfg.norm_type
+                level.core.layers = nn.ModuleList(RoutedBlock(block, norm) for block in level.core.layers)
+        if cfg.residual_branches > 1 and cfg.residual_levels in (name, "both"):
+            level.core = BranchedTransformer(level.core, cfg.residual_branches, cfg.residual_write_init_scale,
+                                             cfg.residual_input_dependent)
+
+    def _install_stack_mixture(self):
+        """MoS: copies of the L stack as extra experts and a stack router."""
+        cfg = self.gate_config
+        self.L_level.stack_experts = nn.ModuleList(copy.deepcopy(self.L_level.core)
+                                                   for _ in range(cfg.mos_num_experts - 1))
+        self.L_level.stack_router = TopKRouter(self.hidden_size, cfg.mos_num_experts, cfg.mos_top_k,
+                                               balance_enabled=cfg.mos_aux_loss_free,
+                                               balance_update_rate=cfg.routing_bias_update_rate,
+                                               **self._router_options)
+        if cfg.expert_freeze_base:
+            self.L_level.core.requires_grad_(False)
+
+    @staticmethod
+    def _needs_explicit_checkpoint(cfg) -> bool:
+        """Features whose blocks must be checkpointed explicitly (their state is not a plain
+        sequential function of the block input)."""
+        return bool(cfg.ngram_orders or cfg.h_memory_branches > 1 or cfg.l_memory_branches > 1 or cfg.moe_sparse
+                    or cfg.mos_sparse or cfg.residual_input_dependent or cfg.h_residual_persistence
+                    or cfg.h_branch_l_mixing)
 
     # ---------------------------------------------------------------- caches
     def create_cache(self, **kwargs):
@@ -244,155 +354,131 @@ class Mimir2(RecurrentBackbone):
 
     # ---------------------------------------------------------------- helpers
     def _metadata_bias(self, category, kind):
-        values = getattr(self.gate_config, f"{kind}_metadata_bias")
-        if not self.training or self.gate_config.specialist_router_calibration or category is None or not values:
+        """Per-token routing logit bias from the batch's routing category (training only)."""
+        rows = getattr(self.gate_config, f"{kind}_metadata_bias")
+        if category is None or not rows or not self.training or self.gate_config.specialist_router_calibration:
             return None
-        table = torch.tensor(values, device=category.device, dtype=torch.float32)
-        return table[category.long()] * self.routing_bias_scale
+        return torch.tensor(rows, device=category.device, dtype=torch.float32)[category.long()] * self.routing_bias_scale
 
     def _inject(self, level, invocation, hidden, other):
-        if not self.gate_config.gates_enabled:
-            return other
-        return level.invocation_gates[invocation](hidden, other, self.gate_alpha)
+        """The injection a stack receives: gated by that invocation's gate when gates are on."""
+        if self.gate_config.gates_enabled:
+            return level.invocation_gates[invocation](hidden, other, self.gate_alpha)
+        return other
 
     def _stack_step(self, z_L, z_H, states, invocation, cache, diagnostics, seq_info, bias=None, expert_outputs=None):
         """Dense MoS: every L stack expert runs on all tokens; outputs are mixed token-locally."""
         weights = self.L_level.stack_router(z_L + z_H, bias)
-        output = torch.zeros_like(z_H)
-        next_states = []
-        for e, core in enumerate([self.L_level.core, *self.L_level.stack_experts]):
-            prev = states[e] if states is not None else z_L
-            inj = self._inject(self.L_level, invocation, prev, z_H)
-            y = core(prev + inj, **seq_info, cache=cache[e] if cache is not None else None,
-                     stability_diagnostics=diagnostics,
-                     stability_scope=f"L/cycle_{invocation:03d}/expert_{e}" if diagnostics is not None else None)
+        mixed = torch.zeros_like(z_H)
+        updated = [] if states is not None else None
+        for e, core in enumerate((self.L_level.core, *self.L_level.stack_experts)):
+            start = z_L if states is None else states[e]
+            scope = None if diagnostics is None else f"L/cycle_{invocation:03d}/expert_{e}"
+            y = core(start + self._inject(self.L_level, invocation, start, z_H), **seq_info,
+                     cache=None if cache is None else cache[e], stability_diagnostics=diagnostics,
+                     stability_scope=scope)
             w = weights[..., e:e + 1]
-            output = output + w.to(y.dtype) * y
+            mixed = mixed + w.to(y.dtype) * y
             if expert_outputs is not None:
                 expert_outputs.append((y, w))
-            if states is not None:
-                next_states.append(torch.where(w > 0, y, prev))
-        return output, (next_states if states is not None else None)
+            if updated is not None:
+                updated.append(torch.where(w > 0, y, start))
+        return mixed, updated
 
     def _is_v1(self):
+        """No v2 feature is on: the plain HRM v1 backbone forward applies."""
         c = self.gate_config
-        return (c.recurrence_mode == "hierarchical" and not c.gates_enabled and c.moe_num_experts == 1
-                and c.mos_num_experts == 1 and c.residual_branches == 1
-                and c.h_memory_branches == c.l_memory_branches == 1)
+        return (c.recurrence_mode == "hierarchical" and not c.gates_enabled and c.residual_branches == 1
+                and c.moe_num_experts == c.mos_num_experts == c.h_memory_branches == c.l_memory_branches == 1)
 
     # ---------------------------------------------------------------- forward
     def forward(self, carry, x, cache=None, bp_steps=2, stability_diagnostics=None, **seq_info):
-        cfg = self.gate_config
         category = seq_info.pop("routing_category", None)
         if self.ngram_enabled:
             x = self.ngram(x, seq_info.pop("token_ids"), seq_info.get("position_ids"),
-                           cache["ngram_history"] if cache is not None else None)
+                           None if cache is None else cache["ngram_history"])
         if self._is_v1():
             return super().forward(carry, x, cache=cache, bp_steps=bp_steps,
                                    stability_diagnostics=stability_diagnostics, **seq_info)
-        looped = cfg.recurrence_mode == "looped"
-        z_H, z_L = x, self.zL_init
-        h_streams = self.H_level.core.initialize_streams(x) if cfg.h_residual_persistence else None
-        memories = {}
-        for name, value in (("H", z_H), ("L", z_L)):
-            memory = getattr(getattr(self, f"{name}_level"), "memory", None)
-            if memory is not None:
-                memories[name] = memory.initialize(value.expand_as(x))
-        moe_bias, mos_bias = self._metadata_bias(category, "moe"), self._metadata_bias(category, "mos")
-        level_info = {name: dict(seq_info) for name in ("L", "H")}
-        for name in ("L", "H"):
-            if moe_bias is not None and cfg.moe_levels in (name, "both"):
-                level_info[name]["routing_bias"] = moe_bias
-        mixture = cfg.mos_num_experts > 1
-        routes = None
-        if mixture and cfg.mos_sparse:
-            from mimir_b200.models.sparse_stacks import cached_sequence_routes, sequence_routes
-            routes = (cached_sequence_routes(self, x, cache, seq_info, mos_bias) if cache is not None else
-                      sequence_routes(self.L_level.stack_router, x, seq_info, mos_bias, cfg.mos_sparse_routing))
-        states = [self.zL_init] * cfg.mos_num_experts if mixture and cfg.mos_state_mode == "separate" else None
-        h_bp, l_bp = backward_call_counts(self.H_cycles, self.L_cycles, bp_steps, has_h_stack=self.has_h_stack)
-        grad = torch.is_grad_enabled()
-        total_l = self.H_cycles * self.L_cycles
-        for i in range(self.H_cycles):
-            if looped:
-                z_L = z_H
-            l_context = None if looped else z_H  # looped: L sees no H injection (a zero tensor in the reference)
-            expert_outputs = None
-            for k in range(i * self.L_cycles, (i + 1) * self.L_cycles):
-                expert_outputs = [] if cfg.h_branch_l_mixing and k == (i + 1) * self.L_cycles - 1 else None
-                with torch.set_grad_enabled(grad and k >= total_l - l_bp):
-                    if "L" in memories:
-                        z_L = self.L_level.memory.read_state(memories["L"])
-                    ctx = torch.zeros_like(z_H) if l_context is None and (mixture or cfg.gates_enabled) else l_context
-                    if mixture:
-                        z_L, states = self._mos_step(z_L, ctx, states, k, cache, stability_diagnostics,
-                                                     level_info["L"], routes, mos_bias, expert_outputs)
-                    else:
-                        z_L = self._l_invocation(z_L, ctx, k, cache, stability_diagnostics, level_info["L"])
-                    if "L" in memories:
-                        memories["L"] = self.L_level.memory.update(memories["L"], z_L)
-                        z_L = self.L_level.memory.read_state(memories["L"])
-            if not self.has_h_stack:
-                z_H = z_L
-                continue
-            with torch.set_grad_enabled(grad and i >= self.H_cycles - h_bp):
-                if "H" in memories:
-                    z_H = self.H_level.memory.read_state(memories["H"])
-                if looped:
-                    z_H = z_L
-                if cfg.h_residual_persistence or cfg.h_branch_l_mixing:
-                    if not cfg.h_residual_persistence:
-                        h_streams = self.H_level.core.initialize_streams(z_H)
-                    l_inj = (self.H_level.l_branch_mixer(expert_outputs) if cfg.h_branch_l_mixing
-                             else z_L.unsqueeze(-2))
-                    inj = self._inject(self.H_level, i, h_streams, l_inj)
-                    h_streams, z_H = self.H_level(h_streams, inj, **level_info["H"], stream_input=True,
-                                                  return_streams=True,
-                                                  cache=cache["H"][i] if cache is not None else None,
-                                                  stability_diagnostics=stability_diagnostics,
-                                                  stability_scope=f"H/cycle_{i:03d}" if stability_diagnostics is not None else None)
-                    continue
-                h_cache = cache["H"][i] if cache is not None else None
-                if looped and stability_diagnostics is None:
-                    # The reference adds a zero injection here; x + 0 == x, so skip the add.
-                    z_H = self.H_level.core(z_H, **level_info["H"], cache=h_cache)
-                elif looped:
-                    z_H = self.H_level(z_H, torch.zeros_like(z_L), **level_info["H"], cache=h_cache,
-                                       stability_diagnostics=stability_diagnostics, stability_scope=f"H/cycle_{i:03d}")
-                else:
-                    inj = self._inject(self.H_level, i, z_H, z_L)
-                    z_H = self.H_level(z_H, inj, **level_info["H"], cache=cache["H"][i] if cache is not None else None,
-                                       stability_diagnostics=stability_diagnostics,
-                                       stability_scope=f"H/cycle_{i:03d}" if stability_diagnostics is not None else None)
-                if "H" in memories:
-                    memories["H"] = self.H_level.memory.update(memories["H"], z_H)
-                    z_H = self.H_level.memory.read_state(memories["H"])
-        return None, z_H
+        run = _Pass(self, x, cache, stability_diagnostics, seq_info, category)
+        h_window, l_window = backward_call_counts(self.H_cycles, self.L_cycles, bp_steps,
+                                                  has_h_stack=self.has_h_stack)
+        record = torch.is_grad_enabled()
+        last_l = self.L_cycles - 1
+        for call in _schedule(self.H_cycles, self.L_cycles, h_window, l_window):
+            if call.level == "L":
+                if call.slot % self.L_cycles == 0:
+                    run.begin_cycle()
+                run.collect = [] if self.gate_config.h_branch_l_mixing and call.slot % self.L_cycles == last_l else None
+                with torch.set_grad_enabled(record and call.grad):
+                    self._run_l(run, call.slot)
+            elif not self.has_h_stack:
+                run.z_H = run.z_L
+            else:
+                with torch.set_grad_enabled(record and call.grad):
+                    self._run_h(run, call.slot)
+        return None, run.z_H
+
+    def _run_l(self, run, k):
+        """One L-stack invocation (dense or MoS; optional L memory)."""
+        run.read_memory("L")
+        context = run.context
+        if context is None and (run.mixture or self.gate_config.gates_enabled):
+            context = torch.zeros_like(run.z_H)
+        if run.mixture:
+            run.z_L, run.states = self._mos_step(run.z_L, context, run.states, k, run.cache, run.diagnostics,
+                                                 run.info["L"], run.routes, run.mos_bias, run.collect)
+        else:
+            run.z_L = self._l_invocation(run.z_L, context, k, run.cache, run.diagnostics, run.info["L"])
+        run.write_memory("L")
+
+    def _run_h(self, run, i):
+        """One H-stack invocation: persistent residual streams, looped (no injection), or gated."""
+        cfg = self.gate_config
+        run.read_memory("H")
+        if run.looped:
+            run.z_H = run.z_L
+        h_cache = None if run.cache is None else run.cache["H"][i]
+        scope = None if run.diagnostics is None else f"H/cycle_{i:03d}"
+        if cfg.h_residual_persistence or cfg.h_branch_l_mixing:
+            if not cfg.h_residual_persistence:
+                run.h_streams = self.H_level.core.initialize_streams(run.z_H)
+            l_side = self.H_level.l_branch_mixer(run.collect) if cfg.h_branch_l_mixing else run.z_L.unsqueeze(-2)
+            run.h_streams, run.z_H = self.H_level(run.h_streams, self._inject(self.H_level, i, run.h_streams, l_side),
+                                                  **run.info["H"], stream_input=True, return_streams=True,
+                                                  cache=h_cache, stability_diagnostics=run.diagnostics,
+                                                  stability_scope=scope)
+            return  # the stream options exclude an H memory (validated)
+        if run.looped and run.diagnostics is None:
+            run.z_H = self.H_level.core(run.z_H, **run.info["H"], cache=h_cache)  # z + 0: no injection add
+        else:
+            injection = torch.zeros_like(run.z_L) if run.looped else self._inject(self.H_level, i, run.z_H, run.z_L)
+            run.z_H = self.H_level(run.z_H, injection, **run.info["H"], cache=h_cache,
+                                   stability_diagnostics=run.diagnostics, stability_scope=scope)
+        run.write_memory("H")
 
     def _l_invocation(self, z_L, context, k, cache, diagnostics, info):
-        scope = f"L/cycle_{k:03d}" if diagnostics is not None else None
-        layer_cache = cache["L"][k] if cache is not None else None
+        layer_cache = None if cache is None else cache["L"][k]
         if context is None:
-            # Looped mode without gates: the stack input is z_L itself (z_L + 0 in the reference).
+            # Looped mode without gates or mixture: the L stack input is z_L itself (z_L + 0).
             if diagnostics is None:
                 return self.L_level.core(z_L, **info, cache=layer_cache)
             context = torch.zeros_like(z_L)
-        inj = self._inject(self.L_level, k, z_L, context)
-        return self.L_level(z_L, inj, **info, cache=layer_cache, stability_diagnostics=diagnostics,
-                            stability_scope=scope)
+        return self.L_level(z_L, self._inject(self.L_level, k, z_L, context), **info, cache=layer_cache,
+                            stability_diagnostics=diagnostics,
+                            stability_scope=None if diagnostics is None else f"L/cycle_{k:03d}")
 
     def _mos_step(self, z_L, context, states, k, cache, diagnostics, info, routes, mos_bias, expert_outputs):
-        cfg = self.gate_config
-        layer_cache = cache["L"][k] if cache is not None else None
-        if cfg.mos_sparse:
-            from mimir_b200.models.sparse_stacks import batched_sparse_stack_step, sparse_stack_step
-            if cache is not None or z_L.ndim == 3 or context.ndim == 3:
-                return batched_sparse_stack_step(self, z_L, context, states, k, diagnostics, info, routes, layer_cache,
-                                                 expert_outputs=expert_outputs)
+        layer_cache = None if cache is None else cache["L"][k]
+        if not self.gate_config.mos_sparse:
+            return self._stack_step(z_L, context, states, k, layer_cache, diagnostics, info, mos_bias,
+                                    expert_outputs=expert_outputs)
+        from mimir_b200.models.sparse_stacks import batched_sparse_stack_step, sparse_stack_step
+        if cache is None and z_L.ndim < 3 and context.ndim < 3:
             return sparse_stack_step(self, z_L, context, states, k, diagnostics, info, routes,
                                      expert_outputs=expert_outputs)
-        return self._stack_step(z_L, context, states, k, layer_cache, diagnostics, info, mos_bias,
-                                expert_outputs=expert_outputs)
+        return batched_sparse_stack_step(self, z_L, context, states, k, diagnostics, info, routes, layer_cache,
+                                         expert_outputs=expert_outputs)
 
     # ---------------------------------------------------------------- schedules
     def compute_train_extra_args(self, train_state):
@@ -421,15 +507,18 @@ class Mimir2(RecurrentBackbone):
         return super().compute_train_extra_args(train_state)
 
     def configure_gate_updates(self, optimizer, bp_steps):
-        """Map every gate that gets no gradient this step to the first active gate of its level."""
-        h_bp, l_bp = backward_call_counts(self.H_cycles, self.L_cycles, bp_steps, has_h_stack=self.has_h_stack)
-        pairs = {}
+        """Passive invocation gates (outside this step's backward window) follow the first active
+        gate of their level: ``optimizer.shared_parameter_updates`` maps each passive gate
+        parameter to its donor (empty without gates or when the donor is frozen)."""
+        windows = dict(zip(("H", "L"), backward_call_counts(self.H_cycles, self.L_cycles, bp_steps,
+                                                             has_h_stack=self.has_h_stack)))
+        mapping = {}
         if self.gate_config.gates_enabled:
-            for level, active in ((self.H_level, h_bp), (self.L_level, l_bp)):
-                first = len(level.invocation_gates) - active
-                donor = level.invocation_gates[first]
-                if not any(p.requires_grad for p in donor.parameters()):
-                    continue
-                for gate in level.invocation_gates[:first]:
-                    pairs.update(zip(gate.parameters(), donor.parameters()))
-        optimizer.shared_parameter_updates = pairs
+            for name in ("H", "L"):
+                gates = getattr(self, f"{name}_level").invocation_gates
+                first_active = len(gates) - windows[name]
+                donor = gates[first_active]
+                if any(p.requires_grad for p in donor.parameters()):
+                    for passive in gates[:first_active]:
+                        mapping.update(zip(passive.parameters(), donor.parameters()))
+        optimizer.shared_parameter_updates = mapping

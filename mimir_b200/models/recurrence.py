@@ -1,13 +1,20 @@
-"""Hierarchical recurrent backbone (HRM v1): an H stack and an L stack re-applied in nested cycles.
+"""Hierarchical recurrent backbone (HRM v1): an H stack and an L stack applied in nested cycles.
 
-Reference behaviour: ``src/mimir/model/recurrence.py:14-158``.  Per forward, L runs
-``H_cycles * L_cycles`` times and H runs ``H_cycles`` times; only the last ``bp_steps``
-invocations record autograd state (truncated BPTT).  H receives the first
-``min(H_cycles, bp_steps - 1)`` backward slots, L the remainder.
+Behavioural reference: ``src/mimir/model/recurrence.py:14-158``.  One forward is a fixed
+schedule of stack invocations: for every H cycle, ``L_cycles`` calls of the L stack (input:
+its own state plus the H state) followed by one call of the H stack (its state plus the L
+state).  Truncated BPTT: only the last ``bp_steps`` invocations record autograd state; the H
+stack gets ``min(H_cycles, bp_steps - 1)`` of them (the latest H calls) and the L stack the
+rest, so at least one L call is always differentiated.
+
+Module and buffer names (``H_level``, ``L_level``, ``core``, ``zL_init``) and the construction
+order (H stack, L stack, then ``zL_init``: it fixes the RNG consumption) are the checkpoint
+interface.
 """
 from __future__ import annotations
 
-from typing import Any, Dict, Optional, Tuple
+from dataclasses import dataclass
+from typing import Any, Dict, Tuple
 
 import torch
 from torch import Tensor, nn
@@ -27,8 +34,31 @@ class RecurrentConfig(TransformerConfig):
     H_override: Dict[str, Any] = {}
 
 
+def truncated_bptt_split(h_cycles: int, bp_steps: int) -> tuple[int, int]:
+    """(H, L) invocations inside the backward window of ``bp_steps`` calls."""
+    h = min(h_cycles, bp_steps - 1)
+    return h, bp_steps - h
+
+
+@dataclass(frozen=True)
+class StackCall:
+    level: str  # "H" or "L"
+    slot: int   # the call's index within its level (its decode-cache slot)
+    grad: bool  # inside the truncated-BPTT window
+
+
+def invocation_schedule(h_cycles: int, l_cycles: int, bp_steps: int) -> list[StackCall]:
+    h_window, l_window = truncated_bptt_split(h_cycles, bp_steps)
+    first_l_grad, first_h_grad = h_cycles * l_cycles - l_window, h_cycles - h_window
+    calls = []
+    for i in range(h_cycles):
+        calls.extend(StackCall("L", k, k >= first_l_grad) for k in range(i * l_cycles, (i + 1) * l_cycles))
+        calls.append(StackCall("H", i, i >= first_h_grad))
+    return calls
+
+
 class RecurrentBlock(nn.Module):
-    """A stack whose input is ``hidden + injection``."""
+    """A transformer stack applied to ``state + injection``."""
 
     def __init__(self, config: TransformerConfig) -> None:
         super().__init__()
@@ -37,27 +67,27 @@ class RecurrentBlock(nn.Module):
     def create_cache(self, **kwargs):
         return self.core.create_cache(**kwargs)
 
+    @staticmethod
+    def _record_inputs(diag, scope, state, injection, combined) -> None:
+        if scope is None:
+            raise ValueError("stability_scope is required when diagnostics are enabled")
+        prefix = f"recurrent/{scope}"
+        diag.record_tensor(f"{prefix}/hidden", state, record_gradient=True)
+        diag.record_tensor(f"{prefix}/injection", injection, record_gradient=True)
+        diag.record_tensor(f"{prefix}/combined", combined, record_gradient=True)
+        diag.record_pair(f"{prefix}/hidden_injection", state, injection)
+
     def forward(self, hidden: Tensor, injection: Tensor, stability_diagnostics=None, stability_scope=None,
                 **kwargs) -> Tensor:
         combined = hidden + injection
         if stability_diagnostics is not None:
-            if stability_scope is None:
-                raise ValueError("stability_scope is required when diagnostics are enabled")
-            for name, t in (("hidden", hidden), ("injection", injection), ("combined", combined)):
-                stability_diagnostics.record_tensor(f"recurrent/{stability_scope}/{name}", t, record_gradient=True)
-            stability_diagnostics.record_pair(f"recurrent/{stability_scope}/hidden_injection", hidden, injection)
+            self._record_inputs(stability_diagnostics, stability_scope, hidden, injection, combined)
         out = self.core(combined, stability_diagnostics=stability_diagnostics, stability_scope=stability_scope,
                         **kwargs)
         if stability_diagnostics is not None:
-            value = out[1] if isinstance(out, tuple) else out
-            stability_diagnostics.record_tensor(f"recurrent/{stability_scope}/output", value, record_gradient=True)
+            stability_diagnostics.record_tensor(f"recurrent/{stability_scope}/output",
+                                                out[1] if isinstance(out, tuple) else out, record_gradient=True)
         return out
-
-
-def truncated_bptt_split(h_cycles: int, bp_steps: int) -> tuple[int, int]:
-    """(H backward invocations, L backward invocations) for the v1 backbone."""
-    h = min(h_cycles, bp_steps - 1)
-    return h, bp_steps - h
 
 
 class RecurrentBackbone(nn.Module):
@@ -67,47 +97,42 @@ class RecurrentBackbone(nn.Module):
         if config.half_layers:
             assert config.n_layers % 2 == 0, "n_layers must be divisible by 2."
             config.n_layers //= 2
-        # Construction order fixes RNG consumption: H stack, L stack, then zL_init.
         self.H_level = RecurrentBlock(TransformerConfig(**(config.model_dump() | config.H_override)))
         self.L_level = RecurrentBlock(config)
-        self.H_cycles = config.H_cycles
-        self.L_cycles = config.L_cycles
+        self.H_cycles, self.L_cycles = config.H_cycles, config.L_cycles
         self.bp_warmup_ratio = config.bp_warmup_ratio
-        self.bp_min_steps = config.bp_min_steps
-        self.bp_max_steps = config.bp_max_steps
+        self.bp_min_steps, self.bp_max_steps = config.bp_min_steps, config.bp_max_steps
         self.hidden_size = config.hidden_size
         self.head_hint = self.H_level.core.head_hint
-        self.zL_init = nn.Buffer(trunc_normal_init_(torch.empty(config.hidden_size,
-                                                                dtype=getattr(torch, config.fwd_bwd_dtype)), std=1.0),
-                                 persistent=True)
+        init = torch.empty(config.hidden_size, dtype=getattr(torch, config.fwd_bwd_dtype))
+        self.zL_init = nn.Buffer(trunc_normal_init_(init, std=1.0), persistent=True)
 
     def create_cache(self, **kwargs):
-        return dict(H=[self.H_level.create_cache(**kwargs) for _ in range(self.H_cycles)],
-                    L=[self.L_level.create_cache(**kwargs) for _ in range(self.H_cycles * self.L_cycles)])
+        return {"H": [self.H_level.create_cache(**kwargs) for _ in range(self.H_cycles)],
+                "L": [self.L_level.create_cache(**kwargs) for _ in range(self.H_cycles * self.L_cycles)]}
 
     def forward(self, carry: None, x: Tensor, cache=None, bp_steps: int = 2, stability_diagnostics=None,
                 **seq_info) -> Tuple[None, Tensor]:
-        z_H, z_L = x, self.zL_init
-        h_bp, l_bp = truncated_bptt_split(self.H_cycles, bp_steps)
-        total_l = self.H_cycles * self.L_cycles
-        grad = torch.is_grad_enabled()
-        for i in range(self.H_cycles):
-            for k in range(i * self.L_cycles, (i + 1) * self.L_cycles):
-                with torch.set_grad_enabled(grad and k >= total_l - l_bp):
-                    z_L = self.L_level(z_L, z_H, **seq_info, cache=cache["L"][k] if cache is not None else None,
-                                       stability_diagnostics=stability_diagnostics,
-                                       stability_scope=f"L/cycle_{k:03d}" if stability_diagnostics is not None else None)
-            with torch.set_grad_enabled(grad and i >= self.H_cycles - h_bp):
-                z_H = self.H_level(z_H, z_L, **seq_info, cache=cache["H"][i] if cache is not None else None,
-                                   stability_diagnostics=stability_diagnostics,
-                                   stability_scope=f"H/cycle_{i:03d}" if stability_diagnostics is not None else None)
-        return None, z_H
+        state = {"H": x, "L": self.zL_init}
+        partner = {"H": "L", "L": "H"}
+        stacks = {"H": self.H_level, "L": self.L_level}
+        record = torch.is_grad_enabled()
+        for call in invocation_schedule(self.H_cycles, self.L_cycles, bp_steps):
+            scope = f"{call.level}/cycle_{call.slot:03d}" if stability_diagnostics is not None else None
+            with torch.set_grad_enabled(record and call.grad):
+                state[call.level] = stacks[call.level](
+                    state[call.level], state[partner[call.level]], **seq_info,
+                    cache=None if cache is None else cache[call.level][call.slot],
+                    stability_diagnostics=stability_diagnostics, stability_scope=scope)
+        return None, state["H"]
 
     def compute_train_extra_args(self, train_state: Any) -> dict[str, Any]:
+        """``bp_steps`` grows linearly from ``bp_min_steps`` to ``bp_max_steps`` over the first
+        ``bp_warmup_ratio`` of training (integer steps, rounded down)."""
         if self.bp_warmup_ratio == 0:
-            return dict(bp_steps=self.bp_max_steps)
+            return {"bp_steps": self.bp_max_steps}
         progress = min(1, train_state.step / (train_state.total_steps * self.bp_warmup_ratio))
-        return dict(bp_steps=self.bp_min_steps + int(progress * (self.bp_max_steps - self.bp_min_steps)))
+        return {"bp_steps": self.bp_min_steps + int(progress * (self.bp_max_steps - self.bp_min_steps))}
 
     def initial_carry(self, batch_size: int, dtype: torch.dtype) -> None:
         return None

@@ -81,24 +81,19 @@ class AdamATan2(Optimizer):
     @torch.no_grad()
     def step(self, closure=None):
         assert closure is None, "Closure is not supported"
-        shared = getattr(self, "shared_parameter_updates", None)
-        if shared:
-            from mimir_b200.optim.gate_updates import snapshot_donors
-            snapshots = snapshot_donors(self)
-        for group in self.param_groups:
-            fused_items = []
-            for p in group["params"]:
-                if (shared and p in shared) or p.grad is None:
-                    continue
-                if self._use_fused(p):
-                    fused_items.append(p)
-                else:
-                    self._step_reference(group, p)
-            if fused_items:
-                self._step_fused(group, fused_items)
-        if shared:
-            from mimir_b200.optim.gate_updates import apply_shared_updates
-            apply_shared_updates(self, snapshots)
+        from mimir_b200.optim.gate_updates import donor_updates
+        with donor_updates(self) as passive:
+            for group in self.param_groups:
+                fused_items = []
+                for p in group["params"]:
+                    if p in passive or p.grad is None:
+                        continue
+                    if self._use_fused(p):
+                        fused_items.append(p)
+                    else:
+                        self._step_reference(group, p)
+                if fused_items:
+                    self._step_fused(group, fused_items)
 
     def _use_fused(self, p) -> bool:
         if self.fused is False:

@@ -1,42 +1,85 @@
-"""Shared updates for invocation gates that receive no gradient in a step.
+"""Donor updates for invocation gates that receive no gradient in a step.
 
-Reference: ``src/mimir/model/gate_updates.py:6-40``.  Gates outside the truncated-BPTT
-window copy the actual parameter delta of their level's first active gate ("donor") and
-track its optimizer moments, so they stay usable when the window later widens.
+Behavioural reference: ``src/mimir/model/gate_updates.py:6-40``.  A gate whose level is outside
+the truncated-BPTT window this step gets no gradient.  Instead of standing still it moves by the
+same amount as its level's first active gate (the "donor"), and it adopts the donor's optimizer
+moments, so the update history it carries into a later, wider window is the one that moved it.
+Only its parameter EMA stays its own (advanced towards the moved value).
+
+Usage inside an optimizer's ``step``::
+
+    with donor_updates(self) as passive:
+        for p in params:
+            if p in passive or p.grad is None:
+                continue
+            ...  # the regular update
+
+The donors' values are recorded on entry; on a clean exit every passive gate receives its
+donor's parameter change.
 """
 from __future__ import annotations
+
+from contextlib import contextmanager
+from typing import Iterator
 
 import torch
 
 
-@torch.no_grad()
-def snapshot_donors(optimizer):
-    pairs = getattr(optimizer, "shared_parameter_updates", {})
-    for target, donor in pairs.items():
-        if target is donor or donor in pairs:
+def _mapping(optimizer) -> dict:
+    return getattr(optimizer, "shared_parameter_updates", None) or {}
+
+
+def _check(optimizer, mapping: dict) -> None:
+    donors = set(mapping.values())
+    for target, donor in mapping.items():
+        if donor is target or donor in mapping:
             raise ValueError("Gate donors must be active, independent parameters")
+        # The invocation schedule decides which gates are passive; an FSDP zero gradient on a
+        # passive gate is harmless, but a donor without a gradient means the schedule is wrong.
         if donor.grad is None:
             raise RuntimeError("Gate donor mapping disagrees with gradient eligibility")
-        if target.shape != donor.shape:
+        if donor.shape != target.shape:
             raise ValueError("Gate donor and target shapes must match")
-        if target not in optimizer.state or donor not in optimizer.state:
+        if any(p not in optimizer.state for p in (target, donor)):
             raise ValueError("Gate parameters must belong to this optimizer")
-    return {donor: donor.detach().clone() for donor in set(pairs.values())}
+    del donors
+
+
+def _group_ema(optimizer) -> dict:
+    """EMA decay of each parameter's group, keyed by the parameter."""
+    return {p: group.get("ema") for group in optimizer.param_groups for p in group["params"]}
 
 
 @torch.no_grad()
-def apply_shared_updates(optimizer, before):
-    pairs = getattr(optimizer, "shared_parameter_updates", {})
-    deltas = {donor: donor - old for donor, old in before.items()}
-    for group in optimizer.param_groups:
-        for target in group["params"]:
-            if target not in pairs:
+def _follow_donors(optimizer, mapping: dict, before: dict) -> None:
+    moved = {donor: donor - value for donor, value in before.items()}
+    ema_decay = _group_ema(optimizer)
+    for target, donor in mapping.items():
+        if target not in ema_decay:
+            continue
+        target.add_(moved[donor])
+        mine, theirs = optimizer.state[target], optimizer.state[donor]
+        for slot, value in theirs.items():
+            if slot == "param_ema":
                 continue
-            donor = pairs[target]
-            target.add_(deltas[donor])
-            state = optimizer.state[target]
-            for key, value in optimizer.state[donor].items():
-                if key != "param_ema":
-                    state[key].copy_(value)
-            if "param_ema" in state:
-                state["param_ema"].lerp_(target.to(state["param_ema"].dtype), 1 - group["ema"])
+            if torch.is_tensor(value):
+                mine[slot].copy_(value)
+            else:
+                mine[slot] = value
+        ema = mine.get("param_ema")
+        if ema is not None:
+            ema.lerp_(target.to(ema.dtype), 1 - ema_decay[target])
+
+
+@contextmanager
+def donor_updates(optimizer) -> Iterator[frozenset]:
+    """Yield the passive gates (to be skipped by the regular update); move them on exit."""
+    mapping = _mapping(optimizer)
+    if not mapping:
+        yield frozenset()
+        return
+    _check(optimizer, mapping)
+    with torch.no_grad():
+        before = {donor: donor.detach().clone() for donor in set(mapping.values())}
+    yield frozenset(mapping)
+    _follow_donors(optimizer, mapping, before)

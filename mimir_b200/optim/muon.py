@@ -84,13 +84,15 @@ class MuonAdamW(AdamATan2):
     def step(self, closure=None):
         if closure is not None:
             raise ValueError("Closures are not supported")
-        from mimir_b200.optim.gate_updates import apply_shared_updates, snapshot_donors
-        shared = getattr(self, "shared_parameter_updates", None)
-        snaps = snapshot_donors(self) if shared else None
+        from mimir_b200.optim.gate_updates import donor_updates
+        with donor_updates(self) as passive:
+            self._step_groups(passive)
+
+    def _step_groups(self, passive):
         pending = []  # (group, param, lr, momentum update) for distributed owner mode
         for group in self.param_groups:
             for p in group["params"]:
-                if not p.requires_grad or (shared and p in shared) or p.grad is None:
+                if not p.requires_grad or p in passive or p.grad is None:
                     continue
                 count = self.matrix_layout[p]
                 st = self.state[p]
@@ -118,8 +120,6 @@ class MuonAdamW(AdamATan2):
                 self._apply(group, p, lr, upd)
         if pending:
             self._owner_updates(pending)
-        if shared:
-            apply_shared_updates(self, snaps)
 
     def _apply(self, group, p, lr, upd):
         p.mul_(1 - lr * group["weight_decay"]).add_(upd, alpha=-lr)

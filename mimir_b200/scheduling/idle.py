@@ -1,13 +1,14 @@
-"""Serial scheduler that runs queued work only while the selected GPUs are idle.
+"""Serial scheduler that runs queued work only while the chosen GPUs are idle.
 
-Reference behaviour: ``src/mimir/scheduling/idle.py:22-140``.  It never signals other users'
-processes: a GPU counts as free when no foreign compute process uses it (or, with no
-processes, when memory <= 1 GiB and utilisation <= 5 %) for ``quiet_polls`` consecutive
-polls.  Non-evaluation jobs run one at a time; pending evaluations then run as one worker
-process per GPU (each pinned with ``CUDA_VISIBLE_DEVICES`` and draining only jobs whose
-server names that GPU), all joined before the next training job.  After each unit of work a
-verified backup of the queue replaces ``queue.backup.sqlite``.  Status for the monitor goes
-to ``idle-status.json``.  GPU state is only read (``nvidia-smi --query``).
+Behavioural reference: ``src/mimir/scheduling/idle.py:22-140``.  It never signals other users'
+processes and only reads GPU state (``nvidia-smi --query-*``).  A GPU is free when no foreign
+compute process uses it, or, when no compute process is listed at all, when it holds at most
+1 GiB and is at most 5 % busy; work starts after ``quiet_polls`` consecutive free polls.
+Training-type jobs run one at a time; pending evaluations then run as one worker process per
+GPU (each pinned with ``CUDA_VISIBLE_DEVICES`` and draining only the jobs whose server names
+that GPU), and all workers are joined before the next training job.  After every unit of work
+a verified copy of the queue replaces ``queue.backup.sqlite``; the monitor reads
+``idle-status.json``.
 """
 from __future__ import annotations
 
@@ -20,7 +21,9 @@ import sys
 import time
 import uuid
 import warnings
+from dataclasses import dataclass
 from pathlib import Path
+from typing import Callable
 
 import psutil
 
@@ -30,99 +33,151 @@ from mimir_b200.scheduling.worker import recover_abandoned, run_one
 from mimir_b200.serving.server import ServerPool
 from mimir_b200.train.suspension.protocol import exclusive
 
+IDLE_MEMORY_MIB = 1024.0
+IDLE_UTILIZATION_PCT = 5.0
+
 
 def query(fields: str, section: str) -> list[list[str]]:
-    out = subprocess.check_output(["nvidia-smi", f"--query-{section}={fields}", "--format=csv,noheader,nounits"],
-                                  text=True, timeout=10)
-    return list(csv.reader(io.StringIO(out), skipinitialspace=True))
+    """Rows of ``nvidia-smi --query-<section>=<fields>`` (CSV, no header, no units)."""
+    text = subprocess.check_output(["nvidia-smi", f"--query-{section}={fields}", "--format=csv,noheader,nounits"],
+                                   text=True, timeout=10)
+    return list(csv.reader(io.StringIO(text), skipinitialspace=True))
+
+
+@dataclass
+class _Gpu:
+    index: str
+    uuid: str
+    memory_mib: float
+    utilization: float
+    pids: list
+
+    def verdict(self, owned) -> str | None:
+        """None when free for us, else why not."""
+        strangers = [pid for pid in self.pids if pid not in owned]
+        if strangers:
+            return f"GPU {self.index}: external PIDs {strangers}"
+        if not self.pids and (self.memory_mib > IDLE_MEMORY_MIB or self.utilization > IDLE_UTILIZATION_PCT):
+            return f"GPU {self.index}: memory/utilization not idle"
+        return None
+
+
+def _read_gpus() -> dict[str, _Gpu]:
+    gpus = {row[0]: _Gpu(row[0], row[1], float(row[2]), float(row[3]), [])
+            for row in query("index,uuid,memory.used,utilization.gpu", "gpu")}
+    by_uuid = {g.uuid: g for g in gpus.values()}
+    for gpu_uuid, pid in query("gpu_uuid,pid", "compute-apps"):
+        if gpu_uuid in by_uuid:
+            by_uuid[gpu_uuid].pids.append(int(pid))
+    return gpus
 
 
 def available(gpus, owned=()) -> tuple[bool, str]:
-    devices = {row[0]: row for row in query("index,uuid,memory.used,utilization.gpu", "gpu")}
-    if any(g not in devices for g in gpus):
+    """(free, reason) for the GPU indices ``gpus``; processes in ``owned`` are our own."""
+    state = _read_gpus()
+    if not all(g in state for g in gpus):
         return False, "Requested GPU missing"
-    apps = query("gpu_uuid,pid", "compute-apps")
-    reasons = []
-    for gpu in gpus:
-        _, uid, memory, util = devices[gpu]
-        pids = [int(pid) for dev, pid in apps if dev == uid]
-        foreign = [p for p in pids if p not in owned]
-        if foreign:
-            reasons.append(f"GPU {gpu}: external PIDs {foreign}")
-        elif not pids and (float(memory) > 1024 or float(util) > 5):
-            reasons.append(f"GPU {gpu}: memory/utilization not idle")
-    return not reasons, "; ".join(reasons) or "No external GPU users detected"
+    problems = [v for v in (state[g].verdict(set(owned)) for g in gpus) if v is not None]
+    return (False, "; ".join(problems)) if problems else (True, "No external GPU users detected")
 
 
 def refresh_backup(store: Store) -> bool:
-    target = store.path.parent / "queue.backup.sqlite"
-    staged = target.with_name(f".{target.name}.{uuid.uuid4().hex}.partial")
+    """Replace ``queue.backup.sqlite`` with a fresh verified copy; a failure keeps the old copy
+    (and is only warned about: a backup problem must not stop the queue)."""
+    final = store.path.parent / "queue.backup.sqlite"
+    partial = final.with_name(f".{final.name}.{uuid.uuid4().hex}.partial")
+    ok = False
     try:
-        store.backup(staged)
-        staged.replace(target)
-        return True
-    except Exception as exc:  # noqa: BLE001 - a failed backup must not stop the queue
+        store.backup(partial)
+        partial.replace(final)
+        ok = True
+    except Exception as exc:  # noqa: BLE001
         warnings.warn(f"Queue backup failed; previous snapshot retained: {exc}", RuntimeWarning)
-        return False
     finally:
-        staged.unlink(missing_ok=True)
+        partial.unlink(missing_ok=True)
+    return ok
+
+
+def _own_pids() -> set:
+    return {child.pid for child in psutil.Process().children(recursive=True)}
+
+
+class IdleCoordinator:
+    def __init__(self, database, gpus, poll: float, quiet_polls: int, probe: Callable):
+        self.database = Path(database)
+        self.root = self.database.parent
+        self.store = Store(self.database)
+        self.gpus, self.poll, self.quiet_polls, self.probe = gpus, poll, quiet_polls, probe
+        self.status_file = self.root / "idle-status.json"
+        self.quiet = 0
+
+    def _status(self, **fields) -> None:
+        write_record(self.status_file, {"pid": os.getpid(), "time": time.time()} | fields)
+
+    def _queue_empty(self) -> bool:
+        return all(row["state"] not in ("pending", "running") for row in self.store.rows())
+
+    def _observe(self) -> None:
+        try:
+            free, reason = self.probe(self.gpus, _own_pids())
+        except Exception as exc:  # noqa: BLE001 - an unreadable GPU counts as busy
+            free, reason = False, f"GPU probe failed: {exc}"
+        self.quiet = self.quiet + 1 if free else 0
+        self._status(state="ready" if self.quiet >= self.quiet_polls else "waiting_for_gpus", gpus=self.gpus,
+                     reason=reason, quiet_polls=self.quiet)
+
+    def _evaluate_on_every_gpu(self) -> None:
+        workers = [subprocess.Popen([sys.executable, "-m", "mimir_b200.scheduling.idle", str(self.database), "--gpus",
+                                     gpu, "--eval-worker"], env=os.environ | {"CUDA_VISIBLE_DEVICES": gpu})
+                   for gpu in self.gpus]
+        codes = [w.wait() for w in workers]
+        if any(codes):
+            raise RuntimeError("Evaluation worker exited unexpectedly; inspect runner log")
+
+    def serve(self, pool: ServerPool) -> None:
+        recover_abandoned(self.store, self.root / "attempts")
+        while not self._queue_empty():
+            self._observe()
+            if self.quiet >= self.quiet_polls:
+                ran_training = run_one(self.store, self.root / "attempts", pool, predicate=lambda j: j["kind"] != "eval")
+                if not ran_training:
+                    self._evaluate_on_every_gpu()
+                refresh_backup(self.store)
+                self.quiet = 0
+                if ran_training:
+                    continue
+            time.sleep(self.poll)
+        self._status(state="complete")
 
 
 def run(database, gpus, poll: float = 30, quiet_polls: int = 3, probe=available) -> None:
-    database = Path(database)
-    store = Store(database)
-    status = database.parent / "idle-status.json"
-    with exclusive(database.with_suffix(".runner.lock")):
-        pool = ServerPool(database.parent / "servers")
-        stable = 0
+    coordinator = IdleCoordinator(database, gpus, poll, quiet_polls, probe)
+    with exclusive(coordinator.database.with_suffix(".runner.lock")):
+        pool = ServerPool(coordinator.root / "servers")
         try:
-            recover_abandoned(store, database.parent / "attempts")
-            while True:
-                if not any(r["state"] in ("pending", "running") for r in store.rows()):
-                    write_record(status, {"state": "complete", "pid": os.getpid(), "time": time.time()})
-                    return
-                owned = {p.pid for p in psutil.Process().children(recursive=True)}
-                try:
-                    free, reason = probe(gpus, owned)
-                except Exception as exc:  # noqa: BLE001 - treated as busy
-                    free, reason = False, f"GPU probe failed: {exc}"
-                stable = stable + 1 if free else 0
-                write_record(status, {"state": "waiting_for_gpus" if stable < quiet_polls else "ready",
-                                      "pid": os.getpid(), "gpus": gpus, "reason": reason, "quiet_polls": stable,
-                                      "time": time.time()})
-                if stable >= quiet_polls:
-                    if run_one(store, database.parent / "attempts", pool, predicate=lambda j: j["kind"] != "eval"):
-                        refresh_backup(store)
-                        stable = 0
-                        continue
-                    workers = [subprocess.Popen([sys.executable, "-m", "mimir_b200.scheduling.idle", str(database),
-                                                 "--gpus", g, "--eval-worker"],
-                                                env=os.environ | {"CUDA_VISIBLE_DEVICES": g}) for g in gpus]
-                    if any(w.wait() for w in workers):
-                        raise RuntimeError("Evaluation worker exited unexpectedly; inspect runner log")
-                    refresh_backup(store)
-                    stable = 0
-                time.sleep(poll)
+            coordinator.serve(pool)
         finally:
             pool.close()
 
 
 def evaluate_assigned(database, gpu: str, probe=available) -> None:
+    """Evaluation worker for one GPU: drain the eval jobs whose server is pinned to ``gpu``."""
     database = Path(database)
     store = Store(database)
     pool = ServerPool(database.parent / "servers" / f"gpu-{gpu}")
+
+    def mine(job) -> bool:
+        return job["kind"] == "eval" and job["config"].get("server", {}).get("gpus") == gpu
+
     try:
         while True:
-            owned = {p.pid for p in psutil.Process().children(recursive=True)}
             try:
-                free, _ = probe([gpu], owned)
+                free = probe([gpu], _own_pids())[0]
             except Exception:  # noqa: BLE001
                 free = False
             if not free:
                 time.sleep(30)
-                continue
-            if not run_one(store, database.parent / "attempts", pool,
-                           predicate=lambda j: j["kind"] == "eval" and j["config"].get("server", {}).get("gpus") == gpu):
+            elif not run_one(store, database.parent / "attempts", pool, predicate=mine):
                 return
     finally:
         pool.close()
@@ -136,16 +191,16 @@ def main(argv=None) -> None:
     parser.add_argument("--eval-worker", action="store_true", help=argparse.SUPPRESS)
     args = parser.parse_args(argv)
     gpus = args.gpus.split(",")
-    if not gpus or any(not g.isdigit() for g in gpus) or len(set(gpus)) != len(gpus):
+    if not gpus or not all(g.isdigit() for g in gpus) or len(set(gpus)) != len(gpus):
         parser.error("Provide distinct numeric GPU indices")
     if args.poll <= 0:
         parser.error("poll must be positive")
-    if args.eval_worker:
-        if len(gpus) != 1:
-            parser.error("Evaluation worker requires exactly one GPU")
+    if not args.eval_worker:
+        run(args.database, gpus, args.poll)
+    elif len(gpus) == 1:
         evaluate_assigned(args.database, gpus[0])
     else:
-        run(args.database, gpus, args.poll)
+        parser.error("Evaluation worker requires exactly one GPU")
 
 
 if __name__ == "__main__":

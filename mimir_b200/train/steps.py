@@ -24,7 +24,7 @@ from torch.nn.parallel import DistributedDataParallel
 
 from mimir_b200.models.common import IGNORE_LABEL_ID, wrap_tensor
 from mimir_b200.optim.clipping import clip_grad_norm_mean_units
-from mimir_b200.optim.routing_balance import balanced_optimizer_step
+from mimir_b200.optim.routing_balance import has_balanced_routers, routing_balance
 from mimir_b200.utils.trace import trace_print
 
 
@@ -69,9 +69,24 @@ def supervised_token_count(config, rank: int, batch: dict) -> Tensor:
     return count
 
 
-@balanced_optimizer_step
 def train_accumulated_batches(config, rank: int, train_state, batches: list, use_compiled: bool = False,
                               zero_grad_after_step: bool = True, optimizer_step_enabled: bool = True, **kwargs):
+    """One optimizer step over ``batches`` (gradient accumulation); returns ``(metrics, skipped)``.
+    Models with balanced MoE routers record their selections for the whole step and move the
+    selection biases only when the optimizer update ran."""
+    if not has_balanced_routers(train_state.model):
+        return _accumulate_and_step(config, rank, train_state, batches, use_compiled, zero_grad_after_step,
+                                    optimizer_step_enabled, **kwargs)
+    with routing_balance(train_state.model) as ledger:
+        metrics, skipped = _accumulate_and_step(config, rank, train_state, batches, use_compiled,
+                                                zero_grad_after_step, optimizer_step_enabled, **kwargs)
+        if optimizer_step_enabled and not skipped:
+            ledger.commit()
+    return metrics, skipped
+
+
+def _accumulate_and_step(config, rank: int, train_state, batches: list, use_compiled: bool,
+                         zero_grad_after_step: bool, optimizer_step_enabled: bool, **kwargs):
     trace_print(config, rank, f"train_accumulated_begin step={train_state.step} microbatches={len(batches)}")
     if config.gradient_skip_norm is not None and train_state.carry is not None:
         raise RuntimeError("gradient_skip_norm currently supports only models with no persistent carry")

@@ -162,11 +162,11 @@ def _balance_worker(rank, world, init, out):
     dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
     try:
         from mimir_b200.models.experts import TopKRouter
-        from mimir_b200.optim.routing_balance import BalanceStep
+        from mimir_b200.optim.routing_balance import routing_balance
         torch.manual_seed(0)
         router = TopKRouter(8, 4, 1, balance_enabled=True, balance_update_rate=0.1)
         router.train()
-        with BalanceStep(router) as step:
+        with routing_balance(router) as step:
             if rank == 0:  # rank 1 routes no tokens at all but still joins the reduction
                 x = torch.randn(16, 8)
                 with torch.no_grad():
