@@ -6,8 +6,9 @@ For every projection (gqkv, o, gate_up, down, lm_head) it times the three GEMMs 
 step: forward ``Y = X W^T`` ("nt"), input gradient ``dX = dY W`` ("nn") and weight gradient
 ``dW = dY^T X`` ("tn"), bf16 in / fp32 accumulate / bf16 out.  Each launch is timed with CUDA
 events after a write of a 512 MB buffer that flushes the 126 MB L2, so every operand comes from
-HBM; the median of ``--iters`` launches is reported with TFLOP/s and the fraction of the
-measured bf16 peak.  ``ours`` runs the hand-written tcgen05 kernel (``mimir_b200.ops.gemm``).
+HBM; the two implementations alternate launch by launch, and the median of ``--iters`` launches
+is reported with TFLOP/s and the fraction of the measured bf16 peak.  ``ours`` runs the
+hand-written tcgen05 kernel (``mimir_b200.ops.gemm``).
 """
 from __future__ import annotations
 
@@ -40,6 +41,23 @@ def _time(fn, flush, iters):
         torch.cuda.synchronize()
         times.append(s.elapsed_time(e))
     return statistics.median(times[3:])
+
+
+def _time_interleaved(fns, flush, iters):
+    """Median time of each function, the functions alternating launch by launch so that clock
+    drift and neighbours on the machine affect them alike."""
+    times = [[] for _ in fns]
+    for it in range(iters + 3):
+        for k, fn in enumerate(fns):
+            flush.add_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            if it >= 3:
+                times[k].append(s.elapsed_time(e))
+    return [statistics.median(t) for t in times]
 
 
 def main():
@@ -82,8 +100,8 @@ def main():
         for kind in ("nt", "nn", "tn"):
             row = {"proj": name, "kind": kind, "M": T if kind != "tn" else n_out,
                    "N": n_out if kind == "nt" else n_in, "K": n_in if kind == "nt" else (n_out if kind == "nn" else T)}
-            for impl in impls:
-                ms = _time(cases[impl][kind], flush, args.iters)
+            timed = _time_interleaved([cases[impl][kind] for impl in impls], flush, args.iters)
+            for impl, ms in zip(impls, timed):
                 row[f"{impl}_ms"] = round(ms, 4)
                 row[f"{impl}_tflops"] = round(flops / ms / 1e9, 1)
                 row[f"{impl}_frac_of_measured"] = round(flops / ms / 1e9 / peak, 3)
@@ -121,7 +139,7 @@ def fused_rows(T, iters, flush, peak):
          lambda: C.gemm(dgu, True, x, True, grad, grad, 1.0, 1.0), lambda: grad.add_(torch.mm(dgu.t(), x))),
     ]
     for name, flops, ours, ref in cases:
-        o, r = _time(ours, flush, iters), _time(ref, flush, iters)
+        o, r = _time_interleaved([ours, ref], flush, iters)
         print(json.dumps({"fused": name, "ours_ms": round(o, 4), "cublas_plus_kernel_ms": round(r, 4),
                           "ours_tflops": round(flops / o / 1e9, 1),
                           "ours_frac_of_measured": round(flops / o / 1e9 / peak, 3)}), flush=True)

@@ -6,6 +6,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "swiglu_math.cuh"
 
 using namespace mimir;
 
@@ -212,7 +213,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_res_kernel(const T* __restric
 }
 
 // ------------------------------------------------------------------ SwiGLU
-__device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
+__device__ __forceinline__ float silu_f(float g) { return swiglu_silu(g); }
 
 template <typename T>
 __global__ void swiglu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t rows, int f) {
@@ -246,9 +247,7 @@ __global__ void swiglu_bwd_kernel(const T* __restrict__ dp, const T* __restrict_
     Vec<T>::load(dp + r * f + c, d);
 #pragma unroll
     for (int j = 0; j < N; ++j) {
-      const float s = 1.f / (1.f + __expf(-g[j]));
-      du[j] = d[j] * g[j] * s;
-      dg[j] = d[j] * u[j] * s * (1.f + g[j] * (1.f - s));
+      swiglu_backward(d[j], g[j], u[j], dg[j], du[j]);
     }
     Vec<T>::store(dgu + r * 2 * f + c, dg);
     Vec<T>::store(dgu + r * 2 * f + f + c, du);

@@ -15,15 +15,16 @@
 // reads both CTAs' shared memory and writes each CTA's 128 accumulator rows into its own TMEM.
 // Per SM that is half the shared-memory operand traffic of a one-CTA 128 x BN tile.
 //
-// Persistent kernel, one CTA per SM, 6 warps per CTA:
+// Persistent kernel, one CTA per SM, 10 warps per CTA:
 //   warp 0      TMA producer (both CTAs): ring of kStages stages; every stage's bytes from both
 //               CTAs complete on the even CTA's `full` barrier.
 //   warp 1      MMA issuer (even CTA only): 4 MMAs per k-block into one of two TMEM
 //               accumulators; commits release the stage in both CTAs (`empty`) and hand the
 //               finished accumulator to both CTAs' epilogues (`acc_full`).
-//   warps 2-5   epilogue (both CTAs): tcgen05.ld of the CTA's 128 rows (one row per thread),
-//               the fused epilogue, 16-byte global stores; the 8 epilogue warps of the pair
-//               release the accumulator on the even CTA's `acc_empty` barrier.
+//   warps 2-9   epilogue (both CTAs): tcgen05.ld of the CTA's 128 rows (one row per thread; two
+//               warps per TMEM lane quarter, each converting half of the columns), the fused
+//               epilogue, 16-byte global stores; the 16 epilogue warps of the pair release the
+//               accumulator on the even CTA's `acc_empty` barrier.
 // Tiles are visited in groups of `group_m` 256-row blocks (all column blocks of a group before
 // the next group) so that the clusters running at the same time share A and B panels in L2.
 //
@@ -44,6 +45,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "swiglu_math.cuh"  // shared bit for bit with the standalone SwiGLU kernels
 #include "tma.cuh"
 
 using namespace mimir;
@@ -52,8 +54,8 @@ namespace {
 
 constexpr int kBM = 128;  // A rows per CTA (256 per pair)
 constexpr int kBK = 64;   // k per stage: one 128-byte swizzle row of bf16
-constexpr int kThreads = 192;
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, each taking half of the tile's columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 enum EpiKind : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiSwiGLUBwd = 2 };
 
@@ -67,6 +69,8 @@ struct GemmParams {
   int64_t ldx;
   int ffn;  // SwiGLU: F
   int M, N, K;
+  int batch;                          // independent problems; z coordinate of the 3-D TMA maps
+  int64_t bs_out, bs_add, bs_aux;     // element strides between the problems' out / add / aux
   int tiles_m, tiles_n, group_m;
   int* status;
   unsigned long long wait_ns;
@@ -94,7 +98,10 @@ struct PairBars {
   uint32_t tmem_base;
 };
 
-__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mt, int& nt) {
+__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& bt, int& mt, int& nt) {
+  const int per_problem = p.tiles_m * p.tiles_n;
+  bt = t / per_problem;
+  t -= bt * per_problem;
   const int per_group = p.group_m * p.tiles_n;
   const int g = t / per_group;
   const int first = g * p.group_m;
@@ -104,7 +111,15 @@ __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mt,
   nt = r / gsize;
 }
 
-__device__ __forceinline__ float silu_ref(float g) { return g / (1.f + __expf(-g)); }
+// Element offsets of one output row of problem `bt` in out / add / aux.
+struct RowOffsets {
+  int64_t out, add, aux;
+};
+__device__ __forceinline__ RowOffsets row_offsets(const GemmParams& p, int bt, int row) {
+  return {bt * p.bs_out + static_cast<int64_t>(row) * p.ldo, bt * p.bs_add + static_cast<int64_t>(row) * p.ldd,
+          bt * p.bs_aux + static_cast<int64_t>(row) * p.ldx};
+}
+
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
@@ -130,6 +145,146 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v
   }
 }
 
+// ------------------------------------------------------------------------------ epilogues
+// One thread holds one accumulator row (its TMEM lane); `half` selects which half of the tile's
+// 32-column chunks this warp converts.  tcgen05.ld is warp-collective, so it stays outside the
+// per-thread `valid` branches.
+
+template <int BN, bool kOutF32>
+__device__ __forceinline__ void epilogue_store(const GemmParams& p, uint32_t tacc, const RowOffsets& ro, bool valid,
+                                               int n0, int half) {
+  constexpr int kChunks = BN / 64;
+#pragma unroll 1
+  for (int j = 0; j < kChunks; ++j) {
+    const int c = half * kChunks + j;
+    float v[32];
+    tmem_ld32(tacc + c * 32, v);
+    const int col = n0 + c * 32;
+    if (!valid || col >= p.N) continue;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] *= p.alpha;
+    if (kOutF32) {
+      if (p.add != nullptr) {
+        const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.add) + ro.add + col);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 a = src[q];
+          v[4 * q] += p.beta * a.x;
+          v[4 * q + 1] += p.beta * a.y;
+          v[4 * q + 2] += p.beta * a.z;
+          v[4 * q + 3] += p.beta * a.w;
+        }
+      }
+      float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + ro.out + col);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+      if (p.add != nullptr) {
+        float a[32];
+        load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(p.add) + ro.add + col, a);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] += p.beta * a[e];
+      }
+      store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.out) + ro.out + col, v);
+    }
+  }
+}
+
+// Accumulator columns [0, BN/2) are gate rows, [BN/2, BN) the matching up rows: writes gate|up
+// (saved for the backward) and h = silu(gate) * up formed from the bf16-rounded values.
+template <int BN>
+__device__ __forceinline__ void epilogue_swiglu_fwd(const GemmParams& p, uint32_t tacc, const RowOffsets& ro,
+                                                    bool valid, int h0, int half) {
+  constexpr int kHalf = BN / 2;
+  constexpr int kChunks = kHalf / 64;
+  __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(p.aux) + ro.aux;
+  __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out) + ro.out;
+#pragma unroll 1
+  for (int j = 0; j < kChunks; ++j) {
+    const int c = half * kChunks + j;
+    float g[32], u[32];
+    tmem_ld32(tacc + c * 32, g);
+    tmem_ld32(tacc + kHalf + c * 32, u);
+    if (!valid) continue;
+    const int col = h0 + c * 32;
+    store_bf16x32(gu + col, g);
+    store_bf16x32(gu + p.ffn + col, u);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) g[e] = swiglu_silu(bf16_round(g[e])) * bf16_round(u[e]);
+    store_bf16x32(h + col, g);
+  }
+}
+
+__device__ __forceinline__ void load_raw4(const __nv_bfloat16* src, uint4 (&r)[4]) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) r[q] = __ldg(s + q);
+}
+
+__device__ __forceinline__ void unpack_bf16x32(const uint4 (&r)[4], float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t words[4] = {r[q].x, r[q].y, r[q].z, r[q].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&words[e]));
+      v[8 * q + 2 * e] = f.x;
+      v[8 * q + 2 * e + 1] = f.y;
+    }
+  }
+}
+
+// Accumulator = d(silu(gate) * up) for columns n0 .. n0 + BN of F; writes d[gate|up] from the
+// saved gate|up.  The gate|up operand of the next chunk is loaded while the current one is
+// converted (the first before the accumulator wait).  Returns false if that wait timed out.
+template <int BN>
+__device__ __forceinline__ bool epilogue_swiglu_bwd(const GemmParams& p, uint64_t* acc_full, uint32_t parity,
+                                                    uint32_t tacc, const RowOffsets& ro, bool valid, int n0,
+                                                    int half) {
+  constexpr int kChunks = BN / 64;
+  const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(p.aux) + ro.aux;
+  __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(p.out) + ro.out;
+  uint4 gn[4], un[4];
+  int c = half * kChunks;
+  if (valid && n0 + c * 32 < p.N) {
+    load_raw4(gu + n0 + c * 32, gn);
+    load_raw4(gu + p.ffn + n0 + c * 32, un);
+  }
+  if (!warp_wait_ns(acc_full, parity, p.status, kStatusTimeoutS, p.wait_ns)) return false;
+  tc_fence_after();
+#pragma unroll 1
+  for (int j = 0; j < kChunks; ++j, ++c) {
+    const int col = n0 + c * 32;
+    const bool live = valid && col < p.N;
+    uint4 gc[4], uc[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      gc[q] = gn[q];
+      uc[q] = un[q];
+    }
+    if (j + 1 < kChunks && valid && col + 32 < p.N) {
+      load_raw4(gu + col + 32, gn);
+      load_raw4(gu + p.ffn + col + 32, un);
+    }
+    float d[32];
+    tmem_ld32(tacc + c * 32, d);
+    if (!live) continue;
+    float g[32], u[32];
+    unpack_bf16x32(gc, g);
+    unpack_bf16x32(uc, u);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      float dg, du;
+      swiglu_backward(bf16_round(d[e]), g[e], u[e], dg, du);
+      g[e] = dg;
+      u[e] = du;
+    }
+    store_bf16x32(dgu + col, g);
+    store_bf16x32(dgu + p.ffn + col, u);
+  }
+  return true;
+}
+
 template <int BN, bool kAMn, bool kBMn, int kEpi, bool kOutF32>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -142,7 +297,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
-  const int total = p.tiles_m * p.tiles_n;
+  const int total = p.batch * p.tiles_m * p.tiles_n;
   const int nkb = (p.K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -176,8 +331,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int it = 0;
       bool ok = true;
       for (int t = cid; ok && t < total; t += ncl) {
-        int mt, nt;
-        tile_coords(t, p, mt, nt);
+        int bt, mt, nt;
+        tile_coords(t, p, bt, mt, nt);
         const int am = mt * 2 * kBM + static_cast<int>(rank) * kBM;
         const int bn = kEpi == kEpiSwiGLU ? nt * CF::kBHalf + (rank ? p.ffn : 0)  // gate rows | up rows
                                           : nt * BN + static_cast<int>(rank) * CF::kBHalf;
@@ -195,16 +350,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const int k0 = kb * kBK;
           if (kAMn) {
 #pragma unroll
-            for (int c = 0; c < kBM / 64; ++c) tma_load_2d_pair(sa + c * (kBK * 128), &map_a, fb, am + c * 64, k0);
+            for (int c = 0; c < kBM / 64; ++c) tma_load_3d_pair(sa + c * (kBK * 128), &map_a, fb, am + c * 64, k0, bt);
           } else {
-            tma_load_2d_pair(sa, &map_a, fb, k0, am);
+            tma_load_3d_pair(sa, &map_a, fb, k0, am, bt);
           }
           if (kBMn) {
 #pragma unroll
             for (int c = 0; c < CF::kBHalf / 64; ++c)
-              tma_load_2d_pair(sb + c * (kBK * 128), &map_b, fb, bn + c * 64, k0);
+              tma_load_3d_pair(sb + c * (kBK * 128), &map_b, fb, bn + c * 64, k0, bt);
           } else {
-            tma_load_2d_pair(sb, &map_b, fb, k0, bn);
+            tma_load_3d_pair(sb, &map_b, fb, k0, bn, bt);
           }
         }
       }
@@ -260,106 +415,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
+    // Warp w reads TMEM lanes 32 * (w % 4) .. + 32 (its rows) and one half of the columns.
     const int wq = warp & 3;
+    const int half = (warp - 2) >> 2;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     int i = 0;
     for (int t = cid; t < total; t += ncl, ++i) {
       const int buf = i & 1;
-      if (!warp_wait_ns(&bars.acc_full[buf], (i >> 1) & 1, p.status, kStatusTimeoutS, p.wait_ns)) break;
-      tc_fence_after();
-      int mt, nt;
-      tile_coords(t, p, mt, nt);
+      int bt, mt, nt;
+      tile_coords(t, p, bt, mt, nt);
       const int row = mt * 2 * kBM + static_cast<int>(rank) * kBM + wq * 32 + lane;
       const bool valid = row < p.M;
+      const RowOffsets ro = row_offsets(p, bt, row);
       const uint32_t tacc = tmem + lane_off + buf * BN;
-      if (kEpi == kEpiStore) {
-        const int n0 = nt * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld32(tacc + c * 32, v);
-          const int col = n0 + c * 32;
-          if (valid && col < p.N) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] *= p.alpha;
-            if (kOutF32) {
-              float* dst = reinterpret_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + col;
-              if (p.add != nullptr) {
-                const float4* src =
-                    reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.add) + static_cast<int64_t>(row) * p.ldd + col);
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                  const float4 a = src[q];
-                  v[4 * q] += p.beta * a.x;
-                  v[4 * q + 1] += p.beta * a.y;
-                  v[4 * q + 2] += p.beta * a.z;
-                  v[4 * q + 3] += p.beta * a.w;
-                }
-              }
-              float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-              for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-            } else {
-              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + col;
-              if (p.add != nullptr) {
-                float a[32];
-                load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(p.add) + static_cast<int64_t>(row) * p.ldd + col, a);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) v[e] += p.beta * a[e];
-              }
-              store_bf16x32(dst, v);
-            }
-          }
-        }
-      } else if (kEpi == kEpiSwiGLU) {
-        // Columns [0, BN/2) of the accumulator are gate rows, [BN/2, BN) the matching up rows.
-        const int h0 = nt * CF::kBHalf;
-        __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(p.aux) + static_cast<int64_t>(row) * p.ldx;
-        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo;
-#pragma unroll 1
-        for (int c = 0; c < CF::kBHalf / 32; ++c) {
-          float g[32], u[32];
-          tmem_ld32(tacc + c * 32, g);
-          tmem_ld32(tacc + CF::kBHalf + c * 32, u);
-          if (valid) {
-            const int col = h0 + c * 32;
-            store_bf16x32(gu + col, g);
-            store_bf16x32(gu + p.ffn + col, u);
-            // The backward reads the bf16 gate|up, so the product is formed from the rounded values.
-#pragma unroll
-            for (int e = 0; e < 32; ++e) g[e] = silu_ref(bf16_round(g[e])) * bf16_round(u[e]);
-            store_bf16x32(h + col, g);
-          }
-        }
-      } else {  // kEpiSwiGLUBwd: accumulator = d(silu(gate) * up) for columns n0 .. n0 + BN of F
-        const int n0 = nt * BN;
-        const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(p.aux) + static_cast<int64_t>(row) * p.ldx;
-        __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float d[32];
-          tmem_ld32(tacc + c * 32, d);
-          const int col = n0 + c * 32;
-          if (valid && col < p.N) {
-            float g[32], u[32];
-            load_bf16x32(gu + col, g);
-            load_bf16x32(gu + p.ffn + col, u);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float de = bf16_round(d[e]);
-              const float s = 1.f / (1.f + __expf(-g[e]));
-              const float du = de * g[e] * s;
-              g[e] = de * u[e] * s * (1.f + g[e] * (1.f - s));
-              u[e] = du;
-            }
-            store_bf16x32(dgu + col, g);
-            store_bf16x32(dgu + p.ffn + col, u);
-          }
-        }
+      if (kEpi == kEpiSwiGLUBwd) {
+        // Issues its first operand loads before waiting for the accumulator.
+        if (!epilogue_swiglu_bwd<BN>(p, &bars.acc_full[buf], (i >> 1) & 1, tacc, ro, valid, nt * BN, half)) break;
+      } else {
+        if (!warp_wait_ns(&bars.acc_full[buf], (i >> 1) & 1, p.status, kStatusTimeoutS, p.wait_ns)) break;
+        tc_fence_after();
+        if (kEpi == kEpiStore) epilogue_store<BN, kOutF32>(p, tacc, ro, valid, nt * BN, half);
+        else epilogue_swiglu_fwd<BN>(p, tacc, ro, valid, nt * (BN / 2), half);
       }
       tc_fence_before();
       __syncwarp();
-      const bool withhold = p.inject == 1 && i == 0 && leader && wq == 0;
+      const bool withhold = p.inject == 1 && i == 0 && leader && warp == 4;
       if (lane == 0 && !withhold) mbar_arrive_remote(mapa_shared(smem_u32(&bars.acc_empty[buf]), 0));
     }
     // Every MMA that writes this CTA's TMEM has completed before TMEM is freed (the last
@@ -423,16 +503,25 @@ void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams&
     attr[device] = true;
   }
   const int pairs = std::min(resident_pairs(device, reinterpret_cast<const void*>(kernel), CF::kSmem),
-                             p.tiles_m * p.tiles_n);
+                             p.batch * p.tiles_m * p.tiles_n);
   kernel<<<2 * pairs, kThreads, CF::kSmem, st>>>(ma, mb, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 void check_operand(const at::Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.stride(1) == 1, name,
-              ": bf16 CUDA matrix with unit column stride");
-  TORCH_CHECK((t.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name,
-              ": 16-byte aligned base and row stride");
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && (t.dim() == 2 || t.dim() == 3) && t.stride(-1) == 1,
+              name, ": bf16 CUDA matrix (or batch of matrices) with unit column stride");
+  TORCH_CHECK((t.stride(-2) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0 &&
+                  (t.dim() == 2 || (t.stride(0) * 2) % 16 == 0),
+              name, ": 16-byte aligned base and strides");
+}
+
+// TMA map of one operand (2-D: a batch of one), rows x cols with a box of box_cols x box_rows.
+CUtensorMap operand_map(const at::Tensor& t, int box_cols, int box_rows) {
+  const int64_t rows = t.size(-2), cols = t.size(-1), ld = t.stride(-2);
+  const int64_t batch = t.dim() == 3 ? t.size(0) : 1;
+  const int64_t bstride = t.dim() == 3 ? t.stride(0) : rows * ld;
+  return make_tmap_bf16_3d(t.data_ptr(), batch, rows, cols, ld, bstride, box_cols, box_rows);
 }
 
 template <int BN>
@@ -460,6 +549,7 @@ GemmParams base_params(int M, int N, int K, int BN, int64_t group_m, int64_t wai
   p.tiles_m = (M + 2 * kBM - 1) / (2 * kBM);
   p.tiles_n = (N + BN - 1) / BN;
   p.group_m = static_cast<int>(std::max<int64_t>(1, group_m));
+  p.batch = 1;
   p.status = status_word(device);
   p.wait_ns = wait_ns > 0 ? static_cast<unsigned long long>(wait_ns) : 2000000000ull;
   p.inject = static_cast<int>(inject);
@@ -470,42 +560,50 @@ GemmParams base_params(int M, int N, int K, int BN, int64_t group_m, int64_t wai
 
 // out[M, N] = alpha * op(a) @ op(b)^T (+ beta * add).  a: [M, K] (a_mn = false) or [K, M] (a_mn =
 // true); b: [N, K] (b_mn = false) or [K, N] (b_mn = true).  `out` (bf16 or fp32) is allocated as
-// bf16 when absent; `add` has out's dtype and may be `out` itself (in-place accumulation).
+// bf16 when absent; `add` has out's dtype and may be `out` itself (in-place accumulation).  With
+// 3-D operands ([batch, ...], every tensor the same batch) the problems run in one launch.
 at::Tensor gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, c10::optional<at::Tensor> out,
                 c10::optional<at::Tensor> add, double alpha, double beta, int64_t bn, int64_t group_m,
                 int64_t wait_ns, int64_t inject) {
   check_operand(a, "a");
   check_operand(b, "b");
-  const int64_t M = a_mn ? a.size(1) : a.size(0), K = a_mn ? a.size(0) : a.size(1);
-  const int64_t N = b_mn ? b.size(1) : b.size(0);
-  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "inner dimensions differ");
+  TORCH_CHECK(a.dim() == b.dim(), "a and b must both be matrices or both batches");
+  const bool batched = a.dim() == 3;
+  const int64_t B = batched ? a.size(0) : 1;
+  TORCH_CHECK(!batched || b.size(0) == B, "a and b batch sizes differ");
+  const int64_t M = a_mn ? a.size(-1) : a.size(-2), K = a_mn ? a.size(-2) : a.size(-1);
+  const int64_t N = b_mn ? b.size(-1) : b.size(-2);
+  TORCH_CHECK((b_mn ? b.size(-2) : b.size(-1)) == K, "inner dimensions differ");
   TORCH_CHECK(!a_mn || b_mn, "an M-major A needs an N-major B");
   TORCH_CHECK(N % 32 == 0, "N must be a multiple of 32");  // inner extents are checked by the TMA maps
-  TORCH_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "dimensions must fit in int32");
+  TORCH_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31) && B < (1ll << 16), "dimensions out of range");
   const c10::cuda::CUDAGuard guard(a.device());
-  at::Tensor o = out.has_value() ? *out : at::empty({M, N}, a.options());
-  TORCH_CHECK(o.is_cuda() && o.dim() == 2 && o.size(0) == M && o.size(1) == N && o.stride(1) == 1 &&
-                  (o.scalar_type() == at::kBFloat16 || o.scalar_type() == at::kFloat),
-              "out: [M, N] bf16 or fp32 with unit column stride");
+  at::Tensor o = out.has_value() ? *out : (batched ? at::empty({B, M, N}, a.options()) : at::empty({M, N}, a.options()));
+  TORCH_CHECK(o.is_cuda() && o.dim() == a.dim() && o.size(-2) == M && o.size(-1) == N && o.stride(-1) == 1 &&
+                  (!batched || o.size(0) == B) && (o.scalar_type() == at::kBFloat16 || o.scalar_type() == at::kFloat),
+              "out: [(batch,) M, N] bf16 or fp32 with unit column stride");
   const bool f32 = o.scalar_type() == at::kFloat;
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(o.data_ptr()) % 16 == 0 && (o.stride(0) * o.element_size()) % 16 == 0,
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(o.data_ptr()) % 16 == 0 && (o.stride(-2) * o.element_size()) % 16 == 0,
               "out: 16-byte aligned base and row stride");
-  if (M == 0 || N == 0) return o;
+  if (M == 0 || N == 0 || B == 0) return o;
   const int BN = bn == 128 ? 128 : 256;
   const int dev = a.device().index();
   GemmParams p = base_params(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), BN, group_m, wait_ns,
                              inject, dev);
+  p.batch = static_cast<int>(B);
   p.out = o.data_ptr();
-  p.ldo = o.stride(0);
+  p.ldo = o.stride(-2);
+  p.bs_out = batched ? o.stride(0) : 0;
   p.alpha = static_cast<float>(alpha);
   if (add.has_value() && beta != 0.0) {
     const auto& d = *add;
-    TORCH_CHECK(d.scalar_type() == o.scalar_type() && d.dim() == 2 && d.size(0) == M && d.size(1) == N &&
-                    d.stride(1) == 1 && reinterpret_cast<uintptr_t>(d.data_ptr()) % 16 == 0 &&
-                    (d.stride(0) * d.element_size()) % 16 == 0,
+    TORCH_CHECK(d.scalar_type() == o.scalar_type() && d.dim() == o.dim() && d.size(-2) == M && d.size(-1) == N &&
+                    (!batched || d.size(0) == B) && d.stride(-1) == 1 &&
+                    reinterpret_cast<uintptr_t>(d.data_ptr()) % 16 == 0 && (d.stride(-2) * d.element_size()) % 16 == 0,
                 "add: same dtype and shape as out, 16-byte aligned");
     p.add = d.data_ptr();
-    p.ldd = d.stride(0);
+    p.ldd = d.stride(-2);
+    p.bs_add = batched ? d.stride(0) : 0;
     p.beta = static_cast<float>(beta);
   }
   if (K == 0) {  // no products: the result is the scaled addend (or zero)
@@ -513,10 +611,8 @@ at::Tensor gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, c10::optional<
     else o.zero_();
     return o;
   }
-  const CUtensorMap ma = a_mn ? make_tmap_bf16_2d(a.data_ptr(), K, M, a.stride(0), 64, kBK)
-                              : make_tmap_bf16_2d(a.data_ptr(), M, K, a.stride(0), kBK, kBM);
-  const CUtensorMap mb = b_mn ? make_tmap_bf16_2d(b.data_ptr(), K, N, b.stride(0), 64, kBK)
-                              : make_tmap_bf16_2d(b.data_ptr(), N, K, b.stride(0), kBK, BN / 2);
+  const CUtensorMap ma = a_mn ? operand_map(a, 64, kBK) : operand_map(a, kBK, kBM);
+  const CUtensorMap mb = b_mn ? operand_map(b, 64, kBK) : operand_map(b, kBK, BN / 2);
   auto st = at::cuda::getCurrentCUDAStream();
   if (BN == 256) dispatch_store<256>(a_mn, b_mn, f32, ma, mb, p, dev, st);
   else dispatch_store<128>(a_mn, b_mn, f32, ma, mb, p, dev, st);
@@ -528,6 +624,7 @@ at::Tensor gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, c10::optional<
 std::vector<at::Tensor> gemm_swiglu(at::Tensor x, at::Tensor w_gu, int64_t group_m) {
   check_operand(x, "x");
   check_operand(w_gu, "w_gu");
+  TORCH_CHECK(x.dim() == 2 && w_gu.dim() == 2, "x and w_gu must be matrices");
   const int64_t M = x.size(0), K = x.size(1), F = w_gu.size(0) / 2;
   TORCH_CHECK(w_gu.size(1) == K && w_gu.size(0) == 2 * F, "w_gu: [2F, K]");
   TORCH_CHECK(F % 128 == 0, "F must be a multiple of 128");
@@ -544,8 +641,8 @@ std::vector<at::Tensor> gemm_swiglu(at::Tensor x, at::Tensor w_gu, int64_t group
   p.aux = gu.data_ptr();
   p.ldx = gu.stride(0);
   p.ffn = static_cast<int>(F);
-  const CUtensorMap ma = make_tmap_bf16_2d(x.data_ptr(), M, K, x.stride(0), kBK, kBM);
-  const CUtensorMap mb = make_tmap_bf16_2d(w_gu.data_ptr(), 2 * F, K, w_gu.stride(0), kBK, BN / 2);
+  const CUtensorMap ma = operand_map(x, kBK, kBM);
+  const CUtensorMap mb = operand_map(w_gu, kBK, BN / 2);
   launch_pair<256, false, false, kEpiSwiGLU, false>(ma, mb, p, dev, at::cuda::getCurrentCUDAStream());
   return {h, gu};
 }
@@ -557,6 +654,7 @@ at::Tensor gemm_swiglu_bwd(at::Tensor dy, at::Tensor w_down, at::Tensor gu, int6
   check_operand(dy, "dy");
   check_operand(w_down, "w_down");
   check_operand(gu, "gu");
+  TORCH_CHECK(dy.dim() == 2 && w_down.dim() == 2 && gu.dim() == 2, "dy, w_down and gu must be matrices");
   const int64_t M = dy.size(0), D = dy.size(1), F = w_down.size(1);
   TORCH_CHECK(w_down.size(0) == D && gu.size(0) == M && gu.size(1) == 2 * F, "shapes: dy [M, D], w_down [D, F], gu [M, 2F]");
   TORCH_CHECK(F % 32 == 0, "F must be a multiple of 32");
@@ -570,8 +668,8 @@ at::Tensor gemm_swiglu_bwd(at::Tensor dy, at::Tensor w_down, at::Tensor gu, int6
   p.aux = gu.data_ptr();
   p.ldx = gu.stride(0);
   p.ffn = static_cast<int>(F);
-  const CUtensorMap ma = make_tmap_bf16_2d(dy.data_ptr(), M, D, dy.stride(0), kBK, kBM);
-  const CUtensorMap mb = make_tmap_bf16_2d(w_down.data_ptr(), D, F, w_down.stride(0), 64, kBK);
+  const CUtensorMap ma = operand_map(dy, kBK, kBM);
+  const CUtensorMap mb = operand_map(w_down, 64, kBK);
   launch_pair<256, false, true, kEpiSwiGLUBwd, false>(ma, mb, p, dev, at::cuda::getCurrentCUDAStream());
   return dgu;
 }

@@ -16,10 +16,18 @@ GEMM.  Every function needs CUDA bf16 operands; :func:`supported` says when the 
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.nn.functional as F
 
 from mimir_b200.ops._ext import ext, kernels_enabled
+
+
+def _library_comparison() -> bool:
+    """``MIMIR_GEMM=cublas`` routes the projections through ``F.linear`` (cuBLAS) instead of the
+    tcgen05 kernel: an explicit A/B switch for benchmarks, never a fallback."""
+    return os.environ.get("MIMIR_GEMM", "tcgen05") == "cublas"
 
 
 def mm_nt(x: torch.Tensor, w: torch.Tensor, out=None) -> torch.Tensor:
@@ -52,7 +60,8 @@ def _aligned(t: torch.Tensor) -> bool:
 def supported(x: torch.Tensor, w: torch.Tensor) -> bool:
     """True when ``linear(x, w)`` runs on the tcgen05 kernel: CUDA bf16, kernels enabled,
     16-byte aligned rows and an output width that is a multiple of 32."""
-    return (kernels_enabled(x) and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and w.dim() == 2
+    return (kernels_enabled(x) and not _library_comparison() and x.dtype == torch.bfloat16
+            and w.dtype == torch.bfloat16 and w.dim() == 2
             and w.shape[0] % 32 == 0 and w.shape[1] % 8 == 0 and w.shape[1] == x.shape[-1] and w.is_contiguous()
             and _aligned(w))
 
@@ -131,7 +140,7 @@ class _SwiGLUMLPFn(torch.autograd.Function):
 
 def swiglu_mlp_supported(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor) -> bool:
     """True when :func:`swiglu_mlp` runs on the tcgen05 kernels (F a multiple of 128)."""
-    if not (kernels_enabled(x) and x.dtype == w_gu.dtype == w_down.dtype == torch.bfloat16):
+    if not (kernels_enabled(x) and x.dtype == w_gu.dtype == w_down.dtype == torch.bfloat16) or _library_comparison():
         return False
     if w_gu.dim() != 2 or w_down.dim() != 2:
         return False

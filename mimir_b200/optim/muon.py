@@ -55,7 +55,13 @@ def matrix_splits(name, parameter):
 
 
 def muon_update(full, count, steps):
+    """Orthogonalised update of a packed matrix: each of its ``count`` logical pieces separately,
+    scaled by sqrt(max(1, rows/cols)).  On CUDA the pieces go through the batched tcgen05 chain."""
+    from mimir_b200.optim.newton_schulz import orthogonalize_batch, tensor_core_ns_enabled
     pieces = full.chunk(count, dim=0)
+    scale = math.sqrt(max(1, pieces[0].shape[0] / pieces[0].shape[1]))
+    if tensor_core_ns_enabled(full):
+        return (orthogonalize_batch(torch.stack(pieces), steps) * scale).reshape(full.shape).to(full.dtype)
     return torch.cat([orthogonalize(p, steps) * math.sqrt(max(1, p.shape[0] / p.shape[1])) for p in pieces])
 
 

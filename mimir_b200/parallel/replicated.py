@@ -567,12 +567,17 @@ class ReplicatedMuonAdamW(ReplicatedAdamATan2):
     def _orthogonalise(self, owned: list, steps: int) -> None:
         """Newton-Schulz in place on this rank's matrices, batched over equal-shape logical pieces."""
         from mimir_b200.optim.muon import orthogonalize
+        from mimir_b200.optim.newton_schulz import orthogonalize_pieces_, tensor_core_ns_enabled
         by_shape: dict = {}
         for s in owned:
             for piece in self._matrix(s).chunk(self.splits[s.fqn], dim=0):
                 by_shape.setdefault(tuple(piece.shape), []).append(piece)
         for (rows, cols), pieces in by_shape.items():
-            out = orthogonalize(torch.stack(pieces), steps) * math.sqrt(max(1, rows / cols))
+            scale = math.sqrt(max(1, rows / cols))
+            if tensor_core_ns_enabled(pieces[0]):
+                orthogonalize_pieces_(pieces, steps, scale)  # batched bf16 tcgen05 chain
+                continue
+            out = orthogonalize(torch.stack(pieces), steps) * scale
             for piece, o in zip(pieces, out):
                 piece.copy_(o)
 

@@ -161,3 +161,18 @@ def test_bounded_wait_times_out_and_the_next_launch_is_clean():
     assert G.status(0) in (3, 5, 6)
     _close(G.mm_nt(x, w), x.float() @ w.float().t(), name="after the timeout")
     assert G.status(0) == 0
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
+def test_batched_problems_match_per_problem_matmuls(a_mn, b_mn):
+    """A batch of independent problems (3-D operands) in one launch, with the alpha/beta epilogue."""
+    B, M, N, K = 3, 384, 352, 320
+    a = _rand(B, K, M, seed=31) if a_mn else _rand(B, M, K, seed=31)
+    b = _rand(B, K, N, seed=32) if b_mn else _rand(B, N, K, seed=32)
+    add = _rand(B, M, N, seed=33)
+    out = ops.ext().gemm(a, a_mn, b, b_mn, None, add, 0.75, 0.5)
+    af = a.float().mT if a_mn else a.float()
+    bf = b.float() if b_mn else b.float().mT
+    for i in range(B):
+        _close(out[i], 0.75 * (af[i] @ bf[i]) + 0.5 * add[i].float(), name=f"batch {i}")
+    assert G.status(0) == 0
