@@ -38,42 +38,45 @@ RESIDUAL_MIB = 64          # per-process GPU memory still counted as "released"
 RESTORE_MARGIN_MIB = 512
 
 
-def _run(args, timeout=30) -> str:
-    return subprocess.run(args, check=True, text=True, capture_output=True, timeout=timeout).stdout.strip()
+def _output(argv, timeout=30) -> str:
+    return subprocess.run(argv, check=True, text=True, capture_output=True, timeout=timeout).stdout.strip()
+
+
+def _csv(query: str, fields: str) -> list[list[str]]:
+    """Rows of an ``nvidia-smi --query-<query>=<fields>`` listing, values stripped."""
+    text = _output(["nvidia-smi", f"--query-{query}={fields}", "--format=csv,noheader,nounits"])
+    return [[value.strip() for value in line.split(",")] for line in text.splitlines() if line.strip()]
 
 
 class CudaBackend:
-    """``cuda-checkpoint`` and ``nvidia-smi`` queries (read-only except the checkpoint actions)."""
+    """The two external tools the controller drives: ``cuda-checkpoint`` (per-process CUDA state and
+    lock / checkpoint / restore / unlock actions) and read-only ``nvidia-smi`` queries."""
 
-    STATES = ("running", "locked", "checkpointed")
+    STATES = frozenset({"running", "locked", "checkpointed"})
+    LOCK_TIMEOUT_MS = 60000
 
     def __init__(self, executable: str = "cuda-checkpoint", action_timeout: int = 300):
         self.executable, self.action_timeout = executable, action_timeout
 
     def state(self, pid: int) -> str:
-        out = _run([self.executable, "--get-state", "--pid", str(pid)]).lower().strip()
-        if out not in self.STATES:
-            raise RuntimeError(f"Unsupported CUDA state for {pid}: {out!r}")
-        return out
+        reported = _output([self.executable, "--get-state", "--pid", str(pid)]).lower().strip()
+        if reported not in self.STATES:
+            raise RuntimeError(f"Unsupported CUDA state for {pid}: {reported!r}")
+        return reported
 
     def action(self, pid: int, action: str) -> None:
-        args = [self.executable, "--action", action, "--pid", str(pid)]
+        argv = [self.executable, "--action", action, "--pid", str(pid)]
         if action == "lock":
-            args += ["--timeout", "60000"]
-        _run(args, timeout=self.action_timeout)
+            argv += ["--timeout", str(self.LOCK_TIMEOUT_MS)]
+        _output(argv, timeout=self.action_timeout)
 
     def memory(self) -> dict[tuple[int, str], int]:
-        rows = _run(["nvidia-smi", "--query-compute-apps=pid,gpu_uuid,used_gpu_memory",
-                     "--format=csv,noheader,nounits"]).splitlines()
-        out = {}
-        for row in rows:
-            pid, gpu, used = (v.strip() for v in row.split(","))
-            out[(int(pid), gpu)] = int(used)
-        return out
+        """MiB used per (pid, GPU uuid)."""
+        return {(int(pid), gpu): int(used) for pid, gpu, used in _csv("compute-apps", "pid,gpu_uuid,used_gpu_memory")}
 
     def free(self) -> dict[str, int]:
-        rows = _run(["nvidia-smi", "--query-gpu=uuid,memory.free", "--format=csv,noheader,nounits"]).splitlines()
-        return {gpu.strip(): int(free.strip()) for gpu, free in (r.split(",") for r in rows)}
+        """Free MiB per GPU uuid."""
+        return {gpu: int(free) for gpu, free in _csv("gpu", "uuid,memory.free")}
 
 
 class RestoreDeferred(RuntimeError):
@@ -87,15 +90,57 @@ def _host_available_bytes() -> int:
     raise RuntimeError("MemAvailable missing from /proc/meminfo")
 
 
+def _decoded(error, name):
+    value = getattr(error, name, None)
+    return value.decode(errors="replace") if isinstance(value, bytes) else value
+
+
+class Journal:
+    """Append-only ``operations.jsonl`` of one generation; every entry is fsynced before the
+    operation it announces runs."""
+
+    def __init__(self, directory: Path):
+        self.path = Path(directory) / "operations.jsonl"
+
+    def add(self, entry: dict) -> None:
+        with open(self.path, "a") as handle:
+            handle.write(json.dumps(entry | {"time": time.time()}) + "\n")
+            handle.flush()
+            os.fsync(handle.fileno())
+
+
+def _owned_mib_by_gpu(allocations: dict, owned: set) -> dict:
+    per_gpu: dict[str, int] = defaultdict(int)
+    for (pid, gpu), mib in allocations.items():
+        if pid in owned:
+            per_gpu[gpu] += mib
+    return dict(per_gpu)
+
+
+def _live_pids(identities) -> set:
+    alive = set()
+    for identity in identities:
+        try:
+            validate_process(identity)
+            alive.add(identity["pid"])
+        except (OSError, RuntimeError):
+            pass
+    return alive
+
+
 class Controller:
+    """Acts on one control directory: the job's published ranks only."""
+
     def __init__(self, root, backend):
         self.root, self.backend = Path(root), backend
 
     # ------------------------------------------------------------------ readiness
     def ready(self):
+        """(readiness handshake, generation directory) after checking that every published rank
+        is the same live process and acknowledged this generation."""
         launch = read_json(self.root / "launch.json")
         ready = read_json(self.root / "suspend_ready.json")
-        if launch["job_id"] != ready["job_id"] or launch["ranks"] != ready["ranks"]:
+        if (launch["job_id"], launch["ranks"]) != (ready["job_id"], ready["ranks"]):
             raise RuntimeError("Readiness does not match launch")
         resumed = self.root / "resumed.json"
         if resumed.exists() and matches(read_json(resumed), ready):
@@ -109,68 +154,94 @@ class Controller:
         return ready, generation
 
     def journal(self, directory: Path, entry: dict) -> None:
-        with open(directory / "operations.jsonl", "a") as f:
-            f.write(json.dumps(entry | {"time": time.time()}) + "\n")
-            f.flush()
-            os.fsync(f.fileno())
+        Journal(directory).add(entry)
 
     def transition(self, directory: Path, rank: dict, action: str, expected: str) -> None:
+        """One ``cuda-checkpoint`` action on one rank, journaled as intent, then verified or error."""
+        log = Journal(directory)
+        pid = rank["pid"]
         validate_process(rank)
-        self.journal(directory, {"pid": rank["pid"], "action": action, "phase": "intent"})
+        log.add({"pid": pid, "action": action, "phase": "intent"})
         try:
-            self.backend.action(rank["pid"], action)
-            state = self.backend.state(rank["pid"])
-            if state != expected:
-                raise RuntimeError(f"{action} left {rank['pid']} in {state}")
+            self.backend.action(pid, action)
+            reached = self.backend.state(pid)
+            if reached != expected:
+                raise RuntimeError(f"{action} left {pid} in {reached}")
         except Exception as error:
-            def text(name):
-                v = getattr(error, name, None)
-                return v.decode(errors="replace") if isinstance(v, bytes) else v
-            self.journal(directory, {"pid": rank["pid"], "action": action, "phase": "error", "error": str(error),
-                                     "stdout": text("stdout"), "stderr": text("stderr")})
+            log.add({"pid": pid, "action": action, "phase": "error", "error": str(error),
+                     "stdout": _decoded(error, "stdout"), "stderr": _decoded(error, "stderr")})
             raise
-        self.journal(directory, {"pid": rank["pid"], "action": action, "phase": "verified"})
+        log.add({"pid": pid, "action": action, "phase": "verified"})
 
-    # ------------------------------------------------------------------ offload / restore
+    def _states(self, ranks) -> dict:
+        return {r["pid"]: self.backend.state(r["pid"]) for r in ranks}
+
+    # ------------------------------------------------------------------ offload
+    def _admit_offload(self, ready, directory):
+        """Checks before any GPU operation; returns (owned MiB per GPU, allocations)."""
+        if (directory / "cancelled.json").exists() or (directory / "restored.json").exists():
+            raise RuntimeError("This generation has already been released")
+        if (directory / "offload.json").exists():
+            raise RuntimeError("Offload already attempted; inspect status and use recover")
+        if set(self._states(ready["ranks"]).values()) != {"running"}:
+            raise RuntimeError("All ranks must be running before initial offload")
+        allocations = self.backend.memory()
+        needed = _owned_mib_by_gpu(allocations, {r["pid"] for r in ready["ranks"]})
+        if not needed:
+            raise RuntimeError("No owned GPU allocations detected")
+        if _host_available_bytes() < (sum(needed.values()) * 1.1 + 1024) * 1024 ** 2:
+            raise RuntimeError("Insufficient host RAM for offload plus safety margin")
+        return needed, allocations
+
     def offload(self, lease_seconds: float = 600) -> None:
         with exclusive(self.root / "controller.lock"):
             ready, directory = self.ready()
-            if (directory / "cancelled.json").exists() or (directory / "restored.json").exists():
-                raise RuntimeError("This generation has already been released")
-            if (directory / "offload.json").exists():
-                raise RuntimeError("Offload already attempted; inspect status and use recover")
-            ranks = ready["ranks"]
-            if any(self.backend.state(r["pid"]) != "running" for r in ranks):
-                raise RuntimeError("All ranks must be running before initial offload")
-            owned = {r["pid"] for r in ranks}
-            allocations = self.backend.memory()
-            needed: dict[str, int] = defaultdict(int)
-            for (pid, gpu), mib in allocations.items():
-                if pid in owned:
-                    needed[gpu] += mib
-            if not needed:
-                raise RuntimeError("No owned GPU allocations detected")
-            if _host_available_bytes() < (sum(needed.values()) * 1.1 + 1024) * 1024 ** 2:
-                raise RuntimeError("Insufficient host RAM for offload plus safety margin")
-            peers = sorted({pid for pid, gpu in allocations if pid not in owned and gpu in needed})
+            needed, allocations = self._admit_offload(ready, directory)
+            owned = {r["pid"] for r in ready["ranks"]}
+            others = sorted({pid for pid, gpu in allocations if pid not in owned and gpu in needed})
             atomic_write(directory / "offload.json", ready | {
-                "needed_mib": dict(needed), "lease_until": time.time() + lease_seconds,
+                "needed_mib": needed, "lease_until": time.time() + lease_seconds,
                 "allocations": [{"pid": pid, "gpu": gpu, "mib": mib} for (pid, gpu), mib in allocations.items()
                                 if pid in owned],
-                "existing_peers": [process_identity(pid) for pid in peers]})
-            for rank in ranks:  # every rank locked before any is checkpointed
-                self.transition(directory, rank, "lock", "locked")
-            for rank in ranks:
-                self.transition(directory, rank, "checkpoint", "checkpointed")
-            left = {k: v for k, v in self.backend.memory().items() if k[0] in owned}
-            if any(mib > RESIDUAL_MIB for mib in left.values()):
+                "existing_peers": [process_identity(pid) for pid in others]})
+            for action, reached in (("lock", "locked"), ("checkpoint", "checkpointed")):
+                for rank in ready["ranks"]:  # every rank locked before any is checkpointed
+                    self.transition(directory, rank, action, reached)
+            leftover = {key: mib for key, mib in self.backend.memory().items() if key[0] in owned}
+            if max(leftover.values(), default=0) > RESIDUAL_MIB:
                 raise RuntimeError("Owned GPU memory not released; do not admit evaluations")
-            atomic_write(directory / "offloaded.json", ready | {"remaining_owned_mib": sum(left.values())})
+            atomic_write(directory / "offloaded.json", ready | {"remaining_owned_mib": sum(leftover.values())})
 
+    # ------------------------------------------------------------------ restore
     def _held(self) -> bool:
+        if (self.root / "hold").exists():
+            return True
         managed = self.root / "managed.json"
-        supervisor_hold = managed.exists() and (Path(read_json(managed)["supervisor_root"]) / "hold").exists()
-        return (self.root / "hold").exists() or supervisor_hold
+        return managed.exists() and (Path(read_json(managed)["supervisor_root"]) / "hold").exists()
+
+    def _check_restore_room(self, ready: dict, receipt: dict, states: dict) -> None:
+        """No new occupant on the job's GPUs, and headroom for what still has to come back."""
+        pending: dict[str, int] = defaultdict(int)
+        for entry in receipt.get("allocations", []):
+            if states[entry["pid"]] == "checkpointed":  # after a partial restore only these need room
+                pending[entry["gpu"]] += entry["mib"]
+        if not pending:
+            pending.update(receipt["needed_mib"])
+        tolerated = {r["pid"] for r in ready["ranks"]} | _live_pids(receipt.get("existing_peers", []))
+        if any(pid not in tolerated and gpu in receipt["needed_mib"] for pid, gpu in self.backend.memory()):
+            raise RestoreDeferred("New GPU workload is still present; defer restore")
+        free = self.backend.free()
+        if any(free.get(gpu, 0) < mib + RESTORE_MARGIN_MIB for gpu, mib in pending.items()):
+            raise RestoreDeferred("Not enough GPU headroom to restore safely")
+
+    def _bring_back(self, directory: Path, rank: dict) -> None:
+        """checkpointed -> locked -> running, from wherever a previous attempt stopped."""
+        state = self.backend.state(rank["pid"])
+        if state == "checkpointed":
+            self.transition(directory, rank, "restore", "locked")
+            state = "locked"
+        if state == "locked":
+            self.transition(directory, rank, "unlock", "running")
 
     def restore(self) -> None:
         with exclusive(self.root / "controller.lock"):
@@ -180,54 +251,31 @@ class Controller:
             receipt = read_json(directory / "offload.json")
             if not matches(receipt, ready):
                 raise RuntimeError("Offload receipt mismatch")
-            states = {r["pid"]: self.backend.state(r["pid"]) for r in ready["ranks"]}
+            states = self._states(ready["ranks"])
             if "checkpointed" in states.values():
                 self._check_restore_room(ready, receipt, states)
             for rank in ready["ranks"]:
-                state = self.backend.state(rank["pid"])
-                if state == "checkpointed":
-                    self.transition(directory, rank, "restore", "locked")
-                    state = "locked"
-                if state == "locked":
-                    self.transition(directory, rank, "unlock", "running")
-            if any(self.backend.state(r["pid"]) != "running" for r in ready["ranks"]):
-                raise RuntimeError("Not all ranks restored")
+                self._bring_back(directory, rank)
+            if set(self._states(ready["ranks"]).values()) != {"running"}:
+                raise RuntimeError("Not all ranks restored")  # release nobody after a partial restore
             atomic_write(directory / "restored.json", ready)
             self.release(directory, ready)
 
-    def _check_restore_room(self, ready: dict, receipt: dict, states: dict) -> None:
-        needed: dict[str, int] = defaultdict(int)
-        for a in receipt.get("allocations", []):
-            if states[a["pid"]] == "checkpointed":  # after a partial restore only these need room
-                needed[a["gpu"]] += a["mib"]
-        if not needed:
-            needed.update(receipt["needed_mib"])
-        allowed = {r["pid"] for r in ready["ranks"]}
-        for peer in receipt.get("existing_peers", []):
-            try:
-                validate_process(peer)
-                allowed.add(peer["pid"])
-            except (OSError, RuntimeError):
-                pass
-        if any(pid not in allowed and gpu in receipt["needed_mib"] for pid, gpu in self.backend.memory()):
-            raise RestoreDeferred("New GPU workload is still present; defer restore")
-        free = self.backend.free()
-        if any(free.get(gpu, 0) < mib + RESTORE_MARGIN_MIB for gpu, mib in needed.items()):
-            raise RestoreDeferred("Not enough GPU headroom to restore safely")
-
     def release(self, directory: Path, ready: dict) -> None:
+        """Write each rank's resume token (unless that rank already consumed it)."""
+        answer = {key: ready[key] for key in ("job_id", "generation", "step")}
         for rank in ready["ranks"]:
             token = directory / f"resume.{rank['pid']}"
             if not token.with_suffix(token.suffix + ".consumed").exists():
-                atomic_write(token, {k: ready[k] for k in ("job_id", "generation", "step")}
-                             | {"start_ticks": rank["start_ticks"]})
+                atomic_write(token, answer | {"start_ticks": rank["start_ticks"]})
 
     def cancel_unoffloaded(self) -> None:
+        """Release a handshake that never reached a GPU operation."""
         with exclusive(self.root / "controller.lock"):
             ready, directory = self.ready()
             if (self.root / "hold").exists() or (directory / "offload.json").exists():
                 raise RuntimeError("Cannot cancel: user hold or offload already attempted")
-            if any(self.backend.state(r["pid"]) != "running" for r in ready["ranks"]):
+            if set(self._states(ready["ranks"]).values()) != {"running"}:
                 raise RuntimeError("Cannot cancel: CUDA state is not running")
             atomic_write(directory / "cancelled.json", ready)
             self.release(directory, ready)
@@ -235,35 +283,37 @@ class Controller:
     def status(self) -> dict:
         out = {"launch": read_json(self.root / "launch.json")}
         for name in ("queue", "suspend_ready", "resumed"):
-            if (self.root / f"{name}.json").exists():
-                out[name] = read_json(self.root / f"{name}.json")
+            path = self.root / f"{name}.json"
+            if path.exists():
+                out[name] = read_json(path)
         return out
 
 
 def wait_offloaded(proc, backend, controller: Controller, seconds: float, deadline: float, resume_request=None):
-    """Hold an offloaded pause for ``seconds``, re-checking liveness, states and released memory."""
+    """Hold an offloaded pause for ``seconds``, re-checking liveness, CUDA states and released memory
+    (each check journaled as ``pause_health``)."""
     ready, generation = controller.ready()
     pids = {r["pid"] for r in ready["ranks"]}
+    log = Journal(generation)
     end = time.monotonic() + seconds
     while True:
         if proc.poll() is not None:
             raise RuntimeError("Worker launcher exited during offloaded pause")
         if resume_request is not None and Path(resume_request).exists():
-            controller.journal(generation, {"phase": "early_resume_requested", "request": str(resume_request)})
+            log.add({"phase": "early_resume_requested", "request": str(resume_request)})
             return
         controller.ready()
         states = {pid: backend.state(pid) for pid in pids}
         owned = sum(mib for (pid, _), mib in backend.memory().items() if pid in pids)
         if set(states.values()) != {"checkpointed"} or owned > RESIDUAL_MIB * len(pids):
             raise RuntimeError(f"Offloaded state changed: {states}, {owned} MiB")
-        remaining = max(0.0, end - time.monotonic())
-        controller.journal(generation, {"phase": "pause_health", "states": states, "owned_gpu_mib": owned,
-                                        "remaining_seconds": remaining})
-        if not remaining:
+        left = max(0.0, end - time.monotonic())
+        log.add({"phase": "pause_health", "states": states, "owned_gpu_mib": owned, "remaining_seconds": left})
+        if left == 0:
             return
         if time.monotonic() >= deadline:
             raise TimeoutError("Deadline exceeded during offloaded pause")
-        time.sleep(min(30, remaining, max(0, deadline - time.monotonic())))
+        time.sleep(min(30, left, max(0, deadline - time.monotonic())))
 
 
 def bootstrap(root: Path, command) -> None:
@@ -271,14 +321,32 @@ def bootstrap(root: Path, command) -> None:
     source = os.environ.get("CUDA_CHECKPOINT_JOB_FILE")
     if not source:
         raise RuntimeError("bootstrap must be invoked through cuda-checkpoint --launch-job")
-    dest = Path(tempfile.mkdtemp(prefix="cuda-job-", dir=root)) / "job.bin"
-    shutil.copyfile(source, dest)
-    dest.chmod(0o600)
-    os.environ["CUDA_CHECKPOINT_JOB_FILE"] = str(dest)
+    handle = Path(tempfile.mkdtemp(prefix="cuda-job-", dir=root)) / "job.bin"
+    shutil.copyfile(source, handle)
+    handle.chmod(0o600)
+    os.environ["CUDA_CHECKPOINT_JOB_FILE"] = str(handle)
     os.execvp(command[0], command)
 
 
-def main(argv=None) -> None:
+def _watch(controller: Controller, interval: float, ready_timeout: float) -> None:
+    """Recovery watcher for unsupervised jobs: cancel a handshake nobody offloaded in time, restore
+    an offload whose lease ran out."""
+    while True:
+        try:
+            ready, directory = controller.ready()
+            receipt = directory / "offload.json"
+            if not receipt.exists():
+                if time.time() >= ready["ready_at"] + ready_timeout:
+                    controller.cancel_unoffloaded()
+            elif time.time() >= read_json(receipt)["lease_until"]:
+                controller.restore()
+                print("Restoration released; awaiting resumed acknowledgement", flush=True)
+        except (OSError, RuntimeError, subprocess.SubprocessError) as error:
+            print(f"[suspend-watch] {error}", flush=True)
+        time.sleep(interval)
+
+
+def _parser() -> argparse.ArgumentParser:
     parser = argparse.ArgumentParser(description="CUDA suspension controller")
     parser.add_argument("--cuda-checkpoint", default="cuda-checkpoint")
     sub = parser.add_subparsers(dest="action", required=True)
@@ -287,26 +355,36 @@ def main(argv=None) -> None:
         p.add_argument("control_dir", type=Path)
         if action == "request":
             p.add_argument("steps", nargs="+", type=int)
-        if action == "offload":
+        elif action == "offload":
             p.add_argument("--lease-seconds", type=int, default=600)
-        if action == "watch":
+        elif action == "watch":
             p.add_argument("--interval", type=float, default=5)
             p.add_argument("--ready-timeout", type=float, default=600)
     for action in ("launch", "_bootstrap"):
         p = sub.add_parser(action)
         p.add_argument("--control-root", required=True, type=Path)
         p.add_argument("command", nargs=argparse.REMAINDER)
+    return parser
+
+
+def _launch(parser, args) -> None:
+    command = args.command[1:] if args.command[:1] == ["--"] else args.command
+    if not command:
+        parser.error("Missing training command")
+    args.control_root.mkdir(parents=True, exist_ok=True)
+    if args.action == "_bootstrap":
+        bootstrap(args.control_root.resolve(), command)
+    os.execv(args.cuda_checkpoint, [args.cuda_checkpoint, "--launch-job", sys.executable, "-m",
+                                    "mimir_b200.train.suspension.controller", "_bootstrap", "--control-root",
+                                    str(args.control_root.resolve()), "--", *command])
+
+
+def main(argv=None) -> None:
+    parser = _parser()
     args = parser.parse_args(argv)
     if args.action in ("launch", "_bootstrap"):
-        command = args.command[1:] if args.command[:1] == ["--"] else args.command
-        if not command:
-            parser.error("Missing training command")
-        args.control_root.mkdir(parents=True, exist_ok=True)
-        if args.action == "_bootstrap":
-            bootstrap(args.control_root.resolve(), command)
-        os.execv(args.cuda_checkpoint, [args.cuda_checkpoint, "--launch-job", sys.executable, "-m",
-                                        "mimir_b200.train.suspension.controller", "_bootstrap", "--control-root",
-                                        str(args.control_root.resolve()), "--", *command])
+        _launch(parser, args)
+        return
     controller = Controller(args.control_dir, CudaBackend(args.cuda_checkpoint))
     if args.action == "request":
         print(submit(args.control_dir, args.steps))
@@ -327,19 +405,7 @@ def main(argv=None) -> None:
             parser.error("This job has a supervisor; do not run a second recovery watcher")
         if args.interval <= 0:
             parser.error("interval must be positive")
-        while True:
-            try:
-                ready, directory = controller.ready()
-                receipt = directory / "offload.json"
-                if not receipt.exists():
-                    if time.time() >= ready["ready_at"] + args.ready_timeout:
-                        controller.cancel_unoffloaded()
-                elif time.time() >= read_json(receipt)["lease_until"]:
-                    controller.restore()
-                    print("Restoration released; awaiting resumed acknowledgement", flush=True)
-            except (OSError, RuntimeError, subprocess.SubprocessError) as error:
-                print(f"[suspend-watch] {error}", flush=True)
-            time.sleep(args.interval)
+        _watch(controller, args.interval, args.ready_timeout)
 
 
 if __name__ == "__main__":

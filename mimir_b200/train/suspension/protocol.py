@@ -1,16 +1,21 @@
-"""Host-only file protocol shared by the training hook and its controllers (no torch imports).
+"""File protocol shared by the training hook and the processes that suspend it (no torch imports).
 
-Reference behaviour: ``src/mimir/training/suspension/protocol.py:14-116``.  File names and
-JSON shapes are part of the protocol between independent processes, so they match:
+Behavioural reference: ``src/mimir/training/suspension/protocol.py:14-116``.  Independent
+processes (the training ranks, a controller, a supervisor, a user's ``submit``) talk through a
+control directory, so file names and JSON keys are the protocol:
 
-* ``atomic_write`` — temp file in the same directory, fsync, ``os.replace``, fsync the directory;
-* ``exclusive`` — non-blocking ``flock`` (a dead owner releases it; the inode is never unlinked);
-* ``process_identity`` — ``pid`` + start time in clock ticks (``/proc/<pid>/stat`` field 22) +
-  hostname + boot id, so a recycled pid is never mistaken for the original process;
-* requests — ``suspend_after_steps`` (space-separated positive steps) merged under
-  ``requests.lock``; the hook claims the file by renaming it to ``request.<uuid>.claimed``,
-  invalid claims are quarantined as ``.rejected`` with a ``.rejected.json`` reason;
-* ``wait_json`` — poll a JSON record until its ``job_id``/``generation``/``step`` match.
+* every record is replaced atomically (temporary file in the same directory, fsync, rename,
+  fsync of the directory), so a reader sees the old or the new version, never a torn one;
+* single-writer sections hold a non-blocking ``flock`` (released by the kernel if the owner dies;
+  the lock file is never unlinked, so its inode stays the one everyone locks);
+* a process is identified by pid + start time in clock ticks (``/proc/<pid>/stat`` field 22) +
+  host name + boot id, so a recycled pid is never mistaken for the original process;
+* suspend requests live in ``suspend_after_steps`` (space-separated positive steps), merged
+  under ``requests.lock``; the hook claims them by renaming the file to
+  ``request.<uuid>.claimed``; a claim that does not parse is quarantined as ``.rejected`` with a
+  ``.rejected.json`` reason;
+* records that answer a request carry ``job_id``, ``generation`` and ``step``; a waiter polls
+  until all three match.
 """
 from __future__ import annotations
 
@@ -23,29 +28,39 @@ import time
 import uuid
 from contextlib import contextmanager
 from pathlib import Path
+from typing import Iterable, Optional
 
-_TOKEN_KEYS = ("job_id", "generation", "step")
-_IDENTITY_KEYS = ("pid", "start_ticks", "host", "boot_id")
+REQUEST_FILE = "suspend_after_steps"
+REQUEST_LOCK = "requests.lock"
+ANSWER_KEYS = ("job_id", "generation", "step")
+IDENTITY_KEYS = ("pid", "start_ticks", "host", "boot_id")
+
+
+# ------------------------------------------------------------------ atomic records
+def _fsync_directory(directory: Path) -> None:
+    fd = os.open(directory, os.O_RDONLY | os.O_DIRECTORY)
+    try:
+        os.fsync(fd)
+    finally:
+        os.close(fd)
 
 
 def atomic_write(path, value) -> None:
-    path = Path(path)
-    path.parent.mkdir(parents=True, exist_ok=True)
-    fd, temp = tempfile.mkstemp(prefix=f".{path.name}.", dir=path.parent)
+    """Replace ``path`` with ``value`` (a string, or JSON with sorted keys) atomically."""
+    target = Path(path)
+    target.parent.mkdir(parents=True, exist_ok=True)
+    text = value if isinstance(value, str) else json.dumps(value, sort_keys=True)
+    fd, scratch = tempfile.mkstemp(prefix=f".{target.name}.", dir=target.parent)
     try:
-        with os.fdopen(fd, "w") as f:
-            f.write(value if isinstance(value, str) else json.dumps(value, sort_keys=True))
-            f.flush()
-            os.fsync(f.fileno())
-        os.replace(temp, path)
-        dfd = os.open(path.parent, os.O_RDONLY | os.O_DIRECTORY)
-        try:
-            os.fsync(dfd)
-        finally:
-            os.close(dfd)
+        with os.fdopen(fd, "w") as handle:
+            handle.write(text)
+            handle.flush()
+            os.fsync(handle.fileno())
+        os.replace(scratch, target)
+        _fsync_directory(target.parent)
     finally:
-        if os.path.exists(temp):
-            os.unlink(temp)
+        if os.path.exists(scratch):
+            os.unlink(scratch)
 
 
 def read_json(path):
@@ -54,82 +69,102 @@ def read_json(path):
 
 @contextmanager
 def exclusive(path):
-    """Hold a non-blocking exclusive flock on ``path`` (raises ``BlockingIOError`` if held)."""
-    with open(path, "a+") as f:
-        fcntl.flock(f, fcntl.LOCK_EX | fcntl.LOCK_NB)
+    """Hold a non-blocking exclusive flock on ``path``; ``BlockingIOError`` if someone else does."""
+    with open(path, "a+") as handle:
+        fcntl.flock(handle, fcntl.LOCK_EX | fcntl.LOCK_NB)
         try:
             yield
         finally:
-            fcntl.flock(f, fcntl.LOCK_UN)
+            fcntl.flock(handle, fcntl.LOCK_UN)
+
+
+# ------------------------------------------------------------------ process identity
+def _boot_id() -> str:
+    return Path("/proc/sys/kernel/random/boot_id").read_text().strip()
 
 
 def process_identity(pid=None) -> dict:
+    """``{pid, start_ticks, host, boot_id}`` of a live (non-zombie) process."""
     pid = os.getpid() if pid is None else int(pid)
-    fields = Path(f"/proc/{pid}/stat").read_text().rsplit(")", 1)[1].split()
-    if fields[0] == "Z":
+    # Fields after the parenthesised command name: state is the first, start time the 20th.
+    after_name = Path(f"/proc/{pid}/stat").read_text().rsplit(")", 1)[1].split()
+    state, start_ticks = after_name[0], after_name[19]
+    if state == "Z":
         raise RuntimeError(f"Process {pid} is a zombie")
-    return {"pid": pid, "start_ticks": fields[19], "host": socket.gethostname(),
-            "boot_id": Path("/proc/sys/kernel/random/boot_id").read_text().strip()}
+    return {"pid": pid, "start_ticks": start_ticks, "host": socket.gethostname(), "boot_id": _boot_id()}
 
 
 def validate_process(identity: dict) -> None:
-    if process_identity(identity["pid"]) != {k: identity[k] for k in _IDENTITY_KEYS}:
+    """Raise unless the process recorded in ``identity`` is still the same running process."""
+    recorded = {key: identity[key] for key in IDENTITY_KEYS}
+    if process_identity(identity["pid"]) != recorded:
         raise RuntimeError(f"Process identity changed: {identity}")
 
 
+# ------------------------------------------------------------------ suspend requests
 def steps(values) -> list[int]:
-    """Parse suspend steps (a string or an iterable); every value must be a positive integer."""
-    if isinstance(values, str):
-        values = values.split()
-    out = set()
-    for v in values:
-        if isinstance(v, bool) or not str(v).isdigit() or int(v) < 1:
-            raise ValueError(f"Invalid suspend step: {v!r}")
-        out.add(int(v))
-    return sorted(out)
+    """Sorted distinct suspend steps from a string or an iterable; each must be a positive integer."""
+    items: Iterable = values.split() if isinstance(values, str) else values
+    parsed = set()
+    for item in items:
+        text = str(item)
+        if isinstance(item, bool) or not text.isdigit() or int(text) < 1:
+            raise ValueError(f"Invalid suspend step: {item!r}")
+        parsed.add(int(text))
+    return sorted(parsed)
 
 
 def submit(root, values) -> list[int]:
-    """Add suspend steps to a running job's request file; returns the merged pending list."""
-    root = Path(root)
-    read_json(root / "launch.json")  # a typo'd or uninitialised control dir fails here
-    with exclusive(root / "requests.lock"):
-        path = root / "suspend_after_steps"
-        merged = steps((steps(path.read_text()) if path.exists() else []) + steps(values))
-        atomic_write(path, " ".join(map(str, merged)) + "\n")
+    """Add suspend steps to a running job's pending requests; returns the merged list.  A control
+    directory without ``launch.json`` (a typo, or a job not yet launched) is refused."""
+    control = Path(root)
+    read_json(control / "launch.json")
+    requests = control / REQUEST_FILE
+    with exclusive(control / REQUEST_LOCK):
+        pending = steps(requests.read_text()) if requests.exists() else []
+        merged = steps(pending + steps(values))
+        atomic_write(requests, " ".join(str(s) for s in merged) + "\n")
     return merged
 
 
-def claim(root):
-    """Take ownership of pending requests: ``(claimed path, steps)`` or ``(None, [])``."""
-    root = Path(root)
-    path = root / "suspend_after_steps"
-    with exclusive(root / "requests.lock"):
-        if not path.exists():
+def _quarantine(claimed: Path, error: ValueError) -> None:
+    atomic_write(claimed.with_suffix(".rejected.json"), {"error": str(error)})
+    claimed.rename(claimed.with_suffix(".rejected"))
+
+
+def claim(root) -> tuple[Optional[Path], list[int]]:
+    """Take ownership of the pending requests: ``(claimed file, steps)``, or ``(None, [])`` when
+    there are none or they do not parse (then they are quarantined)."""
+    control = Path(root)
+    requests = control / REQUEST_FILE
+    with exclusive(control / REQUEST_LOCK):
+        if not requests.exists():
             return None, []
-        claimed = root / f"request.{uuid.uuid4().hex}.claimed"
-        os.replace(path, claimed)
+        claimed = control / f"request.{uuid.uuid4().hex}.claimed"
+        os.replace(requests, claimed)
     try:
         return claimed, steps(claimed.read_text())
     except ValueError as error:
-        atomic_write(claimed.with_suffix(".rejected.json"), {"error": str(error)})
-        claimed.rename(claimed.with_suffix(".rejected"))
+        _quarantine(claimed, error)
         return None, []
 
 
+# ------------------------------------------------------------------ answers
 def matches(record: dict, expected: dict) -> bool:
-    return all(record.get(k) == expected[k] for k in _TOKEN_KEYS)
+    return all(record.get(key) == expected[key] for key in ANSWER_KEYS)
 
 
 def wait_json(path, expected: dict, interval: float, timeout=None) -> dict:
-    start = time.monotonic()
+    """Poll ``path`` until it holds a record answering ``expected``; ``TimeoutError`` after
+    ``timeout`` seconds (None: wait forever)."""
+    deadline = None if timeout is None else time.monotonic() + timeout
     while True:
         try:
             record = read_json(path)
-            if matches(record, expected):
-                return record
         except FileNotFoundError:
-            pass
-        if timeout is not None and time.monotonic() - start > timeout:
+            record = None
+        if record is not None and matches(record, expected):
+            return record
+        if deadline is not None and time.monotonic() > deadline:
             raise TimeoutError(f"Waiting for {path}")
         time.sleep(interval)
