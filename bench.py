@@ -277,6 +277,8 @@ def measure_ours(args, rank, world, local, kv_heads):
     torch.cuda.synchronize()
     e2e_seconds = max_over_ranks(time.perf_counter() - t0)
     unseen = heldout_loss(lambda b: state.model(batch=b, carry=state.carry, bp_steps=2)[2], device, wrap_tensor)
+    from mimir_b200.ops._ext import check_kernel_status
+    check_kernel_status(device)  # no kernel wait of the measured steps timed out
     flops = model_flops_per_step(hosts[0][0], kv_heads)
     engine = engine_of(model)
     if engine is not None:

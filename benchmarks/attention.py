@@ -30,8 +30,6 @@ def main():
     ap.add_argument("--max-prefix", type=int, default=2048)
     ap.add_argument("--causal", action="store_true")
     ap.add_argument("--once", action="store_true", help="one forward + one backward launch (for profilers)")
-    ap.add_argument("--trace", action="store_true", help="dump per-iteration event times of one backward CTA")
-    ap.add_argument("--bwd-mode", type=int, default=0, help="backward profiling experiment bits (results invalid)")
     args = ap.parse_args()
     from mimir_b200 import ops
     from mimir_b200.data.prefixlm import compute_aux_seq_tensors_scalars
@@ -63,22 +61,8 @@ def main():
     delta = C.attn_delta(do, out, H)
 
     def bwd():
-        return C.fmha_bwd(q, 0, k, 0, v, 0, do, lse, delta, H, KV, args.causal, cu, pl, nseq, kv_tiles, kv_ntiles,
-                          mode=args.bwd_mode)
+        return C.fmha_bwd(q, 0, k, 0, v, 0, do, lse, delta, H, KV, args.causal, cu, pl, nseq, kv_tiles, kv_ntiles)
 
-    if args.trace:
-        trace = torch.zeros(64 * 14 * 4, dtype=torch.int64, device="cuda")
-        for _ in range(2):
-            C.fmha_bwd(q, 0, k, 0, v, 0, do, lse, delta, H, KV, args.causal, cu, pl, nseq, kv_tiles, kv_ntiles,
-                       trace=trace, trace_tile=0, mode=args.bwd_mode)
-        torch.cuda.synchronize()
-        t = trace.view(64, 14, 4).cpu()
-        t0 = int(t[t > 0].min())
-        for it in range(2, 6):
-            for w in range(14):
-                vals = [int(x) - t0 if int(x) > 0 else -1 for x in t[it, w]]
-                print(json.dumps({"iter": it, "warp": w, "ev": vals}))
-        return
     if args.once:
         fwd()
         bwd()

@@ -47,8 +47,7 @@ std::vector<at::Tensor> fmha_bwd_plan(at::Tensor cu_seqlens, at::Tensor prefix_l
 std::vector<at::Tensor> fmha_bwd(at::Tensor q_src, int64_t q_col, at::Tensor k_src, int64_t k_col, at::Tensor v_src,
                                  int64_t v_col, at::Tensor d_o, at::Tensor lse, at::Tensor delta, int64_t H,
                                  int64_t KV, bool is_causal, at::Tensor cu_seqlens, at::Tensor prefix_lens,
-                                 int64_t numseqs, at::Tensor kv_tiles, at::Tensor kv_ntiles,
-                                 c10::optional<at::Tensor> trace, int64_t trace_tile, int64_t mode);
+                                 int64_t numseqs, at::Tensor kv_tiles, at::Tensor kv_ntiles);
 
 // dp_fused.cu
 int64_t dp_segment_bytes();
@@ -124,8 +123,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_swiglu", &gemm_swiglu, py::arg("x"), py::arg("w_gu"), py::arg("group_m") = 8);
   m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd, py::arg("dy"), py::arg("w_down"), py::arg("gu"), py::arg("group_m") = 8);
   m.def("gemm_status", &gemm_status);
-  m.def("fmha_bwd", &fmha_bwd, py::arg("q_src"), py::arg("q_col"), py::arg("k_src"), py::arg("k_col"),
-        py::arg("v_src"), py::arg("v_col"), py::arg("d_o"), py::arg("lse"), py::arg("delta"), py::arg("H"),
-        py::arg("KV"), py::arg("is_causal"), py::arg("cu_seqlens"), py::arg("prefix_lens"), py::arg("numseqs"),
-        py::arg("kv_tiles"), py::arg("kv_ntiles"), py::arg("trace") = py::none(), py::arg("trace_tile") = 0, py::arg("mode") = 0);
+  m.def("fmha_bwd", &fmha_bwd);
 }

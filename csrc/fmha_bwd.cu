@@ -56,16 +56,6 @@ struct BwdParams {
   float scale_log2;            // log2(e) / sqrt(128)
   float scale;                 // 1 / sqrt(128)
   int* status;
-  unsigned long long* trace;   // optional event timestamps of CTA (0, trace_tile) for profiling
-  int trace_tile;
-  int mode;                    // profiling experiments only (results invalid): bit3 no dQ reduce-add, bit4 no dQ staging
-};
-
-// Event slots per iteration in the optional trace buffer.
-enum TraceEvent : int {
-  kEvMmaSdpIssued = 0, kEvMmaDsReady = 1, kEvMmaAccIssued = 2, kEvSmSdpFull = 3, kEvSmLoaded = 4,
-  kEvSmPdsFree = 5, kEvSmDsReady = 6, kEvDqFull = 7, kEvDqStaged = 8, kEvDqReduced = 9, kEvProdIssued = 10,
-  kEvCount = 16
 };
 
 struct __align__(8) Barriers {
@@ -138,11 +128,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  unsigned long long* trace = (p.trace != nullptr && blockIdx.x == 0 && tile == p.trace_tile) ? p.trace : nullptr;
-  // Per-warp event marks (lane 0 of each warp): trace[(iteration * 14 + warp) * 4 + event].
-  auto wmark = [&](int it, int ev) {
-    if (trace != nullptr && it < 64 && lane == 0) trace[(it * 14 + warp) * 4 + ev] = global_timer_ns();
-  };
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->kv_full, 1);
@@ -196,7 +181,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = i % kStages;
         if (i >= kStages && !mbar_wait(&bar->qdo_empty[s], ((i / kStages) - 1) & 1, p.status, kStatusTimeoutEmpty))
           break;
-        wmark(i, 0);
         const int hq = kvh * group + i / nqb;
         const int row = start + (qfirst_block + i % nqb) * kQRows;
         const int qx = p.q_col + hq * kHeadDim, dox = hq * kHeadDim;
@@ -244,11 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; ok && i < n; ++i) {
         const int s = i % kStages;
         if (i + 1 < n && !issue_sdp(i + 1)) { ok = false; break; }
-        wmark(i, 0);
         if (!mbar_wait(&bar->ds_ready, i & 1, p.status, kStatusTimeoutP)) { ok = false; break; }
-        wmark(i, 1);
         if (i >= 2 && !mbar_wait(&bar->dq_free[i & 1], ((i >> 1) - 1) & 1, p.status, kStatusTimeoutO)) { ok = false; break; }
-        wmark(i, 2);
         tc_fence_after();
         const uint32_t sq = smem_u32(q_stage(smem, s)), sdo = smem_u32(do_stage(smem, s));
 #pragma unroll
@@ -269,7 +250,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&bar->dq_full[i & 1]);
         mma_commit(&bar->pds_free);
         mma_commit(&bar->qdo_empty[s]);
-        wmark(i, 3);
       }
       mma_commit(&bar->acc_full);
       mma_commit(&bar->mma_done);
@@ -301,7 +281,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q0 = (qfirst_block + i % nqb) * kQRows;
       if (i + 1 < n) fetch(i + 1, nxt_lse, nxt_dl);
       if (!warp_wait(&bar->sdp_full, i & 1, p.status, kStatusTimeoutS)) { ok = false; break; }
-      wmark(i, 0);
       tc_fence_after();
       float sv[32], dpv[32];
       ld32(tS + lane_off + col_off, sv);
@@ -309,7 +288,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->s_free);
-      wmark(i, 1);
       uint32_t pk[16], dk[16];
       // Branch-free element loop: masked entries get an exponent argument of -inf (exp2 -> 0), so
       // the compiler keeps one basic block and interleaves the 32 independent element chains.
@@ -334,9 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk[c >> 1] = pack_bf16x2(pe[0], pe[1]);
         dk[c >> 1] = pack_bf16x2(de[0], de[1]);
       }
-      wmark(i, 2);
       if (i > 0 && !warp_wait(&bar->pds_free, (i - 1) & 1, p.status, kStatusTimeoutP)) { ok = false; break; }
-      wmark(i, 3);
 #pragma unroll
       for (int u4 = 0; u4 < 4; ++u4) {
         const int u = half * 4 + u4;  // 16-byte unit of the 128-byte row
@@ -392,7 +368,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q0 = (qfirst_block + i % nqb) * kQRows;
       const int b = i & 1;
       if (!warp_wait(&bar->dq_full[b], (i >> 1) & 1, p.status, kStatusTimeoutO)) break;
-      wmark(i, 0);
       tc_fence_after();
       float a[32], c2[32];
       ld32(tdQb(b) + lane_off, a);
@@ -400,7 +375,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->dq_free[b]);
-      wmark(i, 1);
       // Two 32-row halves, alternating between two 16 KB staging tiles: transpose a half into
       // [query][dim] and fold it into global dQ with one TMA reduce-add; the reduce of the
       // previous half overlaps the staging of this one.
@@ -416,8 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tile = sdq_addr + sb * kDqTileBytes;
         const float* src = h2 == 0 ? a : c2;
 #pragma unroll
-        if (!(p.mode & 16))
-          for (int c = 0; c < 32; ++c)
+        for (int c = 0; c < 32; ++c)
             st_shared_f32(tile + (c * kHeadDim + d) * 4, (q0 + 32 * h2 + c < L) ? src[c] * p.scale : 0.f);
         fence_async_shared();
         __syncwarp();
@@ -425,9 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok2 = true;
         if (issuer) {
           ok2 = mbar_wait(&bar->dqs_full[sb], (ph >> 1) & 1, p.status, kStatusTimeoutOther);
-          if (ok2 && (p.mode & 8)) {
-            if (ph >= 1) mbar_arrive(&bar->dqs_free[sb ^ 1]);  // experiment: no global dQ reduction
-          } else if (ok2) {
+          if (ok2) {
             tma_reduce_add_2d(&map_dq, smem + kSmemDQ + sb * kDqTileBytes, hq * kHeadDim, start + q0 + 32 * h2);
             bulk_commit_group();
             pending = true;
@@ -440,7 +411,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!__shfl_sync(0xffffffffu, ok2 ? 1 : 0, 0)) { issued_ok = false; break; }
       }
       if (!issued_ok) break;
-      wmark(i, 3);
     }
     if (issuer && pending) bulk_wait_group0();
   }
@@ -524,8 +494,7 @@ std::vector<at::Tensor> fmha_bwd_plan(at::Tensor cu_seqlens, at::Tensor prefix_l
 std::vector<at::Tensor> fmha_bwd(at::Tensor q_src, int64_t q_col, at::Tensor k_src, int64_t k_col, at::Tensor v_src,
                                  int64_t v_col, at::Tensor d_o, at::Tensor lse, at::Tensor delta, int64_t H,
                                  int64_t KV, bool is_causal, at::Tensor cu_seqlens, at::Tensor prefix_lens,
-                                 int64_t numseqs, at::Tensor kv_tiles, at::Tensor kv_ntiles,
-                                 c10::optional<at::Tensor> trace, int64_t trace_tile, int64_t mode) {
+                                 int64_t numseqs, at::Tensor kv_tiles, at::Tensor kv_ntiles) {
   for (const at::Tensor* t : {&q_src, &k_src, &v_src, &d_o}) {
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->stride(1) == 1,
                 "fmha_bwd: q/k/v/dO must be 2-D bf16 row-major CUDA tensors");
@@ -567,12 +536,6 @@ std::vector<at::Tensor> fmha_bwd(at::Tensor q_src, int64_t q_col, at::Tensor k_s
   prm.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
   prm.scale = 1.f / sqrtf((float)kHeadDim);
   prm.status = fmha_status_ptr(q_src.device());
-  if (trace.has_value()) {
-    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->numel() >= 64 * 14 * 4 && trace->is_cuda());
-    prm.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
-    prm.trace_tile = (int)trace_tile;
-  }
-  prm.mode = (int)mode;
   static bool attr_set[16] = {false};
   if (!attr_set[q_src.device().index()]) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(fmha_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));

@@ -14,7 +14,7 @@ _EXT = None
 _LOAD_ERROR: Exception | None = None
 
 # Kernel launches issued by one call of each binding (for launch accounting in benchmarks).
-_LAUNCHES_PER_CALL = {"fmha_status": 0, "fmha_plan": 1}
+_LAUNCHES_PER_CALL = {"fmha_status": 0, "fmha_plan": 1, "gemm_status": 0, "grouped_gemm_status": 0}
 
 
 class _CountingModule:
@@ -75,3 +75,27 @@ def kernels_enabled(t: torch.Tensor | None = None) -> bool:
     if os.environ.get("MIMIR_DISABLE_KERNELS", "0") == "1":
         return False
     return t is not None and t.is_cuda
+
+
+class KernelTimeout(RuntimeError):
+    """A bounded wait inside a hand-written kernel ran out: the outputs of that launch are not
+    valid.  Raised by :func:`check_kernel_status`."""
+
+
+def kernel_status(device: torch.device) -> dict:
+    """Read and clear the bounded-wait status words of every kernel family on ``device``
+    (attention, dense GEMM, grouped GEMM): 0 means every wait since the last read completed."""
+    if device.type != "cuda" or not available():
+        return {}
+    C = ext()
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    return {"attention": int(C.fmha_status(device)), "gemm": int(C.gemm_status(index)),
+            "grouped_gemm": int(C.grouped_gemm_status(index))}
+
+
+def check_kernel_status(device: torch.device, step=None) -> None:
+    """Raise :class:`KernelTimeout` if any kernel on ``device`` reported a timed-out wait."""
+    bad = {name: code for name, code in kernel_status(device).items() if code}
+    if bad:
+        where = "" if step is None else f" at or before step {step}"
+        raise KernelTimeout(f"Kernel wait timed out{where}: {bad} (status codes from csrc/common.cuh)")

@@ -7,8 +7,9 @@ compute dtype and gradients reduced in fp32 with SUM (divide factor 1 — the Ad
 optimizers are scale invariant).  HSDP uses a ``(replicate, shard)`` mesh whose shard
 degree must divide the world and fit in a node.
 
-NCCL does the collectives here; this is the measured baseline against which the fused
-peer-memory kernels in :mod:`mimir_b200.parallel.symm` are compared.
+NCCL does the collectives here; this is the baseline against which the replicated-weight
+engine (:mod:`mimir_b200.parallel.replicated`, one fused peer-memory update kernel per step)
+is compared.
 """
 from __future__ import annotations
 

@@ -293,6 +293,9 @@ def launch(config) -> None:
             maybe_empty_cache(state.step, device, config.empty_cache_interval)
 
             if state.step % config.log_interval == 0 or skipped or timing:
+                if device.type == "cuda":
+                    from mimir_b200.ops._ext import check_kernel_status
+                    check_kernel_status(device, state.step)  # a timed-out kernel wait invalidates the step
                 metrics = reduce_metrics(metrics, prefix="train/")
                 if rank == 0:
                     metrics.update(module_lr_metrics(config, lr, extra.get("bp_steps")))

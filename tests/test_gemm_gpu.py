@@ -158,7 +158,13 @@ def test_bounded_wait_times_out_and_the_next_launch_is_clean():
     x, w = _rand(16384, 512, seed=27), _rand(2048, 512, seed=28)  # 512 tiles: several per CTA pair
     ops.ext().gemm(x, False, w, False, wait_ns=2_000_000, inject=1)
     torch.cuda.synchronize()
-    assert G.status(0) in (3, 5, 6)
+    from mimir_b200.ops._ext import KernelTimeout, check_kernel_status, kernel_status
+    codes = kernel_status(torch.device("cuda", 0))  # reads and clears, like the training loop
+    assert codes["gemm"] in (3, 5, 6) and codes["attention"] == 0 and codes["grouped_gemm"] == 0
+    ops.ext().gemm(x, False, w, False, wait_ns=2_000_000, inject=1)
+    torch.cuda.synchronize()
+    with pytest.raises(KernelTimeout):
+        check_kernel_status(torch.device("cuda", 0), step=7)
     _close(G.mm_nt(x, w), x.float() @ w.float().t(), name="after the timeout")
     assert G.status(0) == 0
 
