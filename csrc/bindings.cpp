@@ -71,6 +71,10 @@ void grouped_gemm(at::Tensor a, std::vector<at::Tensor> bs, at::Tensor counts, a
 void grouped_wgrad(at::Tensor a, at::Tensor b, std::vector<int64_t> rows, std::vector<at::Tensor> grads);
 int64_t grouped_gemm_status(int64_t device);
 at::Tensor router_topk(at::Tensor scores, int64_t k, c10::optional<at::Tensor> load);
+// embedding.cu
+at::Tensor embed_fwd(at::Tensor ids, at::Tensor weight, double scale);
+void embed_bwd(at::Tensor dout, at::Tensor sorted_ids, at::Tensor order, at::Tensor grad, double scale);
+int64_t embed_status(int64_t device);
 // gemm.cu
 at::Tensor gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, c10::optional<at::Tensor> out,
                 c10::optional<at::Tensor> add, double alpha, double beta, int64_t bn, int64_t group_m,
@@ -123,5 +127,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_swiglu", &gemm_swiglu, py::arg("x"), py::arg("w_gu"), py::arg("group_m") = 8);
   m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd, py::arg("dy"), py::arg("w_down"), py::arg("gu"), py::arg("group_m") = 8);
   m.def("gemm_status", &gemm_status);
+  m.def("embed_fwd", &embed_fwd);
+  m.def("embed_bwd", &embed_bwd);
+  m.def("embed_status", &embed_status);
   m.def("fmha_bwd", &fmha_bwd);
 }

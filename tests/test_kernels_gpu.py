@@ -201,3 +201,25 @@ def test_fmha_backward(lengths, prefixes, H, KV, causal):
     for name, a, b in (("dq", q.grad, qr.grad), ("dk", k.grad, kr.grad), ("dv", v.grad, vr.grad)):
         scale = b[:total].abs().max().item() + 1e-6
         _close(a[:total] / scale, b[:total] / scale, 2e-2, 0.0, f"fmha bwd {name}")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_scaled_embedding_matches_torch(dtype):
+    """Fused gather + scale forward and the sorted, deterministic backward (repeated ids included)."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    V, d, T = 1000, 256, 4097
+    w = torch.randn(V, d, device="cuda", generator=g).to(dtype).requires_grad_(True)
+    ids = torch.randint(0, 50, (T,), device="cuda", generator=g, dtype=torch.int32)  # many repeats
+    out = ops.scaled_embedding(ids, w, 2.5)
+    wr = w.detach().float().requires_grad_(True)
+    ref = 2.5 * torch.nn.functional.embedding(ids.long(), wr)
+    _close(out, ref, 2e-2 if dtype == torch.bfloat16 else 1e-6, 1e-2, "embedding forward")
+    dy = torch.randn(T, d, device="cuda", generator=g).to(dtype)
+    out.backward(dy)
+    ref.backward(dy.float())
+    scale = wr.grad.abs().max().item()
+    _close(w.grad.float() / scale, wr.grad / scale, 1e-2 if dtype == torch.bfloat16 else 1e-5, 0.0, "embedding backward")
+    first = w.grad.clone()
+    w.grad = None
+    ops.scaled_embedding(ids, w, 2.5).backward(dy)
+    assert torch.equal(first, w.grad), "the backward is deterministic"
