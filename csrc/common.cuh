@@ -287,9 +287,12 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Arrive on an mbarrier given by its shared::cluster address (this CTA's or the peer's).
+// Arrive on an mbarrier given by its shared::cluster address (this CTA's or the peer's).  Release
+// semantics at CTA scope (the PTX default): what the waiter needs ordered are this thread's
+// tcgen05 reads (made complete by tcgen05.wait and ordered by tcgen05.fence::before_thread_sync),
+// not its global stores, so the arrive does not wait for those to become visible cluster-wide.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // 2-D tiled TMA load into this CTA's shared memory whose completion is counted on the barrier at

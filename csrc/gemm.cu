@@ -42,6 +42,7 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -77,16 +78,23 @@ struct GemmParams {
   int inject;
 };
 
-template <int BN>
+// Per-warp staging for the TMA-store epilogues: one [32 rows x 32 columns] bf16 chunk is 2 KB
+// (64-byte rows, 64-byte swizzle).  Plain stores double-buffer one output; the SwiGLU forward
+// stages three outputs (gate, up, product) and the SwiGLU backward two (d gate, d up).
+template <int BN, int kEpi>
 struct PairCfg {
   static constexpr int kBHalf = BN / 2;             // B rows staged per CTA
   static constexpr int kABytes = kBM * kBK * 2;     // 16 KB
   static constexpr int kBBytes = kBHalf * kBK * 2;  // 16 KB (BN 256) or 8 KB (BN 128)
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = 196608 / kStageBytes;  // 6 or 8 stages, 192 KB
-  static constexpr int kSmem = kStages * kStageBytes + 1024;
+  static constexpr int kStages = kEpi == 1 ? 5 : 196608 / kStageBytes;  // 5 (SwiGLU forward), 6 or 8
+  static constexpr int kChunkBytes = 32 * 32 * 2;
+  static constexpr int kStagingPerWarp = (kEpi == 1 ? 3 : 2) * kChunkBytes;
+  static constexpr int kStagingOffset = kStages * kStageBytes;  // 1024-aligned (stages are 8 KB multiples)
+  static constexpr int kSmem = kStagingOffset + kEpiWarps * kStagingPerWarp + 1024;
   static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
   static_assert(kStages <= 8, "barrier arrays hold 8 stages");
+  static_assert(kSmem + 1024 <= 232448, "dynamic + static shared memory must fit one SM");
 };
 
 struct PairBars {
@@ -145,6 +153,59 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v
   }
 }
 
+// ------------------------------------------------------------------------------ staged stores
+// Thread `lane` owns row `lane` of a [32 x 32] bf16 chunk: it writes its 64-byte row into the
+// warp's staging tile with the 64-byte TMA swizzle (16-byte piece j of row r at piece
+// j ^ ((r >> 1) & 3)), conflict-free; one lane then stores the tile with TMA.
+__device__ __forceinline__ void stage_row_bf16(uint32_t tile, int lane, const float (&v)[32]) {
+  const uint32_t row = tile + lane * 64;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    st_shared_v4(row + ((j ^ sw) << 4), pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                 pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t smem_src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
+// Both loads in flight before the single wait.
+__device__ __forceinline__ void tmem_ld32_pair(uint32_t a, uint32_t b, float (&va)[32], float (&vb)[32]) {
+  uint32_t ra[32], rb[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(ra[0]), "=r"(ra[1]), "=r"(ra[2]), "=r"(ra[3]), "=r"(ra[4]), "=r"(ra[5]), "=r"(ra[6]), "=r"(ra[7]),
+        "=r"(ra[8]), "=r"(ra[9]), "=r"(ra[10]), "=r"(ra[11]), "=r"(ra[12]), "=r"(ra[13]), "=r"(ra[14]), "=r"(ra[15]),
+        "=r"(ra[16]), "=r"(ra[17]), "=r"(ra[18]), "=r"(ra[19]), "=r"(ra[20]), "=r"(ra[21]), "=r"(ra[22]), "=r"(ra[23]),
+        "=r"(ra[24]), "=r"(ra[25]), "=r"(ra[26]), "=r"(ra[27]), "=r"(ra[28]), "=r"(ra[29]), "=r"(ra[30]), "=r"(ra[31]),
+        "=r"(rb[0]), "=r"(rb[1]), "=r"(rb[2]), "=r"(rb[3]), "=r"(rb[4]), "=r"(rb[5]), "=r"(rb[6]), "=r"(rb[7]),
+        "=r"(rb[8]), "=r"(rb[9]), "=r"(rb[10]), "=r"(rb[11]), "=r"(rb[12]), "=r"(rb[13]), "=r"(rb[14]), "=r"(rb[15]),
+        "=r"(rb[16]), "=r"(rb[17]), "=r"(rb[18]), "=r"(rb[19]), "=r"(rb[20]), "=r"(rb[21]), "=r"(rb[22]), "=r"(rb[23]),
+        "=r"(rb[24]), "=r"(rb[25]), "=r"(rb[26]), "=r"(rb[27]), "=r"(rb[28]), "=r"(rb[29]), "=r"(rb[30]), "=r"(rb[31])
+      : "r"(a), "r"(b)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    va[i] = __uint_as_float(ra[i]);
+    vb[i] = __uint_as_float(rb[i]);
+  }
+}
+
+// Staging tiles of the calling warp and a running count of the chunks it has staged (across
+// tiles), which decides when a tile may be reused.
+struct Staging {
+  uint32_t base;  // this warp's first tile
+  uint32_t count;
+};
+
 // ------------------------------------------------------------------------------ epilogues
 // One thread holds one accumulator row (its TMEM lane); `half` selects which half of the tile's
 // 32-column chunks this warp converts.  tcgen05.ld is warp-collective, so it stays outside the
@@ -190,31 +251,6 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, uint32_t tac
   }
 }
 
-// Accumulator columns [0, BN/2) are gate rows, [BN/2, BN) the matching up rows: writes gate|up
-// (saved for the backward) and h = silu(gate) * up formed from the bf16-rounded values.
-template <int BN>
-__device__ __forceinline__ void epilogue_swiglu_fwd(const GemmParams& p, uint32_t tacc, const RowOffsets& ro,
-                                                    bool valid, int h0, int half) {
-  constexpr int kHalf = BN / 2;
-  constexpr int kChunks = kHalf / 64;
-  __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(p.aux) + ro.aux;
-  __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out) + ro.out;
-#pragma unroll 1
-  for (int j = 0; j < kChunks; ++j) {
-    const int c = half * kChunks + j;
-    float g[32], u[32];
-    tmem_ld32(tacc + c * 32, g);
-    tmem_ld32(tacc + kHalf + c * 32, u);
-    if (!valid) continue;
-    const int col = h0 + c * 32;
-    store_bf16x32(gu + col, g);
-    store_bf16x32(gu + p.ffn + col, u);
-#pragma unroll
-    for (int e = 0; e < 32; ++e) g[e] = swiglu_silu(bf16_round(g[e])) * bf16_round(u[e]);
-    store_bf16x32(h + col, g);
-  }
-}
-
 __device__ __forceinline__ void load_raw4(const __nv_bfloat16* src, uint4 (&r)[4]) {
   const uint4* s = reinterpret_cast<const uint4*>(src);
 #pragma unroll
@@ -234,16 +270,76 @@ __device__ __forceinline__ void unpack_bf16x32(const uint4 (&r)[4], float (&v)[3
   }
 }
 
-// Accumulator = d(silu(gate) * up) for columns n0 .. n0 + BN of F; writes d[gate|up] from the
-// saved gate|up.  The gate|up operand of the next chunk is loaded while the current one is
-// converted (the first before the accumulator wait).  Returns false if that wait timed out.
+// Plain bf16 output through TMA stores (no addend): double-buffered 2 KB tiles per warp.
 template <int BN>
-__device__ __forceinline__ bool epilogue_swiglu_bwd(const GemmParams& p, uint64_t* acc_full, uint32_t parity,
-                                                    uint32_t tacc, const RowOffsets& ro, bool valid, int n0,
-                                                    int half) {
+__device__ __forceinline__ void epilogue_store_tma(const GemmParams& p, const CUtensorMap* map_out, uint32_t tacc,
+                                                   int lane, int row0, int bt, int n0, int half, Staging& st) {
   constexpr int kChunks = BN / 64;
+#pragma unroll 1
+  for (int j = 0; j < kChunks; ++j, ++st.count) {
+    const int c = half * kChunks + j;
+    float v[32];
+    tmem_ld32(tacc + c * 32, v);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] *= p.alpha;
+    const uint32_t tile = st.base + (st.count & 1) * (32 * 32 * 2);
+    if (st.count >= 2) {  // the store issued from this tile two chunks ago has read it
+      if (lane == 0) bulk_wait_group_read1();
+      __syncwarp();
+    }
+    stage_row_bf16(tile, lane, v);
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(map_out, tile, n0 + c * 32, row0, bt);
+      bulk_commit_group();
+    }
+  }
+}
+
+// SwiGLU forward through TMA stores: gate and up to the gate|up buffer, the product to `out`.
+template <int BN>
+__device__ __forceinline__ void epilogue_swiglu_fwd_tma(const GemmParams& p, const CUtensorMap* map_out,
+                                                        const CUtensorMap* map_aux, uint32_t tacc, int lane, int row0,
+                                                        int bt, int h0, int half, Staging& st) {
+  constexpr int kHalf = BN / 2;
+  constexpr int kChunks = kHalf / 64;
+  constexpr uint32_t kTile = 32 * 32 * 2;
+#pragma unroll 1
+  for (int j = 0; j < kChunks; ++j, ++st.count) {
+    const int c = half * kChunks + j;
+    float g[32], u[32];
+    tmem_ld32_pair(tacc + c * 32, tacc + kHalf + c * 32, g, u);
+    if (st.count >= 1) {  // the previous chunk's three stores have read their tiles
+      if (lane == 0) bulk_wait_group_read0();
+      __syncwarp();
+    }
+    stage_row_bf16(st.base, lane, g);
+    stage_row_bf16(st.base + kTile, lane, u);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) g[e] = swiglu_silu(bf16_round(g[e])) * bf16_round(u[e]);
+    stage_row_bf16(st.base + 2 * kTile, lane, g);
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+      const int col = h0 + c * 32;
+      tma_store_3d(map_aux, st.base, col, row0, bt);
+      tma_store_3d(map_aux, st.base + kTile, p.ffn + col, row0, bt);
+      tma_store_3d(map_out, st.base + 2 * kTile, col, row0, bt);
+      bulk_commit_group();
+    }
+  }
+}
+
+// SwiGLU backward through TMA stores of d gate / d up; gate|up read with prefetched 16-byte loads.
+template <int BN>
+__device__ __forceinline__ bool epilogue_swiglu_bwd_tma(const GemmParams& p, const CUtensorMap* map_out,
+                                                        uint64_t* acc_full, uint32_t parity, uint32_t tacc,
+                                                        const RowOffsets& ro, bool valid, int lane, int row0, int bt,
+                                                        int n0, int half, Staging& st) {
+  constexpr int kChunks = BN / 64;
+  constexpr uint32_t kTile = 32 * 32 * 2;
   const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(p.aux) + ro.aux;
-  __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(p.out) + ro.out;
   uint4 gn[4], un[4];
   int c = half * kChunks;
   if (valid && n0 + c * 32 < p.N) {
@@ -253,9 +349,8 @@ __device__ __forceinline__ bool epilogue_swiglu_bwd(const GemmParams& p, uint64_
   if (!warp_wait_ns(acc_full, parity, p.status, kStatusTimeoutS, p.wait_ns)) return false;
   tc_fence_after();
 #pragma unroll 1
-  for (int j = 0; j < kChunks; ++j, ++c) {
+  for (int j = 0; j < kChunks; ++j, ++c, ++st.count) {
     const int col = n0 + c * 32;
-    const bool live = valid && col < p.N;
     uint4 gc[4], uc[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -268,7 +363,6 @@ __device__ __forceinline__ bool epilogue_swiglu_bwd(const GemmParams& p, uint64_
     }
     float d[32];
     tmem_ld32(tacc + c * 32, d);
-    if (!live) continue;
     float g[32], u[32];
     unpack_bf16x32(gc, g);
     unpack_bf16x32(uc, u);
@@ -279,8 +373,19 @@ __device__ __forceinline__ bool epilogue_swiglu_bwd(const GemmParams& p, uint64_
       g[e] = dg;
       u[e] = du;
     }
-    store_bf16x32(dgu + col, g);
-    store_bf16x32(dgu + p.ffn + col, u);
+    if (st.count >= 1) {
+      if (lane == 0) bulk_wait_group_read0();
+      __syncwarp();
+    }
+    stage_row_bf16(st.base, lane, g);
+    stage_row_bf16(st.base + kTile, lane, u);
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0 && col < p.N) {
+      tma_store_3d(map_out, st.base, col, row0, bt);
+      tma_store_3d(map_out, st.base + kTile, p.ffn + col, row0, bt);
+      bulk_commit_group();
+    }
   }
   return true;
 }
@@ -288,8 +393,9 @@ __device__ __forceinline__ bool epilogue_swiglu_bwd(const GemmParams& p, uint64_
 template <int BN, bool kAMn, bool kBMn, int kEpi, bool kOutF32>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                     const __grid_constant__ CUtensorMap map_out, const __grid_constant__ CUtensorMap map_aux,
                      const GemmParams p) {
-  using CF = PairCfg<BN>;
+  using CF = PairCfg<BN, kEpi>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ PairBars bars;
@@ -419,29 +525,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int wq = warp & 3;
     const int half = (warp - 2) >> 2;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    // bf16 outputs without an addend leave through TMA stores from per-warp staging tiles.
+    const bool staged = !kOutF32 && (kEpi != kEpiStore || p.add == nullptr);
+    Staging st{smem_u32(smem + CF::kStagingOffset) + static_cast<uint32_t>((warp - 2) * CF::kStagingPerWarp), 0u};
     int i = 0;
     for (int t = cid; t < total; t += ncl, ++i) {
       const int buf = i & 1;
       int bt, mt, nt;
       tile_coords(t, p, bt, mt, nt);
-      const int row = mt * 2 * kBM + static_cast<int>(rank) * kBM + wq * 32 + lane;
+      const int row0 = mt * 2 * kBM + static_cast<int>(rank) * kBM + wq * 32;
+      const int row = row0 + lane;
       const bool valid = row < p.M;
       const RowOffsets ro = row_offsets(p, bt, row);
       const uint32_t tacc = tmem + lane_off + buf * BN;
       if (kEpi == kEpiSwiGLUBwd) {
         // Issues its first operand loads before waiting for the accumulator.
-        if (!epilogue_swiglu_bwd<BN>(p, &bars.acc_full[buf], (i >> 1) & 1, tacc, ro, valid, nt * BN, half)) break;
+        if (!epilogue_swiglu_bwd_tma<BN>(p, &map_out, &bars.acc_full[buf], (i >> 1) & 1, tacc, ro, valid, lane, row0,
+                                         bt, nt * BN, half, st))
+          break;
       } else {
         if (!warp_wait_ns(&bars.acc_full[buf], (i >> 1) & 1, p.status, kStatusTimeoutS, p.wait_ns)) break;
         tc_fence_after();
-        if (kEpi == kEpiStore) epilogue_store<BN, kOutF32>(p, tacc, ro, valid, nt * BN, half);
-        else epilogue_swiglu_fwd<BN>(p, tacc, ro, valid, nt * (BN / 2), half);
+        if (kEpi == kEpiSwiGLU) {
+          epilogue_swiglu_fwd_tma<BN>(p, &map_out, &map_aux, tacc, lane, row0, bt, nt * (BN / 2), half, st);
+        } else if (staged) {
+          epilogue_store_tma<BN>(p, &map_out, tacc, lane, row0, bt, nt * BN, half, st);
+        } else {
+          epilogue_store<BN, kOutF32>(p, tacc, ro, valid, nt * BN, half);
+        }
       }
       tc_fence_before();
       __syncwarp();
       const bool withhold = p.inject == 1 && i == 0 && leader && warp == 4;
       if (lane == 0 && !withhold) mbar_arrive_remote(mapa_shared(smem_u32(&bars.acc_empty[buf]), 0));
     }
+    if (staged && lane == 0) bulk_wait_group0();  // every staged store has landed before exit
+    __syncwarp();
     // Every MMA that writes this CTA's TMEM has completed before TMEM is freed (the last
     // accumulator was just read, so in a normal run this wait is short).
     if (warp == 2 && lane == 0) mbar_wait_ns(&bars.done, 0, p.status, kStatusTimeoutOther, p.wait_ns);
@@ -494,8 +613,9 @@ int resident_pairs(int device, const void* kernel, int smem) {
 }
 
 template <int BN, bool kAMn, bool kBMn, int kEpi, bool kOutF32>
-void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int device, cudaStream_t st) {
-  using CF = PairCfg<BN>;
+void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const CUtensorMap& mx,
+                 const GemmParams& p, int device, cudaStream_t st) {
+  using CF = PairCfg<BN, kEpi>;
   auto kernel = gemm_pair_kernel<BN, kAMn, kBMn, kEpi, kOutF32>;
   static bool attr[64] = {false};
   if (!attr[device]) {
@@ -504,7 +624,7 @@ void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams&
   }
   const int pairs = std::min(resident_pairs(device, reinterpret_cast<const void*>(kernel), CF::kSmem),
                              p.batch * p.tiles_m * p.tiles_n);
-  kernel<<<2 * pairs, kThreads, CF::kSmem, st>>>(ma, mb, p);
+  kernel<<<2 * pairs, kThreads, CF::kSmem, st>>>(ma, mb, mo, mx, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -526,17 +646,29 @@ CUtensorMap operand_map(const at::Tensor& t, int box_cols, int box_rows) {
 
 template <int BN>
 void dispatch_store(bool a_mn, bool b_mn, bool f32, const CUtensorMap& ma, const CUtensorMap& mb,
-                    const GemmParams& p, int dev, cudaStream_t st) {
+                    const CUtensorMap& mo, const GemmParams& p, int dev, cudaStream_t st) {
   const int code = (a_mn ? 4 : 0) | (b_mn ? 2 : 0) | (f32 ? 1 : 0);
   switch (code) {
-    case 0: launch_pair<BN, false, false, kEpiStore, false>(ma, mb, p, dev, st); break;
-    case 1: launch_pair<BN, false, false, kEpiStore, true>(ma, mb, p, dev, st); break;
-    case 2: launch_pair<BN, false, true, kEpiStore, false>(ma, mb, p, dev, st); break;
-    case 3: launch_pair<BN, false, true, kEpiStore, true>(ma, mb, p, dev, st); break;
-    case 6: launch_pair<BN, true, true, kEpiStore, false>(ma, mb, p, dev, st); break;
-    case 7: launch_pair<BN, true, true, kEpiStore, true>(ma, mb, p, dev, st); break;
+    case 0: launch_pair<BN, false, false, kEpiStore, false>(ma, mb, mo, mo, p, dev, st); break;
+    case 1: launch_pair<BN, false, false, kEpiStore, true>(ma, mb, mo, mo, p, dev, st); break;
+    case 2: launch_pair<BN, false, true, kEpiStore, false>(ma, mb, mo, mo, p, dev, st); break;
+    case 3: launch_pair<BN, false, true, kEpiStore, true>(ma, mb, mo, mo, p, dev, st); break;
+    case 6: launch_pair<BN, true, true, kEpiStore, false>(ma, mb, mo, mo, p, dev, st); break;
+    case 7: launch_pair<BN, true, true, kEpiStore, true>(ma, mb, mo, mo, p, dev, st); break;
     default: TORCH_CHECK(false, "unsupported operand layout: an M-major A needs an N-major B");
   }
+}
+
+// TMA map of a bf16 output written in [32 rows x 32 columns] chunks (64-byte swizzle); a map
+// the kernel never uses (fp32 output, or an output read back as an addend) is left zero.
+CUtensorMap output_map(const at::Tensor& t) {
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  if (t.scalar_type() != at::kBFloat16) return map;
+  const int64_t rows = t.size(-2), cols = t.size(-1), ld = t.stride(-2);
+  const int64_t batch = t.dim() == 3 ? t.size(0) : 1;
+  const int64_t bstride = t.dim() == 3 ? t.stride(0) : rows * ld;
+  return make_tmap_bf16_3d(t.data_ptr(), batch, rows, cols, ld, bstride, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 GemmParams base_params(int M, int N, int K, int BN, int64_t group_m, int64_t wait_ns, int64_t inject, int device) {
@@ -613,9 +745,10 @@ at::Tensor gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, c10::optional<
   }
   const CUtensorMap ma = a_mn ? operand_map(a, 64, kBK) : operand_map(a, kBK, kBM);
   const CUtensorMap mb = b_mn ? operand_map(b, 64, kBK) : operand_map(b, kBK, BN / 2);
+  const CUtensorMap mo = output_map(o);
   auto st = at::cuda::getCurrentCUDAStream();
-  if (BN == 256) dispatch_store<256>(a_mn, b_mn, f32, ma, mb, p, dev, st);
-  else dispatch_store<128>(a_mn, b_mn, f32, ma, mb, p, dev, st);
+  if (BN == 256) dispatch_store<256>(a_mn, b_mn, f32, ma, mb, mo, p, dev, st);
+  else dispatch_store<128>(a_mn, b_mn, f32, ma, mb, mo, p, dev, st);
   return o;
 }
 
@@ -643,7 +776,8 @@ std::vector<at::Tensor> gemm_swiglu(at::Tensor x, at::Tensor w_gu, int64_t group
   p.ffn = static_cast<int>(F);
   const CUtensorMap ma = operand_map(x, kBK, kBM);
   const CUtensorMap mb = operand_map(w_gu, kBK, BN / 2);
-  launch_pair<256, false, false, kEpiSwiGLU, false>(ma, mb, p, dev, at::cuda::getCurrentCUDAStream());
+  launch_pair<256, false, false, kEpiSwiGLU, false>(ma, mb, output_map(h), output_map(gu), p, dev,
+                                                    at::cuda::getCurrentCUDAStream());
   return {h, gu};
 }
 
@@ -670,7 +804,8 @@ at::Tensor gemm_swiglu_bwd(at::Tensor dy, at::Tensor w_down, at::Tensor gu, int6
   p.ffn = static_cast<int>(F);
   const CUtensorMap ma = operand_map(dy, kBK, kBM);
   const CUtensorMap mb = operand_map(w_down, 64, kBK);
-  launch_pair<256, false, true, kEpiSwiGLUBwd, false>(ma, mb, p, dev, at::cuda::getCurrentCUDAStream());
+  const CUtensorMap mo = output_map(dgu);
+  launch_pair<256, false, true, kEpiSwiGLUBwd, false>(ma, mb, mo, mo, p, dev, at::cuda::getCurrentCUDAStream());
   return dgu;
 }
 

@@ -56,7 +56,8 @@ inline CUtensorMap make_tmap_bf16_2d(const void* base, int64_t rows, int64_t col
 // elements between consecutive matrices; box {box_cols, box_rows, 1}.  A single matrix is the
 // batch-of-one case (z coordinate 0).
 inline CUtensorMap make_tmap_bf16_3d(const void* base, int64_t batch, int64_t rows, int64_t cols, int64_t ld,
-                                     int64_t batch_stride, int box_cols, int box_rows) {
+                                     int64_t batch_stride, int box_cols, int box_rows,
+                                     CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
   TORCH_CHECK((ld * 2) % 16 == 0 && (batch_stride * 2) % 16 == 0, "TMA strides must be multiples of 16 bytes");
   bind_device_context();
@@ -66,7 +67,7 @@ inline CUtensorMap make_tmap_bf16_3d(const void* base, int64_t batch, int64_t ro
   cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
-                                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3-D) failed with code ", (int)r);
   return map;
