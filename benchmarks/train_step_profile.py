@@ -1,10 +1,14 @@
 """Where one training step of a bench configuration spends its GPU time (torch.profiler, 1 GPU).
 
     python benchmarks/train_step_profile.py [--config dense|moe] [--optimizer adam_atan2|muon] [--rows 25]
+        [--overlap-report]
 
 Builds the same model, data and engine as ``bench.py`` (our arm), runs three warm-up steps and
 profiles one more, then prints the kernels (and CPU-side ops) ranked by total CUDA time.  The
 profiled step is slower than a timed one (profiler overhead); compare shares, not absolutes.
+``--overlap-report`` adds one JSON line on the fused optimizer update: its kernels' device time,
+the part of it during which some other kernel (the backward) was also running, and when the
+last update kernel ended relative to the last other kernel.
 """
 from __future__ import annotations
 
@@ -23,6 +27,7 @@ def main():
     ap.add_argument("--config", choices=["dense", "moe"], default="dense")
     ap.add_argument("--optimizer", choices=["adam_atan2", "muon"], default="adam_atan2")
     ap.add_argument("--rows", type=int, default=25)
+    ap.add_argument("--overlap-report", action="store_true")
     args = ap.parse_args()
     import bench
     bench.CONFIG["name"] = args.config
@@ -62,8 +67,33 @@ def main():
     print(table.table(sort_by="self_cuda_time_total", row_limit=args.rows))
     total = sum(getattr(e, "self_device_time_total", getattr(e, "self_cuda_time_total", 0)) for e in table)
     print(f"total self CUDA time of the step: {total / 1e3:.1f} ms")
+    if args.overlap_report:
+        print(overlap_report(prof))
     import torch.distributed as dist
     dist.destroy_process_group()
+
+
+def overlap_report(prof) -> str:
+    """JSON line: device time of the update kernels and the part of it shared with other kernels."""
+    import json
+    from torch.autograd import DeviceType
+    kernels = [(e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+               if e.device_type == DeviceType.CUDA and e.time_range.end > e.time_range.start]
+    update = sorted((a, b) for a, b, n in kernels if "dp_update" in n)
+    others = sorted((a, b) for a, b, n in kernels if "dp_update" not in n)
+    merged = []
+    for a, b in others:  # union of the other kernels' busy intervals
+        if merged and a <= merged[-1][1]:
+            merged[-1][1] = max(merged[-1][1], b)
+        else:
+            merged.append([a, b])
+    shared = sum(max(0.0, min(b, mb) - max(a, ma)) for a, b in update for ma, mb in merged)
+    total = sum(b - a for a, b in update)
+    return json.dumps({"update_kernels": len(update), "update_ms": round(total / 1e3, 3),
+                       "update_ms_concurrent_with_other_kernels": round(shared / 1e3, 3),
+                       "last_update_end_minus_last_other_end_ms":
+                           round(((update[-1][1] if update else 0) - (others[-1][1] if others else 0)) / 1e3, 3),
+                       "other_kernels_busy_ms": round(sum(b - a for a, b in merged) / 1e3, 3)})
 
 
 if __name__ == "__main__":

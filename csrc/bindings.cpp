@@ -24,8 +24,10 @@ void adam_atan2_multi(std::vector<at::Tensor> params, std::vector<at::Tensor> gr
 // ngram.cu
 at::Tensor ngram_fwd(at::Tensor ids, at::Tensor pos, std::vector<at::Tensor> tables, std::vector<int64_t> orders,
                      int64_t heads, int64_t buckets, at::ScalarType dtype);
-void ngram_bwd(at::Tensor dout, at::Tensor ids, at::Tensor pos, std::vector<at::Tensor> grads,
-               std::vector<int64_t> orders, int64_t heads, int64_t buckets);
+at::Tensor ngram_keys(at::Tensor ids, at::Tensor pos, std::vector<int64_t> orders, int64_t heads, int64_t buckets,
+                      int64_t width);
+void ngram_bwd(at::Tensor dout, at::Tensor ids, at::Tensor pos, at::Tensor sorted_keys, at::Tensor order,
+               std::vector<at::Tensor> grads, std::vector<int64_t> orders, int64_t heads, int64_t buckets);
 // fmha_fwd.cu
 std::vector<at::Tensor> fmha_plan(at::Tensor cu_seqlens, at::Tensor prefix_lens, int64_t numseqs, int64_t total_tokens,
                                   bool is_causal);
@@ -55,18 +57,20 @@ int64_t dp_chunk_elements();
 void dp_step(std::vector<int64_t> peer_grads, std::vector<int64_t> peer_weights, at::Tensor segs, int64_t nblocks,
              at::Tensor master, c10::optional<at::Tensor> exp_avg, at::Tensor exp_avg_sq, c10::optional<at::Tensor> ema,
              c10::optional<at::Tensor> reduced, c10::optional<at::Tensor> grad_scale, double b1, double b2,
-             double ema_decay, std::vector<int64_t> peer_work, int64_t rank);
+             double ema_decay, std::vector<int64_t> peer_work, int64_t rank, bool lean);
 void dp_reduce(std::vector<int64_t> peer_grads, at::Tensor segs, int64_t nblocks, at::Tensor reduced_out,
                at::Tensor sumsq_out, int64_t rank);
 std::vector<at::Tensor> ipc_alloc(int64_t nbytes, int64_t device);
 int64_t ipc_open(at::Tensor handle_bytes, int64_t device);
 void ipc_close(int64_t ptr, int64_t device);
 bool peer_access_possible(int64_t device, int64_t peer);
-void moe_dispatch(at::Tensor x, at::Tensor rows, at::Tensor dst, std::vector<int64_t> recv, int64_t k);
+void moe_dispatch(at::Tensor x, at::Tensor rows, at::Tensor dst, std::vector<int64_t> recv, int64_t k,
+                  int64_t capacity);
 at::Tensor moe_combine(std::vector<int64_t> y, at::Tensor rows, at::Tensor dst, c10::optional<at::Tensor> w,
-                       int64_t T, int64_t k, int64_t d, c10::optional<at::Tensor> ys);
+                       int64_t T, int64_t k, int64_t d, c10::optional<at::Tensor> ys, int64_t capacity);
 at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::Tensor dst, at::Tensor ys,
-                           std::vector<int64_t> dy, int64_t k);
+                           std::vector<int64_t> dy, int64_t k, int64_t capacity);
+int64_t moe_route_status(int64_t device);
 void grouped_gemm(at::Tensor a, std::vector<at::Tensor> bs, at::Tensor counts, at::Tensor out, bool b_kn);
 void grouped_wgrad(at::Tensor a, at::Tensor b, std::vector<int64_t> rows, std::vector<at::Tensor> grads);
 int64_t grouped_gemm_status(int64_t device);
@@ -99,6 +103,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_bwd_inplace", &ce_bwd_inplace);
   m.def("adam_atan2_multi", &adam_atan2_multi);
   m.def("ngram_fwd", &ngram_fwd);
+  m.def("ngram_keys", &ngram_keys);
   m.def("ngram_bwd", &ngram_bwd);
   m.def("fmha_plan", &fmha_plan);
   m.def("fmha_fwd", &fmha_fwd);
@@ -117,6 +122,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_combine", &moe_combine);
   m.def("moe_combine_bwd", &moe_combine_bwd);
+  m.def("moe_route_status", &moe_route_status);
   m.def("grouped_gemm", &grouped_gemm);
   m.def("grouped_wgrad", &grouped_wgrad);
   m.def("grouped_gemm_status", &grouped_gemm_status);

@@ -43,6 +43,7 @@
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kLeanThreads = 128;
 constexpr int kVec = 8;                              // bf16 elements per 16-byte access
 constexpr int kIters = 4;
 constexpr int kChunk = kThreads * kVec * kIters;     // 8192 elements per CTA
@@ -219,9 +220,16 @@ __device__ __forceinline__ void update8(const float (&gin)[8], float scale, int6
 // Persistent: CTA b handles chunks b, b + gridDim.x, ...  Within a chunk each thread walks its
 // 8-element groups with the next group's gradient loads (peer loads over NVLink) issued before
 // the current group is updated, so NVLink latency overlaps the HBM traffic of the update.
-template <bool kFromPeers>
-__global__ void __launch_bounds__(kThreads, 2) dp_update_kernel(const __grid_constant__ Peers peers,
-                                                                   const StepArgs a, int64_t nchunks) {
+//
+// Lean variant (kT = kLeanThreads): for an update that runs beside the backward's kernels.  128
+// threads and at most 80 registers each, so a CTA fits in what a dense-GEMM CTA leaves of every
+// SM sub-partition's register file; no gradient prefetch; launched with one CTA per chunk, so no
+// CTA holds an SM longer than one chunk (a waiting attention or fused-SwiGLU CTA, which leaves no
+// room beside it, is not delayed by more than that).
+template <bool kFromPeers, int kT>
+__global__ void __launch_bounds__(kT, kT == kThreads ? 2 : 6) dp_update_kernel(const __grid_constant__ Peers peers,
+                                                                                 const StepArgs a, int64_t nchunks) {
+  constexpr bool kPrefetch = kT == kThreads;
   const float scale = a.grad_scale != nullptr ? *a.grad_scale : 1.f;
   for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
     const Segment s = a.segs[find_segment(a.segs, a.nsegs, chunk)];
@@ -234,15 +242,27 @@ __global__ void __launch_bounds__(kThreads, 2) dp_update_kernel(const __grid_con
     const bool needs_grad = kind != kMuonApply;
     if (s.vec) {
       int64_t i = start + int64_t(threadIdx.x) * kVec;
-      uint4 raw[kMaxRanks];
-      if (kFromPeers && needs_grad && i < end) load_grads(peers, r0, nr, s.flat + i, raw);
-      for (; i < end; i += int64_t(kThreads) * kVec) {
+      uint4 raw[kPrefetch ? kMaxRanks : 1];
+      if constexpr (kPrefetch)
+        if (kFromPeers && needs_grad && i < end) load_grads(peers, r0, nr, s.flat + i, raw);
+      for (; i < end; i += int64_t(kT) * kVec) {
         float g[8];
         if (!needs_grad) {
-        } else if (kFromPeers) {
+        } else if constexpr (kFromPeers && kPrefetch) {
           sum_grads(raw, nr, g);
-          const int64_t nxt = i + int64_t(kThreads) * kVec;
+          const int64_t nxt = i + int64_t(kT) * kVec;
           if (nxt < end) load_grads(peers, r0, nr, s.flat + nxt, raw);
+        } else if constexpr (kFromPeers) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) g[e] = 0.f;
+          for (int k = 0; k < nr; ++k) {
+            float f[8];
+            unpack8(*reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peers.grad[r0 + k]) +
+                                                    s.flat + i),
+                    f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) g[e] += f[e];
+          }
         } else {
           ld8(a.reduced + s.shard + i, g);
         }
@@ -275,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 2) dp_update_kernel(const __grid_con
             *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers.weight[r0 + k]) + s.flat + i) = packed;
       }
     } else {
-      for (int64_t i = start + threadIdx.x; i < end; i += kThreads) {
+      for (int64_t i = start + threadIdx.x; i < end; i += kT) {
         const int64_t sh = s.shard + i;
         float* e = a.ema != nullptr ? a.ema + sh : nullptr;
         float w = a.master[sh];
@@ -399,7 +419,7 @@ int64_t dp_chunk_elements() { return kChunk; }
 void dp_step(std::vector<int64_t> peer_grads, std::vector<int64_t> peer_weights, at::Tensor segs, int64_t nblocks,
              at::Tensor master, c10::optional<at::Tensor> exp_avg, at::Tensor exp_avg_sq, c10::optional<at::Tensor> ema,
              c10::optional<at::Tensor> reduced, c10::optional<at::Tensor> grad_scale, double b1, double b2,
-             double ema_decay, std::vector<int64_t> peer_work, int64_t rank) {
+             double ema_decay, std::vector<int64_t> peer_work, int64_t rank, bool lean) {
   const c10::cuda::CUDAGuard guard(master.device());
   const Peers peers = make_peers(peer_grads, peer_weights, peer_work);
   StepArgs a = make_args(segs, peer_grads.size(), master, exp_avg, exp_avg_sq, ema, grad_scale, b1, b2, ema_decay);
@@ -407,12 +427,14 @@ void dp_step(std::vector<int64_t> peer_grads, std::vector<int64_t> peer_weights,
   a.rank = static_cast<int>(rank);
   if (nblocks == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  const unsigned grid = persistent_grid(nblocks, master.device().index());
-  if (reduced) {
-    a.reduced = reduced->data_ptr<float>();
-    dp_update_kernel<false><<<grid, kThreads, 0, stream>>>(peers, a, nblocks);
+  if (reduced) a.reduced = reduced->data_ptr<float>();
+  if (lean) {  // one short CTA per chunk, beside the backward's kernels
+    TORCH_CHECK(!reduced && nblocks < (int64_t(1) << 31), "the lean update reads the peers' gradients");
+    dp_update_kernel<true, kLeanThreads><<<static_cast<unsigned>(nblocks), kLeanThreads, 0, stream>>>(peers, a, nblocks);
   } else {
-    dp_update_kernel<true><<<grid, kThreads, 0, stream>>>(peers, a, nblocks);
+    const unsigned grid = persistent_grid(nblocks, master.device().index());
+    if (reduced) dp_update_kernel<false, kThreads><<<grid, kThreads, 0, stream>>>(peers, a, nblocks);
+    else dp_update_kernel<true, kThreads><<<grid, kThreads, 0, stream>>>(peers, a, nblocks);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -87,7 +87,9 @@ struct PairCfg {
   static constexpr int kABytes = kBM * kBK * 2;     // 16 KB
   static constexpr int kBBytes = kBHalf * kBK * 2;  // 16 KB (BN 256) or 8 KB (BN 128)
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = kEpi == 1 ? 5 : 196608 / kStageBytes;  // 5 (SwiGLU forward), 6 or 8
+  // A 160 KB ring (5 stages at BN 256, 6 at BN 128) keeps the tensor pipe fed and leaves room on
+  // the SM for a CTA of another kernel (the optimizer update overlapping the backward).
+  static constexpr int kStages = 163840 / kStageBytes;
   static constexpr int kChunkBytes = 32 * 32 * 2;
   static constexpr int kStagingPerWarp = (kEpi == 1 ? 3 : 2) * kChunkBytes;
   static constexpr int kStagingOffset = kStages * kStageBytes;  // 1024-aligned (stages are 8 KB multiples)

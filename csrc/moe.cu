@@ -35,7 +35,18 @@ constexpr int kMaxTopK = 8;
 
 struct PeerRows {
   uint64_t ptr[kMaxRanks];  // every rank's buffer (bf16 [rows, d])
+  int nranks;               // valid destination ranks
+  int64_t capacity;         // valid rows per rank's buffer
+  int* bad;                 // set to 1 when a route names a rank or row outside these bounds
 };
+
+// A route (rank q, row r) outside the buffers is skipped (no peer access; zero contribution)
+// and reported through the status word, which the host reads with the other kernel statuses.
+__device__ __forceinline__ bool route_ok(const PeerRows& p, int q, int r) {
+  const bool ok = q >= 0 && q < p.nranks && r >= 0 && r < p.capacity;
+  if (!ok) atomicExch(p.bad, 1);
+  return ok;
+}
 
 __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -74,8 +85,9 @@ __global__ void __launch_bounds__(kWarps * 32) moe_dispatch_kernel(const __nv_bf
   if (t >= T) return;
   const int lane = threadIdx.x & 31;
   int r[K], q[K];
+  bool ok[K];
 #pragma unroll
-  for (int j = 0; j < K; ++j) r[j] = rows[t * K + j], q[j] = dst[t * K + j];
+  for (int j = 0; j < K; ++j) r[j] = rows[t * K + j], q[j] = dst[t * K + j], ok[j] = route_ok(recv, q[j], r[j]);
   const uint4* src = reinterpret_cast<const uint4*>(x + t * d);
   const int64_t nv = d / 8;
   for (int64_t v0 = lane; v0 < nv; v0 += 32 * kUnroll) {
@@ -87,7 +99,8 @@ __global__ void __launch_bounds__(kWarps * 32) moe_dispatch_kernel(const __nv_bf
     for (int u = 0; u < kUnroll; ++u) {
       if (v0 + 32 * u < nv) {
 #pragma unroll
-        for (int j = 0; j < K; ++j) row_ptr_mut(recv, q[j], r[j], d)[v0 + 32 * u] = val[u];
+        for (int j = 0; j < K; ++j)
+          if (ok[j]) row_ptr_mut(recv, q[j], r[j], d)[v0 + 32 * u] = val[u];
       }
     }
   }
@@ -108,9 +121,11 @@ __global__ void __launch_bounds__(kWarps * 32) moe_combine_kernel(const __grid_c
   const int lane = threadIdx.x & 31;
   int r[K], q[K];
   float wt[K];
+  bool ok[K];
 #pragma unroll
   for (int j = 0; j < K; ++j)
-    r[j] = rows[t * K + j], q[j] = dst[t * K + j], wt[j] = w != nullptr ? w[t * K + j] : 1.f;
+    r[j] = rows[t * K + j], q[j] = dst[t * K + j], wt[j] = w != nullptr ? w[t * K + j] : 1.f,
+    ok[j] = route_ok(y, q[j], r[j]);
   uint4* o = reinterpret_cast<uint4*>(out + t * d);
   const int64_t nv = d / 8;
   for (int64_t v0 = lane; v0 < nv; v0 += 32 * kUnroll) {
@@ -119,7 +134,7 @@ __global__ void __launch_bounds__(kWarps * 32) moe_combine_kernel(const __grid_c
     for (int u = 0; u < kUnroll; ++u)
       if (v0 + 32 * u < nv) {
 #pragma unroll
-        for (int j = 0; j < K; ++j) raw[u][j] = row_ptr(y, q[j], r[j], d)[v0 + 32 * u];
+        for (int j = 0; j < K; ++j) raw[u][j] = ok[j] ? row_ptr(y, q[j], r[j], d)[v0 + 32 * u] : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
@@ -153,8 +168,10 @@ __global__ void __launch_bounds__(kWarps * 32) moe_combine_bwd_kernel(const __nv
   const int lane = threadIdx.x & 31;
   int r[K], q[K];
   float wt[K], dot[K];
+  bool ok[K];
 #pragma unroll
-  for (int j = 0; j < K; ++j) r[j] = rows[t * K + j], q[j] = dst[t * K + j], wt[j] = w[t * K + j], dot[j] = 0.f;
+  for (int j = 0; j < K; ++j)
+    r[j] = rows[t * K + j], q[j] = dst[t * K + j], wt[j] = w[t * K + j], dot[j] = 0.f, ok[j] = route_ok(dy, q[j], r[j]);
   const uint4* g = reinterpret_cast<const uint4*>(dout + t * d);
   const int64_t nv = d / 8;
   for (int64_t v0 = lane; v0 < nv; v0 += 32 * kUnroll) {
@@ -181,7 +198,7 @@ __global__ void __launch_bounds__(kWarps * 32) moe_combine_bwd_kernel(const __nv
           dot[j] += gf[e] * yf[e];
           sc[e] = wt[j] * gf[e];
         }
-        row_ptr_mut(dy, q[j], r[j], d)[v] = pack8(sc);
+        if (ok[j]) row_ptr_mut(dy, q[j], r[j], d)[v] = pack8(sc);
       }
     }
   }
@@ -211,13 +228,24 @@ void with_topk(int64_t k, F&& launch) {
   }
 }
 
-PeerRows make_rows(const std::vector<int64_t>& ptrs) {
+int* route_flag(const at::Device& dev) {
+  static at::Tensor flags[64];
+  const int i = dev.index();
+  if (!flags[i].defined()) flags[i] = at::zeros({1}, at::TensorOptions().device(dev).dtype(at::kInt));
+  return flags[i].data_ptr<int>();
+}
+
+PeerRows make_rows(const std::vector<int64_t>& ptrs, int64_t capacity, const at::Device& dev) {
   TORCH_CHECK(ptrs.size() >= 1 && ptrs.size() <= kMaxRanks, "expert parallelism supports 1..", kMaxRanks, " ranks");
+  TORCH_CHECK(capacity >= 0, "row capacity must be non-negative");
   PeerRows p{};
   for (size_t k = 0; k < ptrs.size(); ++k) {
-    TORCH_CHECK(ptrs[k] % 16 == 0, "peer row buffers must be 16-byte aligned");
+    TORCH_CHECK(ptrs[k] % 16 == 0 && ptrs[k] != 0, "peer row buffers must be non-null and 16-byte aligned");
     p.ptr[k] = static_cast<uint64_t>(ptrs[k]);
   }
+  p.nranks = static_cast<int>(ptrs.size());
+  p.capacity = capacity;
+  p.bad = route_flag(dev);
   return p;
 }
 
@@ -232,7 +260,8 @@ unsigned blocks_for(int64_t T) { return static_cast<unsigned>((T + kWarps - 1) /
 
 }  // namespace
 
-void moe_dispatch(at::Tensor x, at::Tensor rows, at::Tensor dst, std::vector<int64_t> recv, int64_t k) {
+void moe_dispatch(at::Tensor x, at::Tensor rows, at::Tensor dst, std::vector<int64_t> recv, int64_t k,
+                  int64_t capacity) {
   TORCH_CHECK(x.is_cuda() && x.dtype() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "x: bf16 [T, d]");
   const int64_t T = x.size(0), d = x.size(1);
   TORCH_CHECK(d % 8 == 0, "hidden size must be a multiple of 8");
@@ -242,13 +271,13 @@ void moe_dispatch(at::Tensor x, at::Tensor rows, at::Tensor dst, std::vector<int
   with_topk(k, [&](auto kk) {
     moe_dispatch_kernel<decltype(kk)::value><<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), rows.data_ptr<int32_t>(), dst.data_ptr<int32_t>(),
-        make_rows(recv), T, d);
+        make_rows(recv, capacity, x.device()), T, d);
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 at::Tensor moe_combine(std::vector<int64_t> y, at::Tensor rows, at::Tensor dst, c10::optional<at::Tensor> w,
-                       int64_t T, int64_t k, int64_t d, c10::optional<at::Tensor> ys) {
+                       int64_t T, int64_t k, int64_t d, c10::optional<at::Tensor> ys, int64_t capacity) {
   TORCH_CHECK(d % 8 == 0, "hidden size must be a multiple of 8");
   check_routes(rows, dst, T, k);
   if (w) TORCH_CHECK(w->is_cuda() && w->dtype() == at::kFloat && w->is_contiguous() && w->numel() == T * k,
@@ -260,7 +289,8 @@ at::Tensor moe_combine(std::vector<int64_t> y, at::Tensor rows, at::Tensor dst, 
   if (T == 0) return out;
   with_topk(k, [&](auto kk) {
     moe_combine_kernel<decltype(kk)::value><<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
-        make_rows(y), rows.data_ptr<int32_t>(), dst.data_ptr<int32_t>(), w ? w->data_ptr<float>() : nullptr,
+        make_rows(y, capacity, rows.device()), rows.data_ptr<int32_t>(), dst.data_ptr<int32_t>(),
+        w ? w->data_ptr<float>() : nullptr,
         reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
         ys ? reinterpret_cast<__nv_bfloat16*>(ys->data_ptr()) : nullptr, T, d);
   });
@@ -269,7 +299,7 @@ at::Tensor moe_combine(std::vector<int64_t> y, at::Tensor rows, at::Tensor dst, 
 }
 
 at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::Tensor dst, at::Tensor ys,
-                           std::vector<int64_t> dy, int64_t k) {
+                           std::vector<int64_t> dy, int64_t k, int64_t capacity) {
   TORCH_CHECK(dout.is_cuda() && dout.dtype() == at::kBFloat16 && dout.is_contiguous() && dout.dim() == 2,
               "dout: bf16 [T, d]");
   const int64_t T = dout.size(0), d = dout.size(1);
@@ -285,9 +315,19 @@ at::Tensor moe_combine_bwd(at::Tensor dout, at::Tensor w, at::Tensor rows, at::T
   with_topk(k, [&](auto kk) {
     moe_combine_bwd_kernel<decltype(kk)::value><<<blocks_for(T), kWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), w.data_ptr<float>(), rows.data_ptr<int32_t>(),
-        dst.data_ptr<int32_t>(), reinterpret_cast<const __nv_bfloat16*>(ys.data_ptr()), make_rows(dy),
+        dst.data_ptr<int32_t>(), reinterpret_cast<const __nv_bfloat16*>(ys.data_ptr()),
+        make_rows(dy, capacity, dout.device()),
         dw.data_ptr<float>(), T, d);
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dw;
+}
+
+// 1 if an exchange kernel met a route outside its buffers since the last read (that slot was skipped).
+int64_t moe_route_status(int64_t device) {
+  int* flag = route_flag(at::Device(at::kCUDA, static_cast<c10::DeviceIndex>(device)));
+  int host = 0;
+  C10_CUDA_CHECK(cudaMemcpy(&host, flag, sizeof(int), cudaMemcpyDeviceToHost));
+  if (host) C10_CUDA_CHECK(cudaMemset(flag, 0, sizeof(int)));
+  return host;
 }

@@ -1,7 +1,7 @@
 // Hashed n-gram memory: for each token, order and head, recompute the polynomial hash of
 // the previous `order` tokens, check that they are consecutive positions of one packed
-// sequence, and sum the gathered table rows (forward); scatter-add gradients into fp32
-// table gradients (backward).  One warp per token.
+// sequence, and sum the gathered table rows (forward, one warp per token); the backward sums
+// each hashed row's gradient over a sorted key list (below).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -71,18 +71,48 @@ __global__ void ngram_fwd_kernel(NGramArgs a, TO* __restrict__ out) {
   }
 }
 
-template <typename TO>
-__global__ void ngram_bwd_kernel(NGramArgs a, const TO* __restrict__ dout) {
-  const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+// Backward, deterministic and without atomics.  Pass 1 gives every (token, order, head) a key:
+// (order index * heads + head) * buckets + hash, or kNoKey when the n-gram is not valid.  The
+// caller sorts the keys stably; pass 2 runs one warp per sorted position: the warp at the head
+// of a run of equal keys sums that run's dout slices in fp32, in token order, and adds the sum
+// to the gradient row once (read-modify-write in the gradient's dtype).  Only hashed rows are
+// touched, so the gradient can be the optimizer's accumulation buffer itself.
+constexpr int64_t kNoKey = INT64_MAX;
+
+__global__ void ngram_keys_kernel(NGramArgs a, int64_t* __restrict__ keys) {
+  const int per = a.norders * a.heads;
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= a.S * per) return;
+  const int64_t t = i / per;
+  const int j = static_cast<int>(i % per);
+  int64_t hv;
+  keys[i] = ngram_hash(a, t, a.orders[j / a.heads], j % a.heads, hv) ? int64_t(j) * a.buckets + hv : kNoKey;
+}
+
+__device__ __forceinline__ float load_f(const float* p) { return *p; }
+__device__ __forceinline__ float load_f(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ void store_f(float* p, float v) { *p = v; }
+__device__ __forceinline__ void store_f(__nv_bfloat16* p, float v) { *p = __float2bfloat16(v); }
+
+template <typename TD, typename TG>
+__global__ void ngram_bwd_kernel(NGramArgs a, const TD* __restrict__ dout, const int64_t* __restrict__ keys,
+                                 const int64_t* __restrict__ order, int64_t n) {
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (t >= a.S) return;
+  const int per = a.norders * a.heads;
   const int hidden = a.width * a.heads;
-  for (int oi = 0; oi < a.norders; ++oi) {
-    for (int h = 0; h < a.heads; ++h) {
-      int64_t hv;
-      if (!ngram_hash(a, t, a.orders[oi], h, hv)) continue;
-      float* row = reinterpret_cast<float*>(a.tables[oi * a.heads + h]) + hv * a.width;
-      for (int c = lane; c < a.width; c += 32) atomicAdd(row + c, to_float(dout[t * hidden + h * a.width + c]));
+  for (int64_t i = warp; i < n; i += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t key = keys[i];
+    if (key == kNoKey || (i > 0 && keys[i - 1] == key)) continue;  // invalid, or not a run head
+    int64_t end = i + 1;
+    while (end < n && keys[end] == key) ++end;
+    const int j = static_cast<int>(key / a.buckets);
+    const int h = j % a.heads;
+    TG* row = reinterpret_cast<TG*>(a.tables[j]) + (key % a.buckets) * a.width;
+    for (int c = lane; c < a.width; c += 32) {
+      float acc = 0.f;
+      for (int64_t k = i; k < end; ++k) acc += to_float(dout[(order[k] / per) * hidden + h * a.width + c]);
+      store_f(row + c, load_f(row + c) + acc);
     }
   }
 }
@@ -134,16 +164,58 @@ at::Tensor ngram_fwd(at::Tensor ids, at::Tensor pos, std::vector<at::Tensor> tab
   return out;
 }
 
-void ngram_bwd(at::Tensor dout, at::Tensor ids, at::Tensor pos, std::vector<at::Tensor> grads,
-               std::vector<int64_t> orders, int64_t heads, int64_t buckets) {
+// Keys of every (token, order, head), for the caller's stable sort.
+at::Tensor ngram_keys(at::Tensor ids, at::Tensor pos, std::vector<int64_t> orders, int64_t heads, int64_t buckets,
+                      int64_t width) {
   c10::cuda::CUDAGuard guard(ids.device());
-  for (auto& g : grads) TORCH_CHECK(g.scalar_type() == at::kFloat, "ngram_bwd: table grads must be fp32");
-  NGramArgs a = make_args(ids, pos, grads, orders, heads, buckets);
-  if (a.S == 0) return;
+  TORCH_CHECK((int64_t)orders.size() <= kMaxOrders && heads <= kMaxHeads, "too many n-gram orders or heads");
+  NGramArgs a{};
+  TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == at::kLong && ids.is_contiguous() && ids.dim() == 1);
+  TORCH_CHECK(pos.scalar_type() == at::kLong && pos.is_contiguous() && pos.numel() == ids.numel());
+  a.ids = ids.data_ptr<int64_t>();
+  a.pos = pos.data_ptr<int64_t>();
+  a.S = ids.numel();
+  a.buckets = buckets;
+  a.norders = (int)orders.size();
+  a.heads = (int)heads;
+  a.width = (int)width;
+  for (size_t i = 0; i < orders.size(); ++i) a.orders[i] = (int)orders[i];
+  auto keys = at::empty({a.S * a.norders * a.heads}, ids.options());
+  if (keys.numel() == 0) return keys;
   const int threads = 256;
-  const int64_t blocks = (a.S * 32 + threads - 1) / threads;
+  ngram_keys_kernel<<<(keys.numel() + threads - 1) / threads, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      a, keys.data_ptr<int64_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return keys;
+}
+
+// grads[j] += sum of dout slices whose sorted key names table j; sorted_keys / order: the stable
+// sort of ngram_keys() and the original indices.  grads: [buckets, width], bf16 or fp32.
+void ngram_bwd(at::Tensor dout, at::Tensor ids, at::Tensor pos, at::Tensor sorted_keys, at::Tensor order,
+               std::vector<at::Tensor> grads, std::vector<int64_t> orders, int64_t heads, int64_t buckets) {
+  c10::cuda::CUDAGuard guard(ids.device());
+  NGramArgs a = make_args(ids, pos, grads, orders, heads, buckets);
+  const auto gdt = grads[0].scalar_type();
+  for (auto& g : grads)
+    TORCH_CHECK(g.scalar_type() == gdt && (gdt == at::kFloat || gdt == at::kBFloat16),
+                "ngram_bwd: table grads must all be fp32 or all bf16");
+  const int64_t n = sorted_keys.numel();
+  TORCH_CHECK(sorted_keys.scalar_type() == at::kLong && order.scalar_type() == at::kLong && order.numel() == n &&
+                  n == a.S * a.norders * a.heads && sorted_keys.is_contiguous() && order.is_contiguous(),
+              "ngram_bwd: one sorted key and index per (token, order, head)");
+  TORCH_CHECK(dout.is_contiguous() && dout.numel() == a.S * a.width * a.heads, "ngram_bwd: dout [tokens, hidden]");
+  if (n == 0) return;
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((n * 32 + threads - 1) / threads, 148 * 16);
   auto st = at::cuda::getCurrentCUDAStream();
-  if (dout.scalar_type() == at::kFloat) ngram_bwd_kernel<float><<<blocks, threads, 0, st>>>(a, dout.data_ptr<float>());
-  else ngram_bwd_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()));
+  const int64_t* k = sorted_keys.data_ptr<int64_t>();
+  const int64_t* o = order.data_ptr<int64_t>();
+  const bool fd = dout.scalar_type() == at::kFloat;
+  TORCH_CHECK(fd || dout.scalar_type() == at::kBFloat16, "ngram_bwd: dout must be fp32 or bf16");
+  const auto* db = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  if (fd && gdt == at::kFloat) ngram_bwd_kernel<float, float><<<blocks, threads, 0, st>>>(a, dout.data_ptr<float>(), k, o, n);
+  else if (fd) ngram_bwd_kernel<float, __nv_bfloat16><<<blocks, threads, 0, st>>>(a, dout.data_ptr<float>(), k, o, n);
+  else if (gdt == at::kFloat) ngram_bwd_kernel<__nv_bfloat16, float><<<blocks, threads, 0, st>>>(a, db, k, o, n);
+  else ngram_bwd_kernel<__nv_bfloat16, __nv_bfloat16><<<blocks, threads, 0, st>>>(a, db, k, o, n);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

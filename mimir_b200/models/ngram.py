@@ -9,7 +9,7 @@ packed sequence (``position[t] - position[t-o] == o`` for every offset).  The su
 optionally gated by ``sigmoid(Wq rms(x) + Wk rms(mem))`` and added as ``x + alpha * mem``.
 
 On CUDA the hash, gather, validity mask and order sum run in one kernel
-(:func:`mimir_b200.ops.ngram_lookup`), with a scatter-add backward into the tables.
+(:func:`mimir_b200.ops.ngram_lookup`), with a deterministic backward that touches only the hashed rows.
 """
 from __future__ import annotations
 

@@ -78,24 +78,28 @@ def kernels_enabled(t: torch.Tensor | None = None) -> bool:
 
 
 class KernelTimeout(RuntimeError):
-    """A bounded wait inside a hand-written kernel ran out: the outputs of that launch are not
-    valid.  Raised by :func:`check_kernel_status`."""
+    """A hand-written kernel reported a launch whose outputs are not valid: a bounded wait ran out,
+    an expert-exchange route named a rank or row outside its buffers, or a token id was outside
+    the embedding table.  Raised by :func:`check_kernel_status`."""
 
 
 def kernel_status(device: torch.device) -> dict:
-    """Read and clear the bounded-wait status words of every kernel family on ``device``
-    (attention, dense GEMM, grouped GEMM): 0 means every wait since the last read completed."""
+    """Read and clear the status words of every kernel family on ``device``: the bounded-wait
+    words of attention, dense GEMM and grouped GEMM (0: every wait since the last read completed),
+    the expert-exchange route word and the embedding's token-id word (0: every index in range)."""
     if device.type != "cuda" or not available():
         return {}
     C = ext()
     index = device.index if device.index is not None else torch.cuda.current_device()
     return {"attention": int(C.fmha_status(device)), "gemm": int(C.gemm_status(index)),
-            "grouped_gemm": int(C.grouped_gemm_status(index))}
+            "grouped_gemm": int(C.grouped_gemm_status(index)), "moe_routes": int(C.moe_route_status(index)),
+            "embedding_ids": int(C.embed_status(index))}
 
 
 def check_kernel_status(device: torch.device, step=None) -> None:
-    """Raise :class:`KernelTimeout` if any kernel on ``device`` reported a timed-out wait."""
+    """Raise :class:`KernelTimeout` if any kernel on ``device`` reported a failed launch."""
     bad = {name: code for name, code in kernel_status(device).items() if code}
     if bad:
         where = "" if step is None else f" at or before step {step}"
-        raise KernelTimeout(f"Kernel wait timed out{where}: {bad} (status codes from csrc/common.cuh)")
+        raise KernelTimeout(f"Kernel wait timed out or index out of range{where}: {bad} "
+                            "(wait status codes from csrc/common.cuh)")

@@ -223,14 +223,14 @@ class _GroupedExpertsFn(torch.autograd.Function):
             from mimir_b200.ops._ext import ext
             C = ext()
             buf = ep.acquire(2 * plan.capacity, d)
-            C.moe_dispatch(x.contiguous(), plan.rows, plan.dst, buf.peer_ptrs(0, d), k)
+            C.moe_dispatch(x.contiguous(), plan.rows, plan.dst, buf.peer_ptrs(0, d), k, plan.capacity)
             ep.barrier()  # every rank's rows have landed in their owners' buffers
             xp = buf.view(0, ex.rows_in, d)
             _, gus = _expert_forward(xp, plan.expert_rows, weights, buf.view(plan.capacity, ex.rows_in, d),
                                      plan.expert_rows_dev)
             ep.barrier()  # every owner's outputs are in place
             ys = torch.empty(T * k, d, dtype=x.dtype, device=x.device) if keep else None
-            out = C.moe_combine(buf.peer_ptrs(plan.capacity, d), plan.rows, plan.dst, w32, T, k, d, ys)
+            out = C.moe_combine(buf.peer_ptrs(plan.capacity, d), plan.rows, plan.dst, w32, T, k, d, ys, plan.capacity)
             if keep:
                 xp = xp.clone()
             ep.release(buf)
@@ -262,13 +262,14 @@ class _GroupedExpertsFn(torch.autograd.Function):
             C = ext()
             gbuf = ep.acquire(2 * plan.capacity, d)
             ep.barrier()  # every owner is done with the previous use of this buffer
-            dw = C.moe_combine_bwd(dout, w32, plan.rows, plan.dst, ys, gbuf.peer_ptrs(0, d), k)
+            dw = C.moe_combine_bwd(dout, w32, plan.rows, plan.dst, ys, gbuf.peer_ptrs(0, d), k, plan.capacity)
             ep.barrier()  # the scaled output gradients have reached their owners
             dy = gbuf.view(0, ex.rows_in, d)
             dxp = gbuf.view(plan.capacity, ex.rows_in, d)
             grads = _expert_backward(dy, xp, gus, plan.expert_rows, weights, dxp, plan.expert_rows_dev)
             ep.barrier()  # every owner's input gradients are in place
-            dx = C.moe_combine(gbuf.peer_ptrs(plan.capacity, d), plan.rows, plan.dst, None, T, k, d, None)
+            dx = C.moe_combine(gbuf.peer_ptrs(plan.capacity, d), plan.rows, plan.dst, None, T, k, d, None,
+                               plan.capacity)
             ep.release(gbuf)
         else:
             dys = (dout.float().unsqueeze(1) * w32.unsqueeze(-1)).to(dout.dtype).reshape(T * k, d)

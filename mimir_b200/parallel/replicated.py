@@ -22,12 +22,26 @@ With global-norm clipping the step is two kernels: a reduce pass that writes the
 gradient shard and per-CTA sums of squares, one scalar all-reduce for the norm, then the
 update pass reading the reduced shard with the clip coefficient.
 
+Without clipping the AdamATan2 update overlaps the backward.  The trainable parameters form
+buckets (one per transformer block, one per other parameter).  The engine counts the gradient
+arrivals of every parameter in a step and notes the order in which the buckets received their
+last arrival; once two consecutive steps agree on the counts, it knows how many arrivals make a
+parameter's gradient final, and the noted order (rank 0's, on every rank) becomes the firing
+order.  During the last micro-batch's backward, a bucket whose parameters have all arrived (and
+every bucket before it in that order) is updated on a side stream: an event on the backward stream orders the update after every kernel that read those
+weights or wrote those gradients, and on several ranks a one-element all-reduce on the side
+stream waits until every rank's backward has passed the bucket.  The optimizer step updates
+what is left, joins the side stream and closes with the usual barrier.  A gradient that arrives
+for a bucket after its update raised an error (the model's graph changed between steps).
+
 On CPU (tests, Gloo) the same algorithm runs with PyTorch collectives (all-reduce of the
 gradients, the reference AdamATan2 arithmetic on the shard, all-gather of the weights).
 """
 from __future__ import annotations
 
 import math
+import os
+from contextlib import contextmanager
 from dataclasses import dataclass
 from typing import Optional
 
@@ -101,11 +115,27 @@ class ReplicatedEngine:
         # optimizer, a parameter without one (e.g. outside the truncated-BPTT window) is not
         # updated at all (no decay, no moment update, no step count).
         self.touched: set[str] = set()
+        self.arrivals: dict[str, int] = {}
         for s in self.slots:
             if s.trainable:
-                s.param.register_post_accumulate_grad_hook(lambda _p, fqn=s.fqn: self.touched.add(fqn))
+                s.param.register_post_accumulate_grad_hook(lambda _p, fqn=s.fqn: self._arrived(fqn))
                 # Ops that accumulate straight into the gradient view report it here instead.
-                s.param._mimir_grad_sink = lambda _p, fqn=s.fqn: self.touched.add(fqn)
+                s.param._mimir_grad_sink = lambda _p, fqn=s.fqn: self._arrived(fqn)
+        self.buckets = self._buckets()
+        self._bucket_of = {s.fqn: b for b, bucket in enumerate(self.buckets) for s in bucket}
+        self.order = list(range(len(self.buckets)))  # firing order (learned)
+        self._position = {b: i for i, b in enumerate(self.order)}
+        self._last_arrival: dict[int, int] = {}  # bucket -> sequence number of its latest arrival
+        self.overlap_enabled = os.environ.get("MIMIR_OVERLAP_UPDATE", "1") != "0"
+        self.expected: Optional[dict[str, int]] = None  # arrivals per parameter in one step
+        self.overlap_ready: Optional[bool] = None  # decided (the same on every rank) after learning
+        self._learn_steps = 0
+        self._arrival_seq = 0
+        self._armed = None  # the optimizer updating bucket by bucket during this backward
+        self._next = 0  # next bucket to update, in bucket order
+        self._late: Optional[str] = None
+        self._side = None
+        self._compute = None
 
     # ------------------------------------------------------------------ setup
     @torch.no_grad()
@@ -198,10 +228,140 @@ class ReplicatedEngine:
                 ext().ipc_close(ptr, self.device.index)
             self._opened = []
 
+    def _buckets(self) -> list[list[ParamSlot]]:
+        """Trainable slots grouped by transformer block (the name up to its first integer
+        component, e.g. ``model.layers.3``); every other parameter is a bucket of its own."""
+        groups: dict[str, list[ParamSlot]] = {}
+        for s in self.slots:
+            if not s.trainable:
+                continue
+            parts = s.fqn.split(".")
+            key = next((".".join(parts[:i + 1]) for i, part in enumerate(parts) if part.isdigit()), s.fqn)
+            groups.setdefault(key, []).append(s)
+        return list(groups.values())[::-1]
+
+    # ------------------------------------------------------------------ update overlapped with the backward
+    def _arrived(self, fqn: str) -> None:
+        self.touched.add(fqn)
+        self.arrivals[fqn] = self.arrivals.get(fqn, 0) + 1
+        b = self._bucket_of[fqn]
+        self._arrival_seq += 1
+        self._last_arrival[b] = self._arrival_seq
+        if self._armed is None:
+            return
+        if self._position[b] < self._next:
+            self._late = self._late or fqn
+            return
+        while self._next < len(self.order) and self._bucket_final(self.order[self._next]):
+            self._fire(self.order[self._next])
+            self._next += 1
+
+    def _bucket_final(self, b: int) -> bool:
+        return all(self.arrivals.get(s.fqn, 0) == self.expected.get(s.fqn, 0) for s in self.buckets[b])
+
+    def _fire(self, b: int) -> None:
+        slots = [s for s in self.buckets[b] if s.fqn in self.touched]
+        if not slots and self.world == 1:
+            return  # (on several ranks every rank still takes the bucket's barrier)
+        if not self.cuda:
+            self._armed.update_slots(slots)
+            return
+        ready = torch.cuda.Event()
+        ready.record(torch.cuda.current_stream(self.device))
+        self._side.wait_event(ready)
+        with torch.cuda.stream(self._side):
+            self._armed.update_slots(slots, lean=True)
+
+    @contextmanager
+    def compute_stream(self):
+        """Run the forward and backward on a high-priority stream (when the overlap is enabled):
+        the block scheduler then hands a freed SM to a waiting backward CTA before a pending CTA of
+        the update, which runs on a default-priority side stream.  The caller's stream waits for
+        the compute stream on exit."""
+        if not (self.cuda and self.overlap_enabled):
+            yield
+            return
+        if self._compute is None:
+            self._compute = torch.cuda.Stream(self.device, priority=-100)  # clamped to the highest
+        outer = torch.cuda.current_stream(self.device)
+        self._compute.wait_stream(outer)
+        try:
+            with torch.cuda.stream(self._compute):
+                yield
+        finally:
+            outer.wait_stream(self._compute)
+
+    def arm_overlap(self, optimizer) -> bool:
+        """Before the last micro-batch's backward: update buckets as their gradients become final.
+        Needs an optimizer whose ``update_slots`` works per bucket and arrival counts that two
+        steps agreed on."""
+        if not (self.overlap_enabled and self.overlap_ready and getattr(optimizer, "bucket_updates", False)
+                and self.reduced is None):
+            return False
+        if self.cuda and self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+        self._armed, self._next, self._late = optimizer, 0, None
+        return True
+
+    def disarm_overlap(self) -> None:
+        self._armed = None
+
+    def overlap_armed(self) -> bool:
+        return self._armed is not None
+
+    def finish_overlap(self) -> None:
+        """Optimizer step after an armed backward: update the remaining buckets, join the side
+        stream, then the closing barrier (every rank's weight stores have landed)."""
+        try:
+            while self._next < len(self.order):
+                self._fire(self.order[self._next])
+                self._next += 1
+        finally:
+            self._armed = None
+        if self.cuda:
+            torch.cuda.current_stream(self.device).wait_stream(self._side)
+        self.barrier()
+        if self._late is not None:
+            raise RuntimeError(f"A gradient of {self._late} arrived after its bucket was updated: the model's "
+                               "backward changed between steps (set MIMIR_OVERLAP_UPDATE=0 for such models)")
+
+    def learn_arrivals(self) -> None:
+        """After an optimizer step: this step's arrival counts become the expectation.  Until the
+        overlap is decided, the order in which the buckets received their last arrival becomes
+        the firing order (rank 0's on every rank, so all ranks take their per-bucket barriers in
+        the same order), and the overlap is switched on once two consecutive steps agree on
+        counts and order on every rank (off for good after 8 steps without agreement).  The
+        decision takes two collectives per learning step and none afterwards."""
+        same_counts = self.arrivals == self.expected
+        self.expected = dict(self.arrivals)
+        if self.overlap_ready is not None or not self.overlap_enabled:
+            return
+        self._learn_steps += 1
+        last = self._last_arrival
+        order = sorted(range(len(self.buckets)), key=lambda b: (b not in last, last.get(b, 0), b))
+        if self.world > 1:
+            box = [order]
+            dist.broadcast_object_list(box, src=dist.get_global_rank(self.group, 0) if self.group else 0,
+                                       group=self.group)
+            order = box[0]
+            flag = torch.tensor([float(same_counts)], device=self.device)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+            same_counts = bool(flag.item())
+        agreed = same_counts and order == self.order
+        self.order = order
+        self._position = {b: i for i, b in enumerate(order)}
+        if agreed:
+            self.overlap_ready = True
+        elif self._learn_steps >= 8:
+            self.overlap_ready = False
+
     # ------------------------------------------------------------------ step plumbing
     def zero_grad(self) -> None:
         self.grads.zero_()
         self.touched.clear()
+        self.arrivals.clear()
+        self._last_arrival.clear()
+        self._arrival_seq = 0
 
     def barrier(self) -> None:
         if self.world == 1:
@@ -260,17 +420,23 @@ class ReplicatedEngine:
             dist.all_reduce(total, group=self.group)
         return total
 
-    def summed_grads(self) -> Tensor:
-        """fp32 gradients summed over the ranks (rank-local parameters keep their own)."""
+    def summed_grads(self, slots: Optional[list] = None) -> Tensor:
+        """fp32 gradients summed over the ranks (rank-local parameters keep their own); with
+        ``slots``, only their ranges are reduced."""
         full = self.grads.to(torch.float32)
         if self.world > 1:
-            dist.all_reduce(full[:self.replicated_total], group=self.group)
+            if slots is None:
+                dist.all_reduce(full[:self.replicated_total], group=self.group)
+            else:
+                for s in slots:
+                    if not s.local:
+                        dist.all_reduce(full[s.flat:s.flat + s.numel], group=self.group)
         return full
 
     @torch.no_grad()
-    def gather_weights(self) -> None:
+    def gather_weights(self, slots: Optional[list] = None) -> None:
         """Rebuild every rank's replicated weights from the master shards (after a load)."""
-        for s in self.slots:
+        for s in self.slots if slots is None else slots:
             local = self.master[s.shard:s.shard + s.shard_numel].to(self.compute_dtype)
             if self.world == 1 or s.local:
                 self.weights[s.shard_flat:s.shard_flat + s.shard_numel] = local
@@ -330,6 +496,8 @@ class ReplicatedAdamATan2(Optimizer):
         lr = group["lr"]
         return float(lr * self.parameter_lr_scales[p]) if self.parameter_lr_scales is not None else float(lr)
 
+    bucket_updates = True  # the update of one set of parameters does not depend on the others
+
     @torch.no_grad()
     def step(self, closure=None):
         if closure is not None:
@@ -337,13 +505,28 @@ class ReplicatedAdamATan2(Optimizer):
         if getattr(self, "shared_parameter_updates", None):
             raise ValueError("Shared gate-donor updates are not supported by the replicated engine")
         eng = self.engine
+        try:
+            if eng.overlap_armed():
+                eng.finish_overlap()
+            else:
+                self.update_slots([s for s in eng.slots if s.trainable and s.fqn in eng.touched], closing=True)
+        finally:
+            eng.reduced = None
+            self.grad_scale = None
+        eng.learn_arrivals()
+
+    @torch.no_grad()
+    def update_slots(self, slots: list, closing: bool = False, lean: bool = False) -> None:
+        """AdamATan2 for the touched trainable ``slots``: one fused kernel on the current stream,
+        after a barrier on several ranks (their gradients for these slots are final); ``closing``
+        adds the barrier after it (every rank's weight stores have landed); ``lean`` selects the
+        kernel variant that runs beside the backward's kernels."""
+        eng = self.engine
         (group,) = self.param_groups
         b1, b2 = group["betas"]
         lrs, wds, bc1, bc2_sqrt = {}, {}, {}, {}
         corrections: dict = {}  # step value -> (bc1, sqrt(bc2)); parameters almost always share one
-        for s in eng.slots:
-            if not s.trainable or s.fqn not in eng.touched:
-                continue
+        for s in slots:
             st = self.state[s.param]
             st["step"] += 1
             lrs[s.fqn] = self._lr(group, s.param)
@@ -360,19 +543,19 @@ class ReplicatedAdamATan2(Optimizer):
             table, blocks = eng.segments(lrs, wds, {k: float(v) for k, v in bc1.items()},
                                          {k: float(v) for k, v in bc2_sqrt.items()})
             if eng.reduced is None:
-                eng.barrier()  # every rank's backward has finished writing its gradients
+                eng.barrier()  # every rank's backward has finished writing these gradients
             ext().dp_step(eng.peer_grads, eng.peer_weights, table, blocks, eng.master, self.exp_avg, self.exp_avg_sq,
-                          self.ema, eng.reduced, self.grad_scale, b1, b2, ema if ema is not None else 0.0, [], eng.rank)
-            eng.barrier()  # every rank's weight stores have landed
+                          self.ema, eng.reduced, self.grad_scale, b1, b2, ema if ema is not None else 0.0, [], eng.rank,
+                          lean)
+            if closing:
+                eng.barrier()  # every rank's weight stores have landed
         else:
-            self._step_cpu(lrs, wds, bc1, bc2_sqrt, b1, b2, ema)
-        eng.reduced = None
-        self.grad_scale = None
+            self._step_cpu(lrs, wds, bc1, bc2_sqrt, b1, b2, ema, None if closing else slots)
 
-    def _step_cpu(self, lrs: dict, wds: dict, bc1: dict, bc2_sqrt: dict, b1, b2, ema) -> None:
+    def _step_cpu(self, lrs: dict, wds: dict, bc1: dict, bc2_sqrt: dict, b1, b2, ema, slots=None) -> None:
         eng = self.engine
         if eng.reduced is None:
-            full = eng.summed_grads()
+            full = eng.summed_grads(slots)
         scale = self.grad_scale if self.grad_scale is not None else None
         for s in eng.slots:
             if s.fqn not in lrs or s.shard_numel == 0:
@@ -396,7 +579,7 @@ class ReplicatedAdamATan2(Optimizer):
                 w.add_(torch.atan2(g, denom), alpha=-lr)
             if self.ema is not None:
                 self.ema[sl].lerp_(w, 1 - ema)
-        eng.gather_weights()
+        eng.gather_weights(slots)
 
     # ------------------------------------------------------------------ checkpoint views
     def slot_buffers(self, s: ParamSlot) -> dict:
@@ -460,6 +643,8 @@ class ReplicatedMuonAdamW(ReplicatedAdamATan2):
     One-element all-reduces order the phases.  Without CUDA the same algorithm runs with
     PyTorch collectives.
     """
+
+    bucket_updates = False  # a Muon matrix needs every rank's rows before its owner orthogonalises it
 
     def __init__(self, engine: ReplicatedEngine, *, momentum: float = 0.95, ns_steps: int = 5,
                  muon_lr_scale: float = 1.0, **kwargs):
@@ -549,13 +734,13 @@ class ReplicatedMuonAdamW(ReplicatedAdamATan2):
                 eng.barrier()  # every rank's backward has finished writing its gradients
             table, blocks = eng.segments(first["lr"], first["wd"], first["bc1"], first["bc2"], first["extra"])
             C.dp_step(eng.peer_grads, eng.peer_weights, table, blocks, eng.master, self.exp_avg, self.exp_avg_sq,
-                      self.ema, eng.reduced, self.grad_scale, b1, b2, ema_decay, self.peer_work, eng.rank)
+                      self.ema, eng.reduced, self.grad_scale, b1, b2, ema_decay, self.peer_work, eng.rank, False)
             eng.barrier()  # every shard of every matrix has reached its owner
             self._orthogonalise(owned, group["muon_ns_steps"])
             eng.barrier()  # every owner has finished
             table, blocks = eng.segments(second["lr"], second["wd"], second["bc1"], second["bc2"], second["extra"])
             C.dp_step(eng.peer_grads, eng.peer_weights, table, blocks, eng.master, self.exp_avg, self.exp_avg_sq,
-                      self.ema, None, None, b1, b2, ema_decay, self.peer_work, eng.rank)
+                      self.ema, None, None, b1, b2, ema_decay, self.peer_work, eng.rank, False)
             eng.barrier()  # every rank's weight stores have landed
         eng.reduced = None
         self.grad_scale = None

@@ -85,6 +85,30 @@ def train_accumulated_batches(config, rank: int, train_state, batches: list, use
     return metrics, skipped
 
 
+def _forward_backward_all(config, rank, train_state, batches, counts, total, step_fn, model, hsdp_rs, overlap_engine,
+                          **kwargs):
+    """Forward and backward of every micro-batch, summing their metrics; ``overlap_engine`` (a
+    replicated engine) is armed before the last backward so that it updates buckets during it."""
+    metrics = None
+    for i, (batch, count) in enumerate(zip(batches, counts), start=1):
+        last = i == len(batches)
+        if last and overlap_engine is not None:
+            overlap_engine.arm_overlap(train_state.optim)
+        ctx = nullcontext()
+        if isinstance(model, DistributedDataParallel) and not last:
+            ctx = model.no_sync()
+        elif isinstance(model, FSDPModule):
+            if hsdp_rs:
+                model.set_requires_gradient_sync(True, recurse=True)
+                model.set_requires_all_reduce(last, recurse=True)
+            else:
+                model.set_requires_gradient_sync(last, recurse=True)
+        with ctx:
+            metrics = _add_metrics(metrics, step_fn(train_state, batch, count / total, **kwargs))
+        trace_print(config, rank, f"forward_backward_end step={train_state.step} microbatch={i}")
+    return metrics
+
+
 def _accumulate_and_step(config, rank: int, train_state, batches: list, use_compiled: bool,
                          zero_grad_after_step: bool, optimizer_step_enabled: bool, **kwargs):
     trace_print(config, rank, f"train_accumulated_begin step={train_state.step} microbatches={len(batches)}")
@@ -99,21 +123,22 @@ def _accumulate_and_step(config, rank: int, train_state, batches: list, use_comp
                and config.fsdp_shard_degree is not None and dist.is_available() and dist.is_initialized()
                and config.fsdp_shard_degree < dist.get_world_size())
     metrics = None
+    engine = getattr(model, "replicated_engine", None)
+    # The replicated engine may run the optimizer update bucket by bucket inside the last backward
+    # when nothing between the backward and the step reads the gradients or the old weights.
+    overlap = (engine is not None and optimizer_step_enabled and not use_compiled
+               and config.gradient_clip_norm is None and config.gradient_skip_norm is None
+               and kwargs.get("stability_diagnostics") is None and not config.experiment_update_probe_interval
+               and not has_balanced_routers(model))
+    streams = engine.compute_stream() if overlap else nullcontext()
     try:
-        for i, (batch, count) in enumerate(zip(batches, counts), start=1):
-            last = i == len(batches)
-            ctx = nullcontext()
-            if isinstance(model, DistributedDataParallel) and not last:
-                ctx = model.no_sync()
-            elif isinstance(model, FSDPModule):
-                if hsdp_rs:
-                    model.set_requires_gradient_sync(True, recurse=True)
-                    model.set_requires_all_reduce(last, recurse=True)
-                else:
-                    model.set_requires_gradient_sync(last, recurse=True)
-            with ctx:
-                metrics = _add_metrics(metrics, step_fn(train_state, batch, count / total, **kwargs))
-            trace_print(config, rank, f"forward_backward_end step={train_state.step} microbatch={i}")
+        with streams:
+            metrics = _forward_backward_all(config, rank, train_state, batches, counts, total, step_fn, model,
+                                            hsdp_rs, engine if overlap else None, **kwargs)
+    except BaseException:
+        if engine is not None:
+            engine.disarm_overlap()
+        raise
     finally:
         if isinstance(model, FSDPModule):
             model.set_requires_gradient_sync(True, recurse=True)

@@ -118,6 +118,67 @@ def test_ngram_kernel_matches_torch():
     _close(out, ref, 1e-5, 1e-5, "ngram")
 
 
+def _ngram_case():
+    from mimir_b200.models.ngram import NGramMemory
+    torch.manual_seed(0)
+    mem = NGramMemory(256, (2, 3), 1021, heads=2).cuda()
+    for t in mem.tables:
+        torch.nn.init.normal_(t)
+    ids = torch.randint(0, 40, (1, 777), device="cuda")  # few distinct ids: long runs of equal keys
+    pos = torch.cat([torch.arange(300), torch.arange(477)]).cuda()[None]
+    return mem, ids, pos
+
+
+def test_ngram_backward_matches_torch_and_is_deterministic():
+    import os
+    mem, ids, pos = _ngram_case()
+    g = torch.randn(1, 777, 256, device="cuda")
+    runs = []
+    for _ in range(2):
+        mem.zero_grad(set_to_none=True)
+        mem.lookup(ids, pos, torch.float32).backward(g)
+        runs.append([t.grad.clone() for t in mem.tables])
+    mem.zero_grad(set_to_none=True)
+    os.environ["MIMIR_DISABLE_KERNELS"] = "1"
+    try:
+        mem.lookup(ids, pos, torch.float32).backward(g)
+    finally:
+        os.environ.pop("MIMIR_DISABLE_KERNELS")
+    for a, b, t in zip(runs[0], runs[1], mem.tables):
+        assert torch.equal(a, b)  # sorted run sums: no atomics, same bits every time
+        _close(a, t.grad, 1e-5, 1e-5, "ngram grad")
+
+
+def test_ngram_backward_accumulates_into_owned_bf16_gradients():
+    """With a gradient sink (the replicated engine's flat buffer) only hashed rows change."""
+    mem, ids, pos = _ngram_case()
+    mem = mem.to(torch.bfloat16)
+    g = torch.randn(1, 777, 256, device="cuda")
+    ref = [torch.zeros_like(t, dtype=torch.float32) for t in mem.tables]
+    import os
+    os.environ["MIMIR_DISABLE_KERNELS"] = "1"
+    try:
+        fp32 = [t.detach().float().requires_grad_(True) for t in mem.tables]
+        from mimir_b200.models.ngram import ngram_hashes
+        for order, (hashes, valid) in ngram_hashes(ids, pos, mem.orders, mem.heads, mem.buckets).items():
+            base = mem.orders.index(order) * mem.heads
+            for h in range(mem.heads):
+                rows = torch.nn.functional.embedding(hashes[h], fp32[base + h]) * valid[..., None]
+                (rows * g[..., h * 128:(h + 1) * 128]).sum().backward()
+    finally:
+        os.environ.pop("MIMIR_DISABLE_KERNELS")
+    sunk = []
+    for t in mem.tables:
+        t.grad = torch.full_like(t, 0.25)
+        t._mimir_grad_sink = sunk.append
+    mem.lookup(ids, pos, torch.bfloat16).backward(g.to(torch.bfloat16))
+    assert len(sunk) == len(mem.tables)
+    for t, f in zip(mem.tables, fp32):
+        hit = f.grad.abs().sum(-1) > 0
+        assert torch.equal(t.grad[~hit], torch.full_like(t.grad[~hit], 0.25))
+        _close(t.grad.float()[hit], (0.25 + f.grad[hit]).to(torch.bfloat16).float(), 3e-2, 3e-2, "ngram in place")
+
+
 def _packed(lengths, prefixes, heads, kv_heads, seed=0, pad=0):
     g = torch.Generator(device="cuda").manual_seed(seed)
     T = sum(lengths) + pad

@@ -28,23 +28,52 @@ def test_exchange_kernels_match_torch():
     ep = expert_parallel(E, dev, distributed=False)
     plan = ep.plan(topi)
     buf = torch.zeros(T * K, D, device=dev, dtype=torch.bfloat16)
-    C.moe_dispatch(x, plan.rows, plan.dst, [buf.data_ptr()], K)
+    C.moe_dispatch(x, plan.rows, plan.dst, [buf.data_ptr()], K, T * K)
     rows = plan.rows.long()
     for j in range(K):
         assert torch.equal(buf[rows[:, j]], x)
     y = torch.randn(T * K, D, device=dev, generator=g).to(torch.bfloat16)
     w = torch.rand(T, K, device=dev, generator=g)
     ys = torch.empty(T * K, D, device=dev, dtype=torch.bfloat16)
-    out = C.moe_combine([y.data_ptr()], plan.rows, plan.dst, w, T, K, D, ys)
+    out = C.moe_combine([y.data_ptr()], plan.rows, plan.dst, w, T, K, D, ys, T * K)
     want = (y[rows].float() * w.unsqueeze(-1)).sum(1)
     torch.testing.assert_close(out.float(), want, rtol=1e-2, atol=1e-2)
     assert torch.equal(ys.view(T, K, D), y[rows])  # the loaded rows are kept for the backward
     dout = torch.randn(T, D, device=dev, generator=g).to(torch.bfloat16)
     dy = torch.zeros_like(y)
-    dw = C.moe_combine_bwd(dout, w, plan.rows, plan.dst, ys, [dy.data_ptr()], K)
+    dw = C.moe_combine_bwd(dout, w, plan.rows, plan.dst, ys, [dy.data_ptr()], K, T * K)
     torch.testing.assert_close(dw, (dout.float().unsqueeze(1) * y[rows].float()).sum(-1), rtol=1e-4, atol=1e-3)
     for j in range(K):
         torch.testing.assert_close(dy[rows[:, j]].float(), (w[:, j:j + 1] * dout.float()), rtol=1e-2, atol=1e-2)
+
+
+def test_exchange_skips_and_reports_routes_outside_the_buffers():
+    """A route naming a rank or row outside the peer buffers is skipped and reported through the
+    status word (read by ``check_kernel_status``) instead of becoming a peer access."""
+    from mimir_b200.ops._ext import KernelTimeout, check_kernel_status, ext
+    C = ext()
+    dev = torch.device("cuda", 0)
+    T, K, D = 8, 2, 64
+    x = torch.randn(T, D, device=dev).to(torch.bfloat16)
+    rows = torch.arange(T * K, device=dev, dtype=torch.int32).view(T, K).contiguous()
+    dst = torch.zeros(T, K, device=dev, dtype=torch.int32)
+    bad_rows, bad_dst = rows.clone(), dst.clone()
+    bad_rows[3, 1] = T * K + 5  # past the buffer
+    bad_dst[5, 0] = 1  # a rank that does not exist (one-rank group)
+    buf = torch.zeros(T * K, D, device=dev, dtype=torch.bfloat16)
+    C.moe_dispatch(x, bad_rows, bad_dst, [buf.data_ptr()], K, T * K)
+    torch.cuda.synchronize()
+    assert C.moe_route_status(0) == 1 and C.moe_route_status(0) == 0  # read clears it
+    good = [t for t in range(T) if t not in (3, 5)]
+    assert torch.equal(buf[rows[good, 0].long()], x[good])
+    y = torch.randn(T * K, D, device=dev).to(torch.bfloat16)
+    out = C.moe_combine([y.data_ptr()], bad_rows, bad_dst, None, T, K, D, None, T * K)
+    torch.testing.assert_close(out[3].float(), y[rows[3, 0].long()].float())  # the bad slot adds zero
+    with pytest.raises(KernelTimeout, match="moe_routes"):
+        check_kernel_status(dev)
+    C.moe_dispatch(x, rows, dst, [buf.data_ptr()], K, T * K)  # a good launch afterwards
+    torch.cuda.synchronize()
+    assert C.moe_route_status(0) == 0
 
 
 def _mixture(grouped, ep=False, shared=1, seed=0):

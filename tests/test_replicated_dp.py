@@ -125,3 +125,98 @@ def test_replicated_training_resumes_exactly_and_matches_plain(tmp_path, optimiz
     assert plain.keys() == rep.keys()
     for k in plain:
         torch.testing.assert_close(plain[k], rep[k], rtol=1e-5, atol=1e-6, msg=k)
+
+
+class _Blocks(torch.nn.Module):
+    """Three blocks and a head; block 1 runs twice per forward (two gradient arrivals per weight).
+    The input projection is registered last but used first, like a language model's embedding."""
+
+    def __init__(self):
+        super().__init__()
+        torch.manual_seed(0)
+        self.blocks = torch.nn.ModuleList(torch.nn.Sequential(torch.nn.Linear(24, 24), torch.nn.Tanh())
+                                          for _ in range(3))
+        self.head = torch.nn.Linear(24, 5, bias=False)
+        self.embed = torch.nn.Linear(16, 24)
+
+    def forward(self, x):
+        h = self.embed(x)
+        for i in (0, 1, 1, 2):
+            h = h + self.blocks[i](h)
+        return self.head(h)
+
+
+def _train_overlapped(model, opt, engine, steps, seed=1):
+    """Arms the engine before each backward, as the training step does; returns the number of
+    bucket updates that ran inside a backward and, for the last step, the gradient arrival after
+    which each of them ran."""
+    gen = torch.Generator().manual_seed(seed)
+    inside, when = [], []
+    update = opt.update_slots
+
+    def spy(slots, closing=False, lean=False):
+        inside.append(engine.overlap_armed() and not closing)
+        when.append(engine._arrival_seq)
+        update(slots, closing, lean)
+    opt.update_slots = spy
+    for i in range(steps):
+        x = torch.randn(7, 16, generator=gen)
+        opt.zero_grad()
+        for g in opt.param_groups:
+            g["lr"] = 1e-2 * (i + 1)
+        when.clear()
+        engine.arm_overlap(opt)
+        model(x).square().sum().backward()
+        opt.step()
+    return sum(inside), list(when)
+
+
+def _overlap_worker(rank, world, init, out):
+    if world > 1:
+        dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
+    try:
+        results = []
+        for enabled in (False, True):
+            model = _Blocks()
+            engine = wrap_replicated(model, torch.device("cpu"), torch.float32)
+            engine.overlap_enabled = enabled
+            opt = ReplicatedAdamATan2(engine, lr=0.0, betas=(0.9, 0.95), weight_decay=0.1, ema=0.9)
+            fired, when = _train_overlapped(model, opt, engine, steps=5)
+            results.append(({n: p.detach().clone() for n, p in model.named_parameters()},
+                            opt.exp_avg_sq.clone(), opt.ema.clone(), fired, when))
+        torch.save(results, f"{out}.{rank}.pt")
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_update_overlapped_with_backward_equals_closing_update(tmp_path, world):
+    """Bucket-by-bucket updates inside the backward give the same weights, moments and EMA as
+    the single update after it; two steps teach the arrival counts, the last three overlap."""
+    init = f"file://{tmp_path / 'rdv'}"
+    if world == 1:
+        _overlap_worker(0, 1, init, str(tmp_path / "o"))
+    else:
+        mp.spawn(_overlap_worker, args=(world, init, str(tmp_path / "o")), nprocs=world, join=True)
+    for rank in range(world):
+        (plain, v0, e0, fired0, _), (over, v1, e1, fired1, when) = torch.load(f"{tmp_path / 'o'}.{rank}.pt")
+        assert fired0 == 0 and fired1 == 3 * 6  # 3 overlapped steps x (head, 3 blocks, embed weight, bias)
+        # head and blocks are updated while the backward still runs (after arrivals 1, 3, 7, 9 of 11)
+        assert when == sorted(when) and len(set(when)) >= 5 and when[0] < when[-1] - 5, when
+        for n in plain:
+            assert torch.equal(plain[n], over[n]), n
+        assert torch.equal(v0, v1) and torch.equal(e0, e1)
+
+
+def test_gradient_after_its_bucket_update_raises():
+    model = _Blocks()
+    engine = wrap_replicated(model, torch.device("cpu"), torch.float32)
+    opt = ReplicatedAdamATan2(engine, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, ema=0.9)
+    _train_overlapped(model, opt, engine, steps=2)
+    opt.zero_grad()
+    assert engine.arm_overlap(opt)
+    model(torch.randn(7, 16)).square().sum().backward()
+    model.head(torch.randn(3, 24)).sum().backward()  # a second arrival for the already-updated head
+    with pytest.raises(RuntimeError, match="arrived after its bucket was updated"):
+        opt.step()

@@ -226,3 +226,28 @@ def test_multi_gpu_muon_step_matches_summed_reference(tmp_path):
         for r in range(world):
             piece = w.reshape(rows, -1)[r * chunk:(r + 1) * chunk].reshape(-1)
             torch.testing.assert_close(masters[r][n], piece, rtol=1e-4, atol=1e-5, msg=lambda m, n=n: f"{n}: {m}")
+
+
+def test_lean_update_variant_is_bit_identical():
+    """The update that runs beside the backward (128-thread CTAs, one per chunk, no gradient
+    prefetch) computes exactly what the persistent variant computes."""
+    from mimir_b200.parallel.replicated import ReplicatedAdamATan2, wrap_replicated
+    dev = torch.device("cuda", 0)
+    runs = []
+    for lean in (False, True):
+        model = _model(dev)
+        engine = wrap_replicated(model, dev, torch.bfloat16)
+        opt = ReplicatedAdamATan2(engine, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, ema=0.9)
+        gen = torch.Generator(device=dev).manual_seed(3)
+        for _ in range(3):
+            opt.zero_grad()
+            x = torch.randn(33, 64, device=dev, dtype=torch.bfloat16, generator=gen)
+            model(x).float().square().mean().backward()
+            slots = [s for s in engine.slots if s.fqn in engine.touched]
+            opt.update_slots(slots[:1], lean=lean)  # two launches, as the overlapped step makes them
+            opt.update_slots(slots[1:], lean=lean, closing=True)
+        torch.cuda.synchronize()
+        runs.append((engine.master.clone(), opt.exp_avg_sq.clone(), opt.ema.clone(), engine.weights.clone()))
+        engine.close()
+    for a, b in zip(*runs):
+        assert torch.equal(a, b)
