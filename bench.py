@@ -179,7 +179,7 @@ def init_distributed(gpus: int):
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     from datetime import timedelta
-    dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=600))
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=300))
     return rank, world, local
 
 

@@ -251,3 +251,74 @@ def test_lean_update_variant_is_bit_identical():
         engine.close()
     for a, b in zip(*runs):
         assert torch.equal(a, b)
+
+
+class _Blocks(torch.nn.Module):
+    """A head, three blocks (block 1 used twice) and an input projection registered last."""
+
+    def __init__(self):
+        super().__init__()
+        self.blocks = torch.nn.ModuleList(torch.nn.Sequential(torch.nn.Linear(64, 64), torch.nn.Tanh())
+                                          for _ in range(3))
+        self.head = torch.nn.Linear(64, 32, bias=False)
+        self.embed = torch.nn.Linear(64, 64)
+
+    def forward(self, x):
+        h = self.embed(x)
+        for i in (0, 1, 1, 2):
+            h = h + self.blocks[i](h)
+        return self.head(h)
+
+
+def _overlap_rank(rank, world, port, out):
+    """Trains the same model with the update overlapped with the backward and without; every rank
+    sees its own data, so each bucket's update reads the peers' gradients."""
+    from contextlib import nullcontext
+    from datetime import timedelta
+
+    import torch.distributed as dist
+    from mimir_b200.parallel.replicated import ReplicatedAdamATan2, wrap_replicated
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
+    try:
+        results = []
+        for enabled in (False, True):
+            torch.manual_seed(0)
+            model = _Blocks().to(dev)
+            engine = wrap_replicated(model, dev, torch.bfloat16)
+            engine.overlap_enabled = enabled
+            opt = ReplicatedAdamATan2(engine, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, ema=0.9)
+            gen = torch.Generator(device=dev).manual_seed(100 + rank)
+            armed_steps = 0
+            for _ in range(6):
+                opt.zero_grad()
+                x = torch.randn(48, 64, device=dev, dtype=torch.bfloat16, generator=gen)
+                armed = engine.arm_overlap(opt)
+                armed_steps += armed
+                with engine.compute_stream() if armed else nullcontext():
+                    model(x).float().square().mean().backward()
+                opt.step()
+            torch.cuda.synchronize()
+            results.append((engine.master.cpu(), opt.exp_avg_sq.cpu(), opt.ema.cpu(), engine.weights.cpu(),
+                            armed_steps))
+            dist.barrier()
+            engine.close()
+        torch.save(results, f"{out}.{rank}.pt")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_multi_gpu_overlapped_update_equals_closing_update(tmp_path):
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 8)
+    mp.spawn(_overlap_rank, args=(world, _free_port(), str(tmp_path / "o")), nprocs=world, join=True)
+    ranks = [torch.load(tmp_path / f"o.{r}.pt") for r in range(world)]
+    for plain, over in ranks:
+        assert plain[4] == 0 and over[4] == 4  # two learning steps, then four overlapped ones
+        for a, b in zip(plain[:4], over[:4]):
+            assert torch.equal(a, b)
+    for r in range(1, world):
+        assert torch.equal(ranks[r][1][3], ranks[0][1][3])  # every replica holds the same weights
