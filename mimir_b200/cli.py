@@ -101,6 +101,26 @@ def _doctor(_args, _rest):
     print(json.dumps(out, indent=2))
 
 
+def _campaign(args, _rest) -> None:
+    from mimir_b200.campaigns.prepare import RECIPES, extend, prepare
+    if args.action == "prepare":
+        print(prepare(args.output, args.data, args.tokenizer, args.template,
+                      recipe=args.recipe or RECIPES / "xxs-dfm15-20k.json", gpus=args.gpus,
+                      eval_steps=args.eval_steps, database=args.database))
+    else:
+        print(f"Added {extend(args.output, extensions=args.extensions or RECIPES / 'xxs-dfm15-20k.extensions.json', release=args.release)} jobs")
+
+
+def _okf(args, _rest) -> None:
+    from mimir_b200.utils.okf import main as okf_main
+    raise SystemExit(okf_main([str(args.bundle)]))
+
+
+def _protocols(args, _rest) -> None:
+    from mimir_b200.evaluation.protocols import main as protocols_main
+    raise SystemExit(protocols_main([str(args.source), str(args.output), *args.folders]))
+
+
 def parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(prog="mimir_b200")
     sub = p.add_subparsers(dest="command", required=True)
@@ -150,6 +170,31 @@ def parser() -> argparse.ArgumentParser:
     qc = sub.add_parser("qualify-cpu", help="isolated CPU campaign: train, export, eval, resume, suspend (bit-exact)")
     qc.add_argument("output", type=Path)
     qc.set_defaults(fn=_qualify)
+    cp = sub.add_parser("campaign", help="prepare or extend a held training/evaluation campaign").add_subparsers(
+        dest="action", required=True)
+    pr = cp.add_parser("prepare", help="recipe -> held scheduler jobs (runs nothing)")
+    pr.add_argument("output", type=Path)
+    pr.add_argument("--data", type=Path, required=True)
+    pr.add_argument("--tokenizer", type=Path, required=True)
+    pr.add_argument("--template", type=Path, required=True)
+    pr.add_argument("--recipe", type=Path)
+    pr.add_argument("--gpus")
+    pr.add_argument("--eval-steps", type=int, nargs="+")
+    pr.add_argument("--database", type=Path)
+    pr.set_defaults(fn=_campaign)
+    xt = cp.add_parser("extend", help="append derived variants to a prepared campaign")
+    xt.add_argument("output", type=Path)
+    xt.add_argument("--extensions", type=Path)
+    xt.add_argument("--release", action="store_true")
+    xt.set_defaults(fn=_campaign)
+    ok = sub.add_parser("okf", help="validate an OKF 0.2 Markdown bundle")
+    ok.add_argument("bundle", type=Path, nargs="?", default=Path("wiki"))
+    ok.set_defaults(fn=_okf)
+    rp = sub.add_parser("recover-protocols", help="allowlisted protocol fields of Inspect .eval logs")
+    rp.add_argument("source", type=Path)
+    rp.add_argument("output", type=Path)
+    rp.add_argument("folders", nargs="*")
+    rp.set_defaults(fn=_protocols)
     return p
 
 
