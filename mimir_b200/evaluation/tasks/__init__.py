@@ -15,7 +15,11 @@ Families:
 * generation scored by chrF3++: ``wmt24pp``, ``andersen_modernize``, ``gec_dala``,
   ``nordjylland_news_summarization``;
 * extractive QA (exact match + token F1): ``multi_wiki_qa``;
-* ``smoke``: one fixed sample for wiring tests.
+* ``smoke``: one fixed sample for wiring tests;
+* the comparison suites' tasks (``tasks/comparison.py``): ``arc_25shot``, ``mmlu_5shot`` and
+  ``hellaswag_ie_fmt`` / ``math_ie`` in chunks, ``drop``, ``gsm8k``, ``winogrande_ie``,
+  ``govreport_summarization``, ``humaneval_ie`` (execution), ``daisy``, ``ifeval_da``
+  (``tasks/ifeval.py``), ``wmt24pp_en_da``.
 """
 from __future__ import annotations
 
@@ -271,3 +275,6 @@ def inspect_task(spec: TaskSpec):
                       target=s["target"] if isinstance(s["target"], str) else s["target"][0],
                       metadata={"target": s["target"]}) for s in spec.samples]
     return Task(dataset=MemoryDataset(samples, name=spec.name), solver=generate(), scorer=spec_scorer())
+
+
+from mimir_b200.evaluation.tasks import comparison  # noqa: E402,F401  (registers the comparison-suite tasks)
