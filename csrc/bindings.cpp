@@ -78,6 +78,14 @@ at::Tensor router_topk(at::Tensor scores, int64_t k, c10::optional<at::Tensor> l
 // embedding.cu
 at::Tensor embed_fwd(at::Tensor ids, at::Tensor weight, double scale);
 void embed_bwd(at::Tensor dout, at::Tensor sorted_ids, at::Tensor order, at::Tensor grad, double scale);
+at::Tensor branch_read(at::Tensor s, at::Tensor logits, c10::optional<at::Tensor> gain, at::Tensor alpha);
+at::Tensor branch_write(at::Tensor s, at::Tensor u, at::Tensor logits, c10::optional<at::Tensor> gain,
+                        at::Tensor alpha);
+std::vector<at::Tensor> branch_mix_bwd(at::Tensor grad, at::Tensor s, c10::optional<at::Tensor> u, at::Tensor logits,
+                                       c10::optional<at::Tensor> gain, at::Tensor alpha);
+at::Tensor invocation_gate_fwd(at::Tensor pre, at::Tensor inj, at::Tensor bias, at::Tensor alpha);
+std::vector<at::Tensor> invocation_gate_bwd(at::Tensor dout, at::Tensor pre, at::Tensor inj, at::Tensor bias,
+                                            at::Tensor alpha);
 int64_t embed_status(int64_t device);
 // gemm.cu
 at::Tensor gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, c10::optional<at::Tensor> out,
@@ -136,5 +144,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_fwd", &embed_fwd);
   m.def("embed_bwd", &embed_bwd);
   m.def("embed_status", &embed_status);
+  m.def("branch_read", &branch_read);
+  m.def("invocation_gate_fwd", &invocation_gate_fwd);
+  m.def("invocation_gate_bwd", &invocation_gate_bwd);
+  m.def("branch_write", &branch_write);
+  m.def("branch_mix_bwd", &branch_mix_bwd);
   m.def("fmha_bwd", &fmha_bwd);
 }

@@ -9,7 +9,9 @@
 //   dK  += dS^T Q       (M=128 keys, N=128, K=64)            TMEM accumulator
 //   dQ^T = K^T dS^T     (M=128 head dims, N=64 queries, K=128 keys) -> TMEM; the dQ warps
 //          transpose it into a [64 x 128] fp32 smem tile that one TMA reduce-add folds into
-//          the global dQ (L2-side line reductions instead of per-element atomics).
+//          the global dQ (L2-side line reductions instead of per-element atomics: reductions
+//          issued straight from registers, 32 head dims per warp instruction, made the whole
+//          backward 1.68 ms instead of 1.01 ms on the 16k-token bench shape).
 // dK/dV are written once per CTA (bf16, no atomics) because the CTA covers all query heads
 // that share its KV head.  TMEM: S^T 64 + dP^T 64 + dQ^T 64 + dV 128 + dK 128 = 448 columns.
 //

@@ -25,6 +25,7 @@ import torch
 from torch import nn
 
 from mimir_b200.models.transformer import Transformer, TransformerBlock
+from mimir_b200.ops import branches as fused
 
 
 def _fanout(x: torch.Tensor, branches: int) -> torch.Tensor:
@@ -58,10 +59,14 @@ class ResidualConnection(nn.Module):
         return (alpha.float() * logits).softmax(dim=-2)
 
     def read(self, streams, alpha):
+        if fused.fused_supported(streams, alpha):  # one CUDA kernel (ops/branches.py)
+            return fused.branch_read(streams, self.read_logits, getattr(self, "read_gain", None), alpha)
         mixed = (streams.float() * self.weights(streams, alpha, "read")).sum(dim=-2)
         return mixed.to(streams.dtype)
 
     def write(self, streams, update, alpha):
+        if fused.fused_supported(streams, alpha):
+            return fused.branch_write(streams, update, self.write_logits, getattr(self, "write_gain", None), alpha)
         share = self.branches * self.weights(streams, alpha, "write")
         return (streams.float() + share * update.float().unsqueeze(-2)).to(streams.dtype)
 
@@ -139,8 +144,11 @@ class BranchedTransformer(Transformer):
         return streams
 
     def readout(self, streams, stability_diagnostics=None, stability_scope=None):
-        weights = (self.residual_alpha.float() * self.residual_readout.float()).softmax(dim=0)
-        out = self.norm_f((streams.float() * weights).sum(dim=-2).to(streams.dtype))
+        if fused.fused_supported(streams, self.residual_alpha):
+            out = self.norm_f(fused.branch_read(streams, self.residual_readout, None, self.residual_alpha))
+        else:
+            weights = (self.residual_alpha.float() * self.residual_readout.float()).softmax(dim=0)
+            out = self.norm_f((streams.float() * weights).sum(dim=-2).to(streams.dtype))
         if stability_diagnostics is not None:
             stability_diagnostics.record_tensor(f"activation/{stability_scope}/final_norm", out, record_gradient=True)
         return out

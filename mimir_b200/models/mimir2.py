@@ -251,6 +251,9 @@ class InvocationGate(nn.Module):
         self.bias = nn.Parameter(torch.zeros(hidden_size))
 
     def forward(self, hidden, injection, alpha):
+        from mimir_b200.ops import gate as fused
+        if fused.supported(hidden, injection, alpha):  # tcgen05 GEMM + fused bias/tanh/gate kernel
+            return fused.invocation_gate(hidden, injection, self.weight, self.bias, alpha)
         hidden, injection = torch.broadcast_tensors(hidden, injection)
         x = torch.cat((hidden, injection), dim=-1)
         gate = F.linear(x, self.weight.to(x.dtype), self.bias.to(x.dtype))

@@ -179,6 +179,85 @@ def test_ngram_backward_accumulates_into_owned_bf16_gradients():
         _close(t.grad.float()[hit], (0.25 + f.grad[hit]).to(torch.bfloat16).float(), 3e-2, 3e-2, "ngram in place")
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("gain", [False, True])
+def test_branch_mixes_match_torch(dtype, gain):
+    """Fused residual-branch read/write (csrc/branches.cu) against the eager fp32 path: outputs
+    and the gradients of streams, update, logits and gains; the broadcast initial streams too."""
+    import os
+
+    from mimir_b200.models.branches import ResidualConnection, _fanout
+    torch.manual_seed(0)
+    B, d = 3, 320
+    conn = ResidualConnection(B, d, 1, 0.5, input_dependent=gain).cuda()
+    with torch.no_grad():
+        for prm in conn.parameters():
+            prm.normal_(0, 0.5)
+    alpha = torch.tensor(0.7, device="cuda")
+    x0 = torch.randn(2, 33, d, device="cuda").to(dtype)
+    upd = torch.randn(2, 33, d, device="cuda").to(dtype)
+    g_read, g_write = torch.randn(2, 33, d, device="cuda"), torch.randn(2, 33, B, d, device="cuda")
+
+    def run():
+        xs = x0.clone().requires_grad_(True)
+        us = upd.clone().requires_grad_(True)
+        streams = _fanout(xs, B) * 1.5 + 0.1 * torch.arange(B, device="cuda", dtype=dtype)[:, None]
+        read = conn.read(streams, alpha)
+        wrote = conn.write(streams, us, alpha)
+        read0 = conn.read(_fanout(xs, B), alpha)  # a broadcast view (branch stride 0), read in place
+        conn.zero_grad()
+        ((read.float() * g_read).sum() + (wrote.float() * g_write).sum() + (read0.float() * g_read).sum()).backward()
+        grads = [xs.grad, us.grad] + [prm.grad.clone() for prm in conn.parameters()]
+        return [read, wrote, read0] + grads
+
+    fused = run()
+    os.environ["MIMIR_DISABLE_KERNELS"] = "1"
+    try:
+        ref = run()
+    finally:
+        os.environ.pop("MIMIR_DISABLE_KERNELS")
+    tol = 1e-4 if dtype == torch.float32 else 3e-2
+    names = ["read", "write", "read of the broadcast view", "d streams", "d update"] + [
+        n for n, _ in conn.named_parameters()]
+    for a, b, name in zip(fused, ref, names):
+        _close(a, b, tol * max(1.0, float(b.float().abs().max())), tol, name)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_invocation_gate_matches_torch(dtype):
+    """GEMM + fused bias/tanh/gate (ops/gate.py) against the eager path, outputs and gradients."""
+    import os
+
+    from mimir_b200.models.mimir2 import InvocationGate
+    torch.manual_seed(0)
+    d = 256
+    gate = InvocationGate(d).cuda().to(dtype)
+    with torch.no_grad():
+        gate.weight.normal_(0, 0.05)
+        gate.bias.normal_(0, 0.5)
+    alpha = torch.tensor(0.6, device="cuda")
+    h0 = torch.randn(2, 40, d, device="cuda").to(dtype)
+    i0 = torch.randn(2, 40, d, device="cuda").to(dtype)
+    g = torch.randn(2, 40, d, device="cuda")
+
+    def run():
+        h, i = h0.clone().requires_grad_(True), i0.clone().requires_grad_(True)
+        gate.zero_grad()
+        out = gate(h, i, alpha)
+        (out.float() * g).sum().backward()
+        return [out, h.grad, i.grad, gate.weight.grad.clone(), gate.bias.grad.clone()]
+
+    fused = run()
+    os.environ["MIMIR_DISABLE_KERNELS"] = "1"
+    try:
+        ref = run()
+    finally:
+        os.environ.pop("MIMIR_DISABLE_KERNELS")
+    tol = 2e-3 if dtype == torch.float32 else 4e-2
+    for a, b, name in zip(fused, ref, ["out", "d hidden", "d injection", "d weight", "d bias"]):
+        _close(a, b, tol * max(1.0, float(b.float().abs().max())), tol, name)
+
+
 def _packed(lengths, prefixes, heads, kv_heads, seed=0, pad=0):
     g = torch.Generator(device="cuda").manual_seed(seed)
     T = sum(lengths) + pad
