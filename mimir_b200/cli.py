@@ -30,7 +30,7 @@ def _export(args, _rest):
 
 def _serve(args, _rest):
     from mimir_b200.serving.server import serve
-    serve(args.model, args.port, args.gpus, eager=args.eager)
+    serve(args.model, args.port, args.gpus, eager=args.eager, backend=args.backend)
 
 
 def _eval(args, _rest):
@@ -145,6 +145,7 @@ def parser() -> argparse.ArgumentParser:
     sv.add_argument("--port", type=int, default=8000)
     sv.add_argument("--gpus", required=True)
     sv.add_argument("--eager", action="store_true")
+    sv.add_argument("--backend", choices=("vllm", "native"), default="vllm")
     sv.set_defaults(fn=_serve)
     ev = sub.add_parser("eval")
     ev.add_argument("suite", type=Path)

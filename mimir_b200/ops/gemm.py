@@ -132,9 +132,11 @@ class _SwiGLUMLPFn(torch.autograd.Function):
         if not _aligned(dy2):
             dy2 = dy2.contiguous()
         dgu = C.gemm_swiglu_bwd(dy2, w_down, gu)
+        # Every read of a weight is enqueued before its gradient is announced (the replicated
+        # engine may update a block's weights as soon as all of its gradients are announced).
+        dx = mm_nn(dgu, w_gu).view(ctx.x_shape) if ctx.needs_input_grad[0] else None
         d_down = weight_grad(w_down, dy2, h) if ctx.needs_input_grad[2] else None
         d_gu = weight_grad(w_gu, dgu, x2) if ctx.needs_input_grad[1] else None
-        dx = mm_nn(dgu, w_gu).view(ctx.x_shape) if ctx.needs_input_grad[0] else None
         return dx, d_gu, d_down
 
 

@@ -164,10 +164,11 @@ def _expert_backward(dy, xp, gus, expert_rows, weights, dxp, rows_dev=None):
         gu_w, dn_w = weights[2 * i], weights[2 * i + 1]
         if n:
             gu = gus[i]
-            d_dn = _weight_grad(dn_w, dy[s:s + n].t(), _swiglu_fwd(gu))
+            # reads of the expert's weights first, then its gradients (announced to the engine)
             dgu = _swiglu_bwd(gu, dy[s:s + n] @ dn_w)
-            d_gu = _weight_grad(gu_w, dgu.t(), xp[s:s + n])
             torch.matmul(dgu, gu_w, out=dxp[s:s + n])
+            d_dn = _weight_grad(dn_w, dy[s:s + n].t(), _swiglu_fwd(gu))
+            d_gu = _weight_grad(gu_w, dgu.t(), xp[s:s + n])
         else:  # every expert gets a gradient (zero) so all ranks update the same parameters
             d_gu, d_dn = _weight_grad(gu_w, None, None), _weight_grad(dn_w, None, None)
         grads += [d_gu, d_dn]
@@ -189,11 +190,11 @@ def _expert_backward_grouped(dy, xp, gu, expert_rows, weights, dxp, rows_dev):
     act = C.swiglu_fwd(gu)
     # Weight gradients, one grouped launch per projection, accumulated in place: into the
     # engine's gradient views when it owns them, else into fresh zero tensors handed to autograd.
-    targets, out = [], []
+    targets, out, sunk = [], [], []
     for w in weights:
         sink = getattr(w, "_mimir_grad_sink", None)
         if sink is not None and w.grad is not None:
-            sink(w)
+            sunk.append((sink, w))
             targets.append(w.grad)
             out.append(None)
         else:
@@ -202,6 +203,8 @@ def _expert_backward_grouped(dy, xp, gu, expert_rows, weights, dxp, rows_dev):
             out.append(z)
     C.grouped_wgrad(dy, act, list(expert_rows), targets[1::2])
     C.grouped_wgrad(dgu, xp, list(expert_rows), targets[0::2])
+    for sink, w in sunk:  # announced only once the kernels that write them are enqueued
+        sink(w)
     return out
 
 

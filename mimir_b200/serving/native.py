@@ -1,0 +1,157 @@
+"""Native OpenAI-compatible serving of exported Mimir2 models (no vLLM).
+
+The vLLM server that the reference launches (``src/mimir/serving/server.py:12-75``) needs its
+patched vLLM fork (``patches/vllm.patch``) to know Mimir2.  This server instead loads the export
+with this framework's Transformers model (:mod:`mimir_b200.export.transformers_mimir2`), which
+serves every configuration the exporter writes, including looped recurrence, exactly as trained:
+the prompt is the prefix-LM prefix (its tokens see each other), generation is causal with a
+per-invocation KV cache.
+
+Endpoints (the subset the evaluation runner and the serving pool use):
+
+* ``GET  /health``, ``GET /v1/models``
+* ``POST /v1/chat/completions`` (``messages``; the export's chat template; ``chat_template_kwargs``)
+* ``POST /v1/completions`` (``prompt``)
+
+Request fields: ``max_tokens``, ``temperature`` (0 = greedy), ``top_p``, ``stop``, ``seed``.
+Requests are served one at a time (one model, one device); the HTTP server accepts concurrent
+connections and queues them.
+
+Usage: ``python -m mimir_b200.serving.native MODEL_DIR [--port 8000] [--device cuda:0]``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import threading
+import time
+import uuid
+from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
+from pathlib import Path
+from typing import Optional
+
+import torch
+
+
+class Engine:
+    """Tokenizer + model + a lock; ``complete`` returns ``(text, prompt_tokens, completion_tokens,
+    finish_reason)``."""
+
+    def __init__(self, model_dir, device: str = "cpu", dtype: Optional[torch.dtype] = None, name: Optional[str] = None):
+        from transformers import AutoModelForCausalLM, AutoTokenizer
+
+        from mimir_b200.export.transformers_mimir2 import register
+        register()
+        self.name = name or Path(model_dir).name
+        self.device = torch.device(device)
+        self.tokenizer = AutoTokenizer.from_pretrained(model_dir, local_files_only=True)
+        kwargs = {"dtype": dtype} if dtype is not None else {}
+        self.model = AutoModelForCausalLM.from_pretrained(model_dir, local_files_only=True, **kwargs).to(self.device)
+        self.model.eval()
+        self.lock = threading.Lock()
+
+    def prompt_ids(self, body: dict, chat: bool) -> list[int]:
+        if chat:
+            kw = dict(body.get("chat_template_kwargs") or {})
+            text = self.tokenizer.apply_chat_template(body["messages"], tokenize=False, add_generation_prompt=True, **kw)
+            return self.tokenizer(text, add_special_tokens=False)["input_ids"]
+        prompt = body["prompt"]
+        if isinstance(prompt, list) and prompt and isinstance(prompt[0], int):
+            return list(prompt)
+        return self.tokenizer(prompt if isinstance(prompt, str) else prompt[0])["input_ids"]
+
+    @torch.no_grad()
+    def complete(self, ids: list[int], body: dict) -> tuple[str, int, int, str]:
+        max_tokens = int(body.get("max_tokens") or body.get("max_completion_tokens") or 16)
+        temperature = float(body.get("temperature") or 0.0)
+        stops = body.get("stop") or []
+        stops = [stops] if isinstance(stops, str) else list(stops)
+        gen = dict(max_new_tokens=max_tokens, do_sample=temperature > 0, pad_token_id=self.tokenizer.pad_token_id
+                   if self.tokenizer.pad_token_id is not None else self.tokenizer.eos_token_id)
+        if temperature > 0:
+            gen.update(temperature=temperature, top_p=float(body.get("top_p") or 1.0))
+        if self.tokenizer.eos_token_id is not None:
+            gen["eos_token_id"] = self.tokenizer.eos_token_id
+        with self.lock:
+            if body.get("seed") is not None:
+                torch.manual_seed(int(body["seed"]))
+            x = torch.tensor([ids], device=self.device)
+            out = self.model.generate(x, attention_mask=torch.ones_like(x), **gen)
+        new = out[0, len(ids):].tolist()
+        finish = "length" if len(new) >= max_tokens else "stop"
+        text = self.tokenizer.decode(new, skip_special_tokens=True)
+        for s in stops:
+            cut = text.find(s)
+            if s and cut >= 0:
+                text, finish = text[:cut], "stop"
+        return text, len(ids), len(new), finish
+
+
+def _handler(engine: Engine):
+    class Handler(BaseHTTPRequestHandler):
+        protocol_version = "HTTP/1.1"
+
+        def log_message(self, fmt, *args):  # quiet by default
+            pass
+
+        def _send(self, code: int, payload: dict) -> None:
+            data = json.dumps(payload).encode()
+            self.send_response(code)
+            self.send_header("Content-Type", "application/json")
+            self.send_header("Content-Length", str(len(data)))
+            self.end_headers()
+            self.wfile.write(data)
+
+        def do_GET(self):
+            if self.path == "/health":
+                self._send(200, {"status": "ok"})
+            elif self.path == "/v1/models":
+                self._send(200, {"object": "list", "data": [{"id": engine.name, "object": "model",
+                                                             "owned_by": "mimir_b200"}]})
+            else:
+                self._send(404, {"error": {"message": f"unknown path {self.path}"}})
+
+        def do_POST(self):
+            try:
+                body = json.loads(self.rfile.read(int(self.headers.get("Content-Length", 0))) or b"{}")
+                chat = self.path == "/v1/chat/completions"
+                if not chat and self.path != "/v1/completions":
+                    return self._send(404, {"error": {"message": f"unknown path {self.path}"}})
+                if body.get("stream"):
+                    return self._send(400, {"error": {"message": "streaming is not supported"}})
+                ids = engine.prompt_ids(body, chat)
+                text, n_in, n_out, finish = engine.complete(ids, body)
+            except (KeyError, ValueError, TypeError) as exc:
+                return self._send(400, {"error": {"message": str(exc)}})
+            usage = {"prompt_tokens": n_in, "completion_tokens": n_out, "total_tokens": n_in + n_out}
+            base = {"id": f"cmpl-{uuid.uuid4().hex}", "created": int(time.time()), "model": engine.name,
+                    "usage": usage}
+            if chat:
+                self._send(200, base | {"object": "chat.completion", "choices": [
+                    {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": finish}]})
+            else:
+                self._send(200, base | {"object": "text_completion", "choices": [
+                    {"index": 0, "text": text, "finish_reason": finish}]})
+    return Handler
+
+
+def make_server(engine: Engine, host: str = "127.0.0.1", port: int = 8000) -> ThreadingHTTPServer:
+    return ThreadingHTTPServer((host, port), _handler(engine))
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description="OpenAI-compatible server for an exported Mimir2 model")
+    ap.add_argument("model", type=Path)
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--device", default="cuda:0" if torch.cuda.is_available() else "cpu")
+    ap.add_argument("--dtype", choices=["float32", "bfloat16"], default=None)
+    args = ap.parse_args(argv)
+    engine = Engine(args.model, args.device, getattr(torch, args.dtype) if args.dtype else None)
+    server = make_server(engine, args.host, args.port)
+    print(f"serving {engine.name} on http://{args.host}:{args.port}/v1", flush=True)
+    server.serve_forever()
+
+
+if __name__ == "__main__":
+    main()

@@ -5,6 +5,9 @@ Reference behaviour: ``src/mimir/serving/server.py:12-75``.
 * ``command(spec)`` validates the export (``model_type == "mimir2"``, hierarchical recurrence,
   no persistent-H / branch-specific L mixing; sparse MoS only in eager mode; explicit numeric
   GPU indices) and builds the OpenAI server argv: loopback host, tensor parallel = #GPUs.
+  ``backend="native"`` launches :mod:`mimir_b200.serving.native` instead (this framework's
+  Transformers model behind an OpenAI-compatible endpoint, one GPU): it serves every exported
+  configuration, looped recurrence included, with the prompt as the prefix-LM prefix.
 * ``ServerPool`` keys servers by SHA-256 of the export receipt, the chat template and the
   spec, so a server is reused only for an identical model/template/launch; it owns each
   server's process group and tears it down (TERM, then KILL after 30 s).
@@ -32,6 +35,7 @@ class ServerSpec:
     eager: bool = False
     max_model_len: Optional[int] = None
     template: Optional[str] = None
+    backend: str = "vllm"  # or "native"
 
     def key(self) -> str:
         receipt = (Path(self.model) / "export_receipt.json").read_bytes()
@@ -43,6 +47,14 @@ def command(spec: ServerSpec) -> list[str]:
     cfg = json.loads((Path(spec.model) / "config.json").read_text())
     if cfg.get("model_type") != "mimir2":
         raise ValueError("Only Mimir2 can be served")
+    if spec.backend == "native":
+        if not spec.gpus or len(spec.gpus.split(",")) != 1 or not spec.gpus.isdigit():
+            raise ValueError("The native server runs on exactly one explicit GPU index")
+        # CUDA_VISIBLE_DEVICES (set by the launcher) makes the chosen GPU cuda:0.
+        return [sys.executable, "-m", "mimir_b200.serving.native", spec.model, "--host", "127.0.0.1",
+                "--port", str(spec.port), "--device", "cuda:0", "--dtype", "bfloat16"]
+    if spec.backend != "vllm":
+        raise ValueError(f"unknown serving backend {spec.backend!r}")
     if cfg.get("recurrence_mode", "hierarchical") != "hierarchical":
         raise ValueError("Looped recurrence is not supported by the inference integrations")
     if cfg.get("h_residual_persistence") or cfg.get("h_branch_l_mixing"):
@@ -62,8 +74,8 @@ def command(spec: ServerSpec) -> list[str]:
     return args
 
 
-def serve(model, port: int, gpus: str, *, eager: bool = False) -> None:
-    spec = ServerSpec(str(model), gpus, port, eager)
+def serve(model, port: int, gpus: str, *, eager: bool = False, backend: str = "vllm") -> None:
+    spec = ServerSpec(str(model), gpus, port, eager, backend=backend)
     subprocess.run(command(spec), env=os.environ | {"CUDA_VISIBLE_DEVICES": gpus}, check=True)
 
 
@@ -91,7 +103,7 @@ class ServerPool:
         deadline = time.monotonic() + timeout
         while time.monotonic() < deadline:
             if proc.poll() is not None:
-                raise RuntimeError("Owned vLLM server exited; inspect its log")
+                raise RuntimeError("Owned inference server exited; inspect its log")
             try:
                 with urllib.request.urlopen(f"http://127.0.0.1:{spec.port}/health", timeout=1):
                     return url

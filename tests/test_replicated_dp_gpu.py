@@ -322,3 +322,44 @@ def test_multi_gpu_overlapped_update_equals_closing_update(tmp_path):
             assert torch.equal(a, b)
     for r in range(1, world):
         assert torch.equal(ranks[r][1][3], ranks[0][1][3])  # every replica holds the same weights
+
+
+def test_overlapped_update_is_bit_identical_in_the_training_step():
+    """The real model on the tcgen05 kernels, trained through ``train_accumulated_batches`` with
+    the update overlapped with the backward and without: the master weights, moments and EMA
+    must match bit for bit (any weight read racing its bucket's update would show here)."""
+    import sys
+    sys.path.insert(0, os.path.dirname(__file__))
+    from test_reference_losses_gpu import MODEL, OPTIM, SEQ, SEQS, _batches, _on
+
+    from mimir_b200.config.schema import PretrainConfig
+    from mimir_b200.models import LMHead, Mimir2
+    from mimir_b200.models.common import wrap_tensor
+    from mimir_b200.optim.schedules import update_lr
+    from mimir_b200.parallel.replicated import ReplicatedAdamATan2, wrap_replicated
+    from mimir_b200.train.setup import make_train_state
+    from mimir_b200.train.steps import train_accumulated_batches
+    dev = torch.device("cuda", 0)
+    arch = {k: v for k, v in MODEL.items() if k not in ("vocab_size", "max_seq_len", "fwd_bwd_dtype")}
+    config = PretrainConfig(arch=arch, data=dict(path="synthetic"), global_batch_size=SEQ * SEQS,
+                            distributed_strategy="replicated", **OPTIM)
+    batches = _batches()
+    runs = []
+    for enabled in (False, True):
+        torch.manual_seed(0)
+        model = LMHead(Mimir2(MODEL), MODEL).to(dev)
+        engine = wrap_replicated(model, dev, torch.bfloat16)
+        engine.overlap_enabled = enabled
+        optim = ReplicatedAdamATan2(engine, lr=0.0, betas=(0.9, 0.95), weight_decay=0.1, ema=0.999,
+                                    ema_dtype=torch.float32)
+        state = make_train_state(config, model, None, optim, total_steps=10_000, device=dev)
+        for i in range(6):
+            state.step += 1
+            update_lr(config, state)
+            train_accumulated_batches(config, 0, state, [_on(dev, batches[i % 2], wrap_tensor)])
+        torch.cuda.synchronize()
+        assert engine.overlap_ready is (True if enabled else None)
+        runs.append((engine.master.clone(), optim.exp_avg_sq.clone(), optim.ema.clone()))
+        engine.close()
+    for a, b in zip(*runs):
+        assert torch.equal(a, b)
