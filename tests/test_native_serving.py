@@ -1,0 +1,74 @@
+"""Native OpenAI-compatible serving of an export (``mimir_b200.serving.native``), CPU: the HTTP
+endpoints answer in the OpenAI schema and the greedy completion equals the Transformers model's
+own ``generate`` on the same prompt (prompt = prefix-LM prefix)."""
+import json
+import threading
+import urllib.request
+
+import pytest
+import torch
+
+pytest.importorskip("transformers")
+
+
+def _tokenizer(path):
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+    vocab = {f"w{i}": i for i in range(90)} | {"<unk>": 90, "<s>": 91, "</s>": 92, "user": 93, "assistant": 94, ":": 95}
+    tok = Tokenizer(models.WordLevel(vocab, unk_token="<unk>"))
+    tok.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
+    fast = PreTrainedTokenizerFast(tokenizer_object=tok, unk_token="<unk>", bos_token="<s>", eos_token="</s>")
+    fast.chat_template = ("{% for m in messages %}{{ m['role'] }} : {{ m['content'] }} {% endfor %}"
+                          "{% if add_generation_prompt %}assistant : {% endif %}")
+    fast.save_pretrained(path)
+
+
+def _post(url, body):
+    req = urllib.request.Request(url, data=json.dumps(body).encode(), headers={"Content-Type": "application/json"})
+    with urllib.request.urlopen(req, timeout=60) as r:
+        return json.loads(r.read())
+
+
+def test_native_server_answers_like_generate(tmp_path):
+    from test_transformers_model import _export
+
+    from mimir_b200.serving.native import Engine, make_server
+    _export(tmp_path, {})
+    _tokenizer(tmp_path)
+    engine = Engine(tmp_path, "cpu", name="tiny")
+    server = make_server(engine, "127.0.0.1", 0)
+    thread = threading.Thread(target=server.serve_forever, daemon=True)
+    thread.start()
+    base = f"http://127.0.0.1:{server.server_address[1]}"
+    try:
+        with urllib.request.urlopen(base + "/health", timeout=10) as r:
+            assert json.loads(r.read()) == {"status": "ok"}
+        with urllib.request.urlopen(base + "/v1/models", timeout=10) as r:
+            assert json.loads(r.read())["data"][0]["id"] == "tiny"
+        chat = _post(base + "/v1/chat/completions", {"model": "tiny", "max_tokens": 4, "temperature": 0,
+                                                     "messages": [{"role": "user", "content": "w1 w2 w3"}]})
+        assert chat["object"] == "chat.completion" and chat["choices"][0]["message"]["role"] == "assistant"
+        assert chat["usage"]["completion_tokens"] <= 4
+        ids = engine.prompt_ids({"messages": [{"role": "user", "content": "w1 w2 w3"}]}, chat=True)
+        out = engine.model.generate(torch.tensor([ids]), max_new_tokens=4, do_sample=False, pad_token_id=92,
+                                    eos_token_id=92)
+        expected = engine.tokenizer.decode(out[0, len(ids):].tolist(), skip_special_tokens=True)
+        assert chat["choices"][0]["message"]["content"] == expected
+        text = _post(base + "/v1/completions", {"prompt": "w5 w6", "max_tokens": 3})
+        assert text["object"] == "text_completion" and isinstance(text["choices"][0]["text"], str)
+        with pytest.raises(urllib.error.HTTPError):
+            _post(base + "/v1/completions", {"prompt": "w5", "stream": True})
+    finally:
+        server.shutdown()
+        server.server_close()
+
+
+def test_native_backend_command(tmp_path):
+    from mimir_b200.serving.server import ServerSpec, command
+    (tmp_path / "config.json").write_text(json.dumps({"model_type": "mimir2", "recurrence_mode": "looped"}))
+    argv = command(ServerSpec(str(tmp_path), "3", 8123, backend="native"))
+    assert argv[1:4] == ["-m", "mimir_b200.serving.native", str(tmp_path)] and "8123" in argv
+    with pytest.raises(ValueError, match="exactly one"):
+        command(ServerSpec(str(tmp_path), "0,1", backend="native"))
+    with pytest.raises(ValueError, match="Looped"):  # the vLLM command keeps its own limits
+        command(ServerSpec(str(tmp_path), "0"))
