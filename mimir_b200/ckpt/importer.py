@@ -35,10 +35,19 @@ def _is_mimir(arch: dict) -> bool:
     return name in ("mimir2", "legacy_v1") or "hrm" in name.lower() or "mimir" in name.lower()
 
 
+def _unwrapped(tensors: dict) -> dict:
+    """Model keys without the DDP wrapper's ``module.`` prefix: a run under DDP checkpoints its
+    wrapped model (as the reference does), and initialisation reads it into an unwrapped model."""
+    if tensors and all(k.startswith("module.") for k in tensors):
+        return {k.removeprefix("module."): v for k, v in tensors.items()}
+    return tensors
+
+
 def _load_model_tensors(source: Path, tag: str) -> dict:
+    source = Path(source)
     unsharded = source / f"unsharded_{tag}.pt"
     if unsharded.is_file():
-        return dict(torch.load(unsharded, map_location="cpu", weights_only=False)["model"])
+        return _unwrapped(dict(torch.load(unsharded, map_location="cpu", weights_only=False)["model"]))
     sharded = source / f"fsdp2_{tag}"
     if sharded.is_dir():
         import torch.distributed.checkpoint as dcp
@@ -48,7 +57,7 @@ def _load_model_tensors(source: Path, tag: str) -> dict:
                   for key, m in meta.state_dict_metadata.items()
                   if key.startswith("model.") and isinstance(m, TensorStorageMetadata)}
         dcp.load(wanted, checkpoint_id=str(sharded), no_dist=True)
-        return {key.removeprefix("model."): value for key, value in wanted.items()}
+        return _unwrapped({key.removeprefix("model."): value for key, value in wanted.items()})
     raise FileNotFoundError(f"No unsharded_{tag}.pt or fsdp2_{tag}/ in {source}")
 
 

@@ -343,6 +343,31 @@ def test_fmha_backward(lengths, prefixes, H, KV, causal):
         _close(a[:total] / scale, b[:total] / scale, 2e-2, 0.0, f"fmha bwd {name}")
 
 
+def test_fmha_padding_rows_do_not_leak():
+    """Sentinels in the padding rows after the last sequence (q, k, v and the output gradient):
+    the outputs and gradients of the valid rows are finite and bit-identical to a run with zero
+    padding, so masked keys and queries contribute exact zeros.  The sentinel is a large finite
+    value, not NaN: the last sequence's 128-row tiles extend into the padding by design, and a
+    NaN there would pass through a tile-wide MMA even with a probability of zero."""
+    lengths, prefixes, H, KV = [300, 129, 513], [100, 129, 0], 4, 2
+    total = sum(lengths)
+    runs = []
+    for poison in (False, True):
+        q, k, v, meta = _packed(lengths, prefixes, H, KV, pad=70, seed=5)
+        for t in (q, k, v):
+            t[total:] = 1.0e4 if poison else 0.0
+        q, k, v = (t.detach().requires_grad_(True) for t in (q, k, v))
+        out = ops.prefixlm_attention(q, k, v, False, **meta)
+        g = torch.randn(out.shape, device="cuda", generator=torch.Generator(device="cuda").manual_seed(6)).to(out.dtype)
+        g[total:] = 1.0e4 if poison else 0.0
+        out.backward(g)
+        runs.append([out[:total], q.grad[:total], k.grad[:total], v.grad[:total]])
+    assert ops.ext().fmha_status(torch.device("cuda", 0)) == 0
+    for a, b, name in zip(runs[0], runs[1], ["out", "dq", "dk", "dv"]):
+        assert bool(torch.isfinite(b.float()).all()), name
+        assert torch.equal(a, b), name
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_scaled_embedding_matches_torch(dtype):
     """Fused gather + scale forward and the sorted, deterministic backward (repeated ids included)."""

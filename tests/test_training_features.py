@@ -216,3 +216,31 @@ def test_compiled_step_matches_eager():
             steps.train_accumulated_batches(cfg_c, 0, st, b, use_compiled=True, bp_steps=3)
     for n, p in st.model.named_parameters():
         torch.testing.assert_close(p.detach(), eager[n], rtol=1e-5, atol=1e-6, msg=n)
+
+
+def test_upcycling_reads_a_ddp_checkpoint(tmp_path):
+    """A dense run under DDP checkpoints its wrapped model (``module.`` keys, as the reference
+    does); ``initialize_from`` with upcycling must read it into the unwrapped expert model."""
+    import os
+    import subprocess
+    import sys
+
+    from mimir_b200.ckpt.importer import _load_model_tensors
+    from mimir_b200.data.synthetic import write_corpus
+    corpus = write_corpus(str(tmp_path / "data"), rows=32, seq_len=64, vocab=256, min_prefix=1, max_prefix=1)
+    base = ["size@arch=XXS", "arch.hidden_size=64", "arch.n_layers=2", "accelerator_type=cpu",
+            "fwd_bwd_dtype=float32", "compile_train_batch=false", f"data.path={corpus}", "global_batch_size=256",
+            "epochs=1"]
+    env = os.environ | {"RANK": "0", "WORLD_SIZE": "1", "LOCAL_RANK": "0", "MASTER_ADDR": "127.0.0.1",
+                        "MASTER_PORT": "29961"}
+    subprocess.run([sys.executable, "-m", "mimir_b200", "train", *base, "distributed_strategy=ddp",
+                    f"checkpoint_path={tmp_path / 'dense'}", "stop_after_step=2", "checkpoint_step_interval=2"],
+                   env=env, check=True)
+    keys = list(_load_model_tensors(tmp_path / "dense" / "step_2", "step_2"))
+    assert keys and not any(k.startswith("module.") for k in keys) and "model.zL_init" in keys
+    from mimir_b200.config.schema import load_config
+    from mimir_b200.train.loop import launch
+    launch(load_config(base + ["distributed_strategy=none", f"checkpoint_path={tmp_path / 'moe'}",
+                               f"initialize_from={tmp_path / 'dense' / 'step_2'}", "arch.upcycle_from_dense=true",
+                               "arch.moe_num_experts=4", "arch.moe_top_k=2", "arch.residual_branches=2",
+                               "stop_after_step=1"]))
