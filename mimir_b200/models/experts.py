@@ -205,7 +205,7 @@ class MLPMixture(nn.Module):
             idx = plan.indices(i)
             y = expert(flat.index_select(0, idx), stability_diagnostics=diagnostics if idx.numel() else None,
                        stability_scope=f"{scope}/expert_{i}" if scope else None)
-            out = out.index_add(0, idx, y * w[idx, i, None].to(y.dtype))
+            out = out.index_add(0, idx, (y * w[idx, i, None].to(y.dtype)).to(out.dtype))  # autocast: y may be bf16
         return out.reshape_as(x)
 
 
