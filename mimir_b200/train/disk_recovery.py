@@ -10,7 +10,10 @@ Reference behaviour: ``src/mimir/training/disk_recovery.py:10-44``.
   ``<control>/hold`` exists, runs the training child, and on status 75 validates the
   published checkpoint (manifest step must equal the ready step) and relaunches with
   ``resume_checkpoint_path``/``resume_checkpoint_tag``.  Status 0 ends; any other status
-  raises (failures are surfaced, never retried endlessly).
+  raises (failures are surfaced, never retried endlessly).  A launcher child (``command=``,
+  e.g. torchrun over several ranks) reports a worker's status 75 as a failure of its own, so a
+  non-zero status also counts as a suspension when this attempt wrote a new
+  ``disk-ready.json`` for a later step than the one it resumed from.
 """
 from __future__ import annotations
 
@@ -45,6 +48,19 @@ class DiskHook:
         raise SystemExit(SUSPEND_EXIT_CODE)
 
 
+def _ready_stamp(root: Path) -> Optional[tuple]:
+    ready = root / "disk-ready.json"
+    if not ready.exists():
+        return None
+    return ready.stat().st_mtime_ns, json.loads(ready.read_text()).get("step")
+
+
+def _suspended_now(root: Path, before: Optional[tuple]) -> bool:
+    """The attempt that just ended wrote a new ready record for a later step."""
+    now = _ready_stamp(root)
+    return now is not None and now != before and (before is None or (now[1] or 0) > (before[1] or 0))
+
+
 def _child_command(args: Sequence[str]) -> list[str]:
     return [sys.executable, "-m", "mimir_b200", "train", *args]
 
@@ -63,10 +79,11 @@ def supervise(overrides: Sequence[str], config, command: Optional[Sequence[str]]
         while True:
             while (root / "hold").exists():
                 time.sleep(poll_seconds)
+            before = _ready_stamp(root)
             status = subprocess.run(make(args)).returncode
             if status == 0:
                 return
-            if status != SUSPEND_EXIT_CODE:
+            if status != SUSPEND_EXIT_CODE and not _suspended_now(root, before):
                 raise RuntimeError(f"Training failed with status {status}")
             ready = json.loads((root / "disk-ready.json").read_text())
             directory = Path(ready["checkpoint"]).parent  # the sidecar JSON inside the tag directory

@@ -61,12 +61,18 @@ def _add_metrics(total, metrics):
 
 
 def supervised_token_count(config, rank: int, batch: dict) -> Tensor:
-    count = (batch["labels"] != IGNORE_LABEL_ID).sum().to(torch.float32)
+    return supervised_token_counts(config, rank, [batch])[0]
+
+
+def supervised_token_counts(config, rank: int, batches: list) -> list[Tensor]:
+    """Supervised-token count of every micro-batch, averaged over the ranks in ONE all-reduce
+    (the reference issues one per micro-batch, ``src/mimir/training/steps.py:66-76``)."""
+    counts = torch.stack([(b["labels"] != IGNORE_LABEL_ID).sum().to(torch.float32) for b in batches])
     if dist.is_available() and dist.is_initialized():
         trace_print(config, rank, "supervised_count_all_reduce_begin")
-        dist.all_reduce(count, op=dist.ReduceOp.AVG)
+        dist.all_reduce(counts, op=dist.ReduceOp.AVG)
         trace_print(config, rank, "supervised_count_all_reduce_end")
-    return count
+    return list(counts.unbind(0))
 
 
 def train_accumulated_batches(config, rank: int, train_state, batches: list, use_compiled: bool = False,
@@ -114,7 +120,7 @@ def _accumulate_and_step(config, rank: int, train_state, batches: list, use_comp
     trace_print(config, rank, f"train_accumulated_begin step={train_state.step} microbatches={len(batches)}")
     if config.gradient_skip_norm is not None and train_state.carry is not None:
         raise RuntimeError("gradient_skip_norm currently supports only models with no persistent carry")
-    counts = [supervised_token_count(config, rank, b) for b in batches]
+    counts = supervised_token_counts(config, rank, batches)
     total = torch.stack(counts).sum().clamp_min(1.0)
     step_fn = compiled_forward_backward(config.compile_train_batch_mode) if use_compiled else forward_backward_batch
     train_state.optim.zero_grad()

@@ -113,3 +113,34 @@ def test_disk_suspension_restarts_to_identical_state(corpus, tmp_path):
     ready = json.loads((control / "disk-ready.json").read_text())
     assert ready["step"] == 3
     _same_state(full, susp, "step_6")
+
+
+# A launcher that, like torchrun, reports any non-zero worker status as its own status 1.
+_MASKING_LAUNCHER = ("import subprocess, sys; "
+                     "r = subprocess.run([sys.executable, '-m', 'mimir_b200', 'train', *sys.argv[1:]]).returncode; "
+                     "sys.exit(1 if r else 0)")
+
+
+def test_disk_suspension_through_a_launcher_that_masks_the_status(corpus, tmp_path):
+    """Under a launcher the worker's status 75 arrives as 1; the new ready record tells the
+    supervisor it was a suspension (two of them here), and the run ends in the same state."""
+    from mimir_b200.train.disk_recovery import supervise
+    full, susp = tmp_path / "full", tmp_path / "susp"
+    _train(corpus, full, "stop_after_step=6")
+    overrides = BASE + [f"data.path={corpus}", f"checkpoint_path={susp}", "stop_after_step=6",
+                        "suspend_after_steps=[2,4]"]
+    control = (susp / "control").resolve()
+    config = load_config(overrides + [f"suspend_control_dir={control}"])
+    supervise(overrides, config, command=[sys.executable, "-c", _MASKING_LAUNCHER])
+    assert json.loads((control / "disk-ready.json").read_text())["step"] == 4
+    _same_state(full, susp, "step_6")
+
+
+def test_launcher_failure_without_a_new_ready_record_raises(corpus, tmp_path):
+    from mimir_b200.train.disk_recovery import supervise
+    run = tmp_path / "r"
+    overrides = BASE + [f"data.path={corpus}", f"checkpoint_path={run}", "stop_after_step=2", "lr=-1"]
+    control = (run / "control").resolve()
+    config = load_config([o for o in overrides if o != "lr=-1"] + [f"suspend_control_dir={control}"])
+    with pytest.raises(RuntimeError, match="Training failed with status 1"):
+        supervise(overrides, config, command=[sys.executable, "-c", _MASKING_LAUNCHER])
