@@ -86,6 +86,8 @@ std::vector<at::Tensor> branch_mix_bwd(at::Tensor grad, at::Tensor s, c10::optio
 at::Tensor invocation_gate_fwd(at::Tensor pre, at::Tensor inj, at::Tensor bias, at::Tensor alpha);
 std::vector<at::Tensor> invocation_gate_bwd(at::Tensor dout, at::Tensor pre, at::Tensor inj, at::Tensor bias,
                                             at::Tensor alpha);
+at::Tensor goldfish_mask(at::Tensor inputs, at::Tensor supervised, at::Tensor cu_seqlens, int64_t k,
+                         int64_t context_width, int64_t seed, std::vector<int64_t> mix);
 int64_t embed_status(int64_t device);
 // gemm.cu
 at::Tensor gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, c10::optional<at::Tensor> out,
@@ -145,6 +147,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd", &embed_bwd);
   m.def("embed_status", &embed_status);
   m.def("branch_read", &branch_read);
+  m.def("goldfish_mask", &goldfish_mask);
   m.def("invocation_gate_fwd", &invocation_gate_fwd);
   m.def("invocation_gate_bwd", &invocation_gate_bwd);
   m.def("branch_write", &branch_write);

@@ -58,6 +58,17 @@ def _splitmix(x: Tensor) -> Tensor:
 
 def goldfish_drop_mask(inputs: Tensor, supervised: Tensor, cu_seqlens: Tensor, k: int, context_width: int,
                        seed: int) -> Tensor:
+    from mimir_b200.ops._ext import ext, kernels_enabled
+    if kernels_enabled(inputs) and inputs.dim() == 1 and cu_seqlens.dtype == torch.int32:
+        # One CUDA kernel (csrc/goldfish.cu): same int64 arithmetic, no host synchronisation.
+        return ext().goldfish_mask(inputs.contiguous(), supervised.contiguous(), cu_seqlens.contiguous(), k,
+                                   context_width, seed, [_signed(v) for v in _MIX_CONSTANTS + _SPLITMIX])
+    return goldfish_drop_mask_reference(inputs, supervised, cu_seqlens, k, context_width, seed)
+
+
+def goldfish_drop_mask_reference(inputs: Tensor, supervised: Tensor, cu_seqlens: Tensor, k: int,
+                                 context_width: int, seed: int) -> Tensor:
+    """The PyTorch formulation (one vectorised pass per context offset and sequence)."""
     c_tok, c_pos, c_seed, c_off = (torch.tensor(_signed(v), dtype=torch.int64, device=inputs.device)
                                    for v in _MIX_CONSTANTS)
     bounds = cu_seqlens.detach().cpu().tolist()

@@ -9,7 +9,8 @@ Reference behaviour: ``src/mimir/training/disk_recovery.py:10-44``.
 * ``supervise`` owns recovery under ``<control>/recovery.lock``: it waits while
   ``<control>/hold`` exists, runs the training child, and on status 75 validates the
   published checkpoint (manifest step must equal the ready step) and relaunches with
-  ``resume_checkpoint_path``/``resume_checkpoint_tag``.  Status 0 ends; any other status
+  ``resume_checkpoint_path``/``resume_checkpoint_tag`` (dropping ``initialize_from``, which only
+  applies to the first start).  Status 0 ends; any other status
   raises (failures are surfaced, never retried endlessly).  A launcher child (``command=``,
   e.g. torchrun over several ranks) reports a worker's status 75 as a failure of its own, so a
   non-zero status also counts as a suspension when this attempt wrote a new
@@ -91,4 +92,7 @@ def supervise(overrides: Sequence[str], config, command: Optional[Sequence[str]]
             if manifest["step"] != ready["step"]:
                 raise ValueError("Recovery step mismatch")
             resume = {"resume_checkpoint_path": str(directory), "resume_checkpoint_tag": manifest["tag"]}
-            args = [a for a in args if a.split("=", 1)[0] not in resume] + [f"{k}={v}" for k, v in resume.items()]
+            # The checkpoint holds everything now; a first start's weight initialisation must not
+            # be repeated (and the two are mutually exclusive in the config).
+            dropped = set(resume) | {"initialize_from"}
+            args = [a for a in args if a.split("=", 1)[0] not in dropped] + [f"{k}={v}" for k, v in resume.items()]

@@ -258,6 +258,21 @@ def test_invocation_gate_matches_torch(dtype):
         _close(a, b, tol * max(1.0, float(b.float().abs().max())), tol, name)
 
 
+@pytest.mark.parametrize("dtype", [torch.int32, torch.int64])
+def test_goldfish_kernel_matches_torch_bit_for_bit(dtype):
+    from mimir_b200.models.goldfish import goldfish_drop_mask, goldfish_drop_mask_reference
+    g = torch.Generator(device="cuda").manual_seed(7)
+    T = 3000
+    inputs = torch.randint(0, 65536, (T,), device="cuda", generator=g, dtype=dtype)
+    supervised = torch.rand(T, device="cuda", generator=g) > 0.2
+    cu = torch.tensor([0, 5, 5, 700, 701, 2100, 2999] + [0] * 9, device="cuda", dtype=torch.int32)  # padded bounds
+    for k, w, seed in ((2, 50, 0), (3, 7, 12345), (50, 50, 2 ** 40 + 3)):
+        ours = goldfish_drop_mask(inputs, supervised, cu, k, w, seed)
+        ref = goldfish_drop_mask_reference(inputs, supervised, cu, k, w, seed)
+        assert torch.equal(ours, ref), (k, w, seed)
+        assert bool(ours.any()) and not bool(ours[2999:].any())
+
+
 def _packed(lengths, prefixes, heads, kv_heads, seed=0, pad=0):
     g = torch.Generator(device="cuda").manual_seed(seed)
     T = sum(lengths) + pad

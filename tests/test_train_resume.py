@@ -144,3 +144,18 @@ def test_launcher_failure_without_a_new_ready_record_raises(corpus, tmp_path):
     config = load_config([o for o in overrides if o != "lr=-1"] + [f"suspend_control_dir={control}"])
     with pytest.raises(RuntimeError, match="Training failed with status 1"):
         supervise(overrides, config, command=[sys.executable, "-c", _MASKING_LAUNCHER])
+
+
+def test_suspended_run_started_from_initialize_from_resumes(corpus, tmp_path):
+    """A suspendable run that starts from ``initialize_from`` resumes from its own checkpoint
+    (the initialisation is not repeated, and the config would reject both at once)."""
+    from mimir_b200.train.disk_recovery import supervise
+    _train(corpus, tmp_path / "src", "stop_after_step=2")
+    run = tmp_path / "r"
+    overrides = BASE + [f"data.path={corpus}", f"checkpoint_path={run}", "stop_after_step=4",
+                        "suspend_after_steps=[3]", f"initialize_from={tmp_path / 'src' / 'step_2'}"]
+    control = (run / "control").resolve()
+    config = load_config(overrides + [f"suspend_control_dir={control}"])
+    supervise(overrides, config, command=[sys.executable, "-m", "mimir_b200", "train"])
+    assert json.loads((control / "disk-ready.json").read_text())["step"] == 3
+    assert (run / "step_4").is_dir()
