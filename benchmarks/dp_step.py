@@ -14,7 +14,8 @@ slower of the HBM bytes at the measured copy bandwidth and the NVLink bytes at t
 ``--optimizer muon`` builds the flagship's real matrix shapes (24 layers of gqkv 5120x2048,
 o 2048x2048, gate_up 11264x2048, down 2048x5632, plus the 65536x2048 embedding and head under
 Adam) and times the replicated MuonAdamW step: fused reduce + momentum + gather-to-owner,
-fp32 Newton-Schulz on each matrix's owner only, fused scatter + update + all-gather.  It also
+Newton-Schulz (batched bf16 tensor-core GEMMs) on each matrix's owner only, fused scatter +
+update + all-gather.  It also
 reports the per-rank Newton-Schulz FLOPs against what a redundant every-rank chain would do.
 """
 from __future__ import annotations
