@@ -151,7 +151,8 @@ def report_muon(opt, engine, world, total, seconds):
                           "world": world, "params": total, "ms": round(seconds * 1e3, 3),
                           "ns_tflop_max_rank": round(max(per_rank.values()) / 1e12, 2),
                           "ns_tflop_every_rank_redundant": round(redundant / 1e12, 2),
-                          "ns_dtype": "fp32 (IEEE, as the reference)"}), flush=True)
+                          "ns_dtype": ("fp32 (IEEE, as the reference)" if os.environ.get("MIMIR_MUON_NS") == "fp32"
+                                       else "bf16 operands, fp32 accumulation (tensor cores)")}), flush=True)
 
 
 if __name__ == "__main__":
