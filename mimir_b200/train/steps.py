@@ -134,8 +134,7 @@ def _accumulate_and_step(config, rank: int, train_state, batches: list, use_comp
     # when nothing between the backward and the step reads the gradients or the old weights.
     overlap = (engine is not None and optimizer_step_enabled and not use_compiled
                and config.gradient_clip_norm is None and config.gradient_skip_norm is None
-               and kwargs.get("stability_diagnostics") is None and not config.experiment_update_probe_interval
-               and not has_balanced_routers(model))
+               and kwargs.get("stability_diagnostics") is None and not config.experiment_update_probe_interval)
     streams = engine.compute_stream() if overlap else nullcontext()
     try:
         with streams:

@@ -324,11 +324,15 @@ def test_multi_gpu_overlapped_update_equals_closing_update(tmp_path):
         assert torch.equal(ranks[r][1][3], ranks[0][1][3])  # every replica holds the same weights
 
 
-def test_overlapped_update_is_bit_identical_in_the_training_step():
-    """The real model on the tcgen05 kernels, trained through ``train_accumulated_batches`` with
-    the update overlapped with the backward and without, and overlapped a second time: the
-    master weights, moments and EMA of all three runs must match bit for bit (any weight read
-    racing its bucket's update, or any nondeterministic kernel, would show here)."""
+@pytest.mark.parametrize("extra", [{}, dict(moe_num_experts=4, moe_top_k=2, moe_sparse=True, moe_dispatch="grouped",
+                                             moe_aux_loss_free=True, moe_expert_intermediate_size=256)],
+                         ids=["dense", "moe"])
+def test_overlapped_update_is_bit_identical_in_the_training_step(extra):
+    """The real model on the tcgen05 kernels (dense, and a routed MoE with grouped experts and
+    routing balance), trained through ``train_accumulated_batches`` with the update overlapped
+    with the backward and without, and overlapped a second time: the master weights, moments and
+    EMA of all three runs must match bit for bit (any weight read racing its bucket's update, or
+    any nondeterministic kernel, would show here)."""
     import sys
     sys.path.insert(0, os.path.dirname(__file__))
     from test_reference_losses_gpu import MODEL, OPTIM, SEQ, SEQS, _batches, _on
@@ -341,14 +345,15 @@ def test_overlapped_update_is_bit_identical_in_the_training_step():
     from mimir_b200.train.setup import make_train_state
     from mimir_b200.train.steps import train_accumulated_batches
     dev = torch.device("cuda", 0)
-    arch = {k: v for k, v in MODEL.items() if k not in ("vocab_size", "max_seq_len", "fwd_bwd_dtype")}
+    model_cfg = MODEL | extra
+    arch = {k: v for k, v in model_cfg.items() if k not in ("vocab_size", "max_seq_len", "fwd_bwd_dtype")}
     config = PretrainConfig(arch=arch, data=dict(path="synthetic"), global_batch_size=SEQ * SEQS,
                             distributed_strategy="replicated", **OPTIM)
     batches = _batches()
     runs = []
     for enabled in (False, True, True):
         torch.manual_seed(0)
-        model = LMHead(Mimir2(MODEL), MODEL).to(dev)
+        model = LMHead(Mimir2(model_cfg), model_cfg).to(dev)
         engine = wrap_replicated(model, dev, torch.bfloat16)
         engine.overlap_enabled = enabled
         optim = ReplicatedAdamATan2(engine, lr=0.0, betas=(0.9, 0.95), weight_decay=0.1, ema=0.999,
