@@ -220,3 +220,32 @@ def test_gradient_after_its_bucket_update_raises():
     model.head(torch.randn(3, 24)).sum().backward()  # a second arrival for the already-updated head
     with pytest.raises(RuntimeError, match="arrived after its bucket was updated"):
         opt.step()
+
+
+def test_stacked_router_rows_match_torch_stack():
+    """Router rows under the engine are read as one strided matrix and their gradients written by
+    one add: the gradients equal those of ``torch.stack`` and every parameter is announced."""
+    from mimir_b200.models.experts import TopKRouter
+    from mimir_b200.ops.stacked import _StackedFn, stacked
+
+    def build(freeze_base=False):
+        torch.manual_seed(0)
+        return TopKRouter(16, 6, 2, init_std=0.02, freeze_base=freeze_base)
+
+    x = torch.randn(10, 16)
+    for freeze in (False, True):
+        plain, wrapped = build(freeze), build(freeze)
+        engine = wrap_replicated(wrapped, torch.device("cpu"), torch.float32)
+        fast = stacked(wrapped.rows).grad_fn
+        assert (type(fast).__name__ == _StackedFn.__name__ + "Backward") is not freeze
+        for m in (plain, wrapped):
+            for _ in range(2):  # two micro-batches accumulate
+                m.scores(x).square().sum().backward()
+        params = dict(plain.named_parameters())
+        for s in engine.slots:
+            if s.trainable:
+                assert torch.allclose(s.param.grad, params[s.fqn].grad, rtol=1e-6, atol=1e-7), s.fqn
+        # every trainable row and bias was announced, equally often (the counts the overlap learns)
+        counts = {engine.arrivals.get(s.fqn, 0) for s in engine.slots if s.trainable}
+        assert len(counts) == 1 and counts.pop() >= 2
+        engine.close()
