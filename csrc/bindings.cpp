@@ -96,6 +96,8 @@ at::Tensor gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, c10::optional<
 std::vector<at::Tensor> gemm_swiglu(at::Tensor x, at::Tensor w_gu, int64_t group_m);
 at::Tensor gemm_swiglu_bwd(at::Tensor dy, at::Tensor w_down, at::Tensor gu, int64_t group_m);
 int64_t gemm_status(int64_t device);
+at::Tensor gemm_allgather(at::Tensor x, std::vector<int64_t> shard_ptrs, int64_t rank, at::Tensor g, at::Tensor flags,
+                          int64_t epoch, int64_t wait_ns);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mimir_b200 hand-written sm_100a kernels";
@@ -143,6 +145,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_swiglu", &gemm_swiglu, py::arg("x"), py::arg("w_gu"), py::arg("group_m") = 8);
   m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd, py::arg("dy"), py::arg("w_down"), py::arg("gu"), py::arg("group_m") = 8);
   m.def("gemm_status", &gemm_status);
+  m.def("gemm_allgather", &gemm_allgather, py::arg("x"), py::arg("shard_ptrs"), py::arg("rank"), py::arg("g"),
+        py::arg("flags"), py::arg("epoch"), py::arg("wait_ns") = 0);
   m.def("embed_fwd", &embed_fwd);
   m.def("embed_bwd", &embed_bwd);
   m.def("embed_status", &embed_status);

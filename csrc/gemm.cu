@@ -576,6 +576,285 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------------------ all-gather + GEMM
+// Forward of a linear layer whose weight W [N, K] is sharded by rows over the `world` GPUs of one
+// node: rank k holds rows [k * S, (k + 1) * S) (S = N / world) in memory that every rank maps.
+// One launch computes y = x W^T and leaves the whole of W in this GPU's buffer G, which the
+// backward's input gradient then reads locally (no second all-gather).
+//
+// Nothing waits on another CTA or another GPU, so no launch order or co-residency matters:
+//   * The odd CTA of every pair runs a gatherer (its warp 1, idle in the pair kernel): it copies
+//     items of W (128 rows x a range of k-blocks, 16 KB per TMA load, two loads in flight) from
+//     their owner's memory into G with TMA stores, and after an item's stores are complete adds
+//     one to its 128-row block's counter (release, GPU scope).  Items run in ring order: the
+//     next rank's rows first, this rank's own rows (a local copy) last.
+//   * Tiles run column by column starting at this rank's own columns, so the first waves read
+//     only local weight rows while the gatherers pull the next ranks' rows over NVLink.
+//   * For each tile the producer reads its 128-row block's counter once (acquire): a complete
+//     block is read from G; otherwise the rows come straight from the owner's memory (correct,
+//     only more NVLink traffic), so a late gatherer costs bandwidth, never a wait.
+// The counters grow by `parts` per call and never reset: a block is complete for call e when
+// its counter reaches e * parts.  Loads from peer memory are plain tiled TMA (no multicast).
+struct GatherArgs {
+  CUtensorMap shard[8];  // rank k's rows [S, K], box 64 x 128
+  CUtensorMap g;         // G [N, K] on this GPU, box 64 x 128
+  unsigned* flags;       // [N / 128] completion counters
+  unsigned target;       // counter value of a block that is complete in this call
+  int rank, world, shard_rows, parts;
+};
+
+constexpr int kGatherSlotBytes = 128 * kBK * 2;  // one 128-row x 64-column bf16 box
+
+__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* ptr) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add_u32(unsigned* ptr, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// 3-D tiled TMA load into this CTA's shared memory, completion on this CTA's barrier.
+__device__ __forceinline__ void tma_load_3d_cta(uint32_t smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
+                                                int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(smem_dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// Column-major tile order starting at the column block that holds this rank's first row.
+template <int BN>
+__device__ __forceinline__ void gather_tile(int t, const GemmParams& p, const GatherArgs& ga, int& mt, int& nt) {
+  const int col = t / p.tiles_m;
+  mt = t - col * p.tiles_m;
+  nt = (col + (ga.rank * ga.shard_rows) / BN) % p.tiles_n;
+}
+
+// Position of one gatherer in its item sequence (items cid, cid + ncl, ...).
+struct GatherCursor {
+  int item, kb, hi;
+};
+__device__ __forceinline__ void cursor_set(GatherCursor& c, int item, int parts, int nkb) {
+  c.item = item;
+  c.kb = ((item % parts) * nkb) / parts;
+  c.hi = ((item % parts + 1) * nkb) / parts;
+}
+__device__ __forceinline__ void cursor_next(GatherCursor& c, int ncl, int parts, int nkb) {
+  if (++c.kb == c.hi) cursor_set(c, c.item + ncl, parts, nkb);
+}
+
+__device__ __forceinline__ int gather_owner(const GatherArgs& ga, int item, int per_rank) {
+  return (ga.rank + 1 + (item / ga.parts) / per_rank) % ga.world;
+}
+__device__ __forceinline__ int gather_srow(const GatherArgs& ga, int item, int per_rank) {
+  return ((item / ga.parts) % per_rank) * 128;
+}
+
+__device__ void gather_rows(const GatherArgs& ga, const GemmParams& p, uint32_t slots, uint64_t* gbar, int cid,
+                            int ncl) {
+  const int nkb = (p.K + kBK - 1) / kBK;
+  const int per_rank = ga.shard_rows / 128;
+  const int items = ga.world * per_rank * ga.parts;
+  GatherCursor ld, st;
+  cursor_set(ld, cid, ga.parts, nkb);
+  st = ld;
+  int loaded = 0, stored = 0;
+  bool ok = true;
+  for (int s = 0; s < 2 && ld.item < items; ++s) {
+    mbar_arrive_expect_tx(&gbar[s], kGatherSlotBytes);
+    tma_load_3d_cta(slots + s * kGatherSlotBytes, &ga.shard[gather_owner(ga, ld.item, per_rank)], &gbar[s],
+                    ld.kb * kBK, gather_srow(ga, ld.item, per_rank), 0);
+    cursor_next(ld, ncl, ga.parts, nkb);
+    ++loaded;
+  }
+  while (stored < loaded) {
+    const int s = stored & 1;
+    if (!mbar_wait_ns(&gbar[s], (stored >> 1) & 1, p.status, kStatusTimeoutOther, p.wait_ns)) {
+      ok = false;
+      break;
+    }
+    const int grow = gather_owner(ga, st.item, per_rank) * ga.shard_rows + gather_srow(ga, st.item, per_rank);
+    tma_store_3d(&ga.g, slots + s * kGatherSlotBytes, st.kb * kBK, grow, 0);
+    bulk_commit_group();
+    bulk_wait_group_read0();  // the slot may be refilled
+    if (st.kb + 1 == st.hi) {  // the item is complete once its stores are
+      bulk_wait_group0();
+      fence_proxy_async_global();
+      red_release_gpu_add_u32(&ga.flags[grow / 128], 1u);
+    }
+    cursor_next(st, ncl, ga.parts, nkb);
+    ++stored;
+    if (ld.item < items) {
+      mbar_arrive_expect_tx(&gbar[s], kGatherSlotBytes);
+      tma_load_3d_cta(slots + s * kGatherSlotBytes, &ga.shard[gather_owner(ga, ld.item, per_rank)], &gbar[s],
+                      ld.kb * kBK, gather_srow(ga, ld.item, per_rank), 0);
+      cursor_next(ld, ncl, ga.parts, nkb);
+      ++loaded;
+    }
+  }
+  bulk_wait_group0();
+  if (!ok) spin_ns(1000000ull);  // loads still in flight land before the CTA exits
+}
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_gather_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_out,
+                       const __grid_constant__ GatherArgs ga, const GemmParams p) {
+  using CF = PairCfg<BN, kEpiStore>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ PairBars bars;
+  __shared__ uint64_t gbar[2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const bool leader = crank == 0;
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  const int total = p.tiles_m * p.tiles_n;
+  const int nkb = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < CF::kStages; ++s) {
+      mbar_init(&bars.full[s], 1);
+      mbar_init(&bars.empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars.acc_full[i], 1);
+      mbar_init(&bars.acc_empty[i], 2 * kEpiWarps);
+      mbar_init(&gbar[i], 1);
+    }
+    mbar_init(&bars.done, 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&bars.tmem_base, CF::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&ga.g);
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = bars.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = cid; ok && t < total; t += ncl) {
+        int mt, nt;
+        gather_tile<BN>(t, p, ga, mt, nt);
+        const int am = mt * 2 * kBM + static_cast<int>(crank) * kBM;
+        const int bn = nt * BN + static_cast<int>(crank) * CF::kBHalf;  // this CTA's 128 weight rows
+        const int owner = bn / ga.shard_rows;
+        const CUtensorMap* mb = &ga.shard[owner];
+        int by = bn - owner * ga.shard_rows;
+        if (owner != ga.rank && static_cast<int>(ld_acquire_gpu_u32(&ga.flags[bn / 128]) - ga.target) >= 0) {
+          fence_proxy_async_global();  // G's rows were written by other CTAs' TMA stores
+          mb = &ga.g;
+          by = bn;
+        }
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % CF::kStages;
+          if (it >= CF::kStages && !mbar_wait_ns(&bars.empty[s], ((it / CF::kStages) - 1) & 1, p.status,
+                                                 kStatusTimeoutEmpty, p.wait_ns)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = smem_u32(smem + s * CF::kStageBytes);
+          const uint32_t sb = sa + CF::kABytes;
+          const uint32_t fb = mapa_shared(smem_u32(&bars.full[s]), 0);
+          if (leader) mbar_arrive_expect_tx(&bars.full[s], 2 * CF::kStageBytes);
+          tma_load_3d_pair(sa, &map_a, fb, kb * kBK, am, 0);
+          tma_load_3d_pair(sb, mb, fb, kb * kBK, by, 0);
+        }
+      }
+      for (int j = max(0, it - CF::kStages); j < it; ++j) {
+        if (!mbar_wait_ns(&bars.empty[j % CF::kStages], (j / CF::kStages) & 1, p.status, kStatusTimeoutKV,
+                          p.wait_ns)) {
+          spin_ns(1000000ull);
+          break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer (even CTA)
+      const uint32_t idesc = idesc_bf16_f32(2 * kBM, BN, 0, 0);
+      int it = 0, i = 0;
+      bool ok = true;
+      for (int t = cid; ok && t < total; t += ncl, ++i) {
+        const int buf = i & 1;
+        if (i >= 2 &&
+            !mbar_wait_ns(&bars.acc_empty[buf], ((i >> 1) - 1) & 1, p.status, kStatusTimeoutO, p.wait_ns))
+          break;
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * BN;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % CF::kStages;
+          if (!mbar_wait_ns(&bars.full[s], (it / CF::kStages) & 1, p.status, kStatusTimeoutKV, p.wait_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * CF::kStageBytes);
+          const uint32_t sb = sa + CF::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_bf16_pair(acc, smem_desc(sa + kk * 32, 16, 1024, kLayoutSW128),
+                          smem_desc(sb + kk * 32, 16, 1024, kLayoutSW128), idesc, (kb | kk) != 0 ? 1u : 0u);
+          mma_commit_pair(&bars.empty[s], 0x3);
+        }
+        if (ok) mma_commit_pair(&bars.acc_full[buf], 0x3);
+      }
+      mma_commit_pair(&bars.done, 0x3);
+    } else if (!leader && lane == 0) {
+      // ---------------------------------------------------------- gatherer (odd CTA)
+      gather_rows(ga, p, smem_u32(smem + CF::kStagingOffset + kEpiWarps * CF::kStagingPerWarp), gbar, cid, ncl);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int wq = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    Staging st{smem_u32(smem + CF::kStagingOffset) + static_cast<uint32_t>((warp - 2) * CF::kStagingPerWarp), 0u};
+    int i = 0;
+    for (int t = cid; t < total; t += ncl, ++i) {
+      const int buf = i & 1;
+      int mt, nt;
+      gather_tile<BN>(t, p, ga, mt, nt);
+      const int row0 = mt * 2 * kBM + static_cast<int>(crank) * kBM + wq * 32;
+      const uint32_t tacc = tmem + lane_off + buf * BN;
+      if (!warp_wait_ns(&bars.acc_full[buf], (i >> 1) & 1, p.status, kStatusTimeoutS, p.wait_ns)) break;
+      tc_fence_after();
+      epilogue_store_tma<BN>(p, &map_out, tacc, lane, row0, 0, nt * BN, half, st);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&bars.acc_empty[buf]), 0));
+    }
+    if (lane == 0) bulk_wait_group0();
+    __syncwarp();
+    if (warp == 2 && lane == 0) mbar_wait_ns(&bars.done, 0, p.status, kStatusTimeoutOther, p.wait_ns);
+    __syncwarp();
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, CF::kTmemCols);
+  }
+}
+
+template <int BN>
+constexpr int gather_smem() {
+  return PairCfg<BN, kEpiStore>::kSmem + 2 * kGatherSlotBytes;
+}
+static_assert(gather_smem<256>() + 1024 <= 232448, "the gather kernel's shared memory must fit one SM");
+
 // ------------------------------------------------------------------------------------ host side
 int* status_word(int device) {
   static int* words[64] = {nullptr};
@@ -809,6 +1088,65 @@ at::Tensor gemm_swiglu_bwd(at::Tensor dy, at::Tensor w_down, at::Tensor gu, int6
   const CUtensorMap mo = output_map(dgu);
   launch_pair<256, false, true, kEpiSwiGLUBwd, false>(ma, mb, mo, mo, p, dev, at::cuda::getCurrentCUDAStream());
   return dgu;
+}
+
+// y = x @ W^T for a weight W [n_rows, K] sharded by rows over len(shard_ptrs) ranks of one node
+// (rank k's rows at shard_ptrs[k], contiguous [n_rows / world, K] bf16, mapped on this GPU), with
+// the whole of W gathered into `g` [n_rows, K] as a by-product.  `flags` (int32 [n_rows / 128],
+// zero before the first call) persists across calls with the same `g`; `epoch` counts those
+// calls from 1.  The shards must not change while any rank's call runs.
+at::Tensor gemm_allgather(at::Tensor x, std::vector<int64_t> shard_ptrs, int64_t rank, at::Tensor g, at::Tensor flags,
+                          int64_t epoch, int64_t wait_ns) {
+  check_operand(x, "x");
+  check_operand(g, "g");
+  const int64_t world = static_cast<int64_t>(shard_ptrs.size());
+  TORCH_CHECK(world >= 1 && world <= 8 && rank >= 0 && rank < world, "1 to 8 shards, 0 <= rank < world");
+  TORCH_CHECK(x.dim() == 2 && g.dim() == 2 && g.is_contiguous(), "x [M, K], g [N, K] contiguous");
+  const int64_t M = x.size(0), K = x.size(1), N = g.size(0);
+  TORCH_CHECK(g.size(1) == K, "g: [N, K]");
+  TORCH_CHECK(N % 256 == 0 && N % (world * 128) == 0, "N must be a multiple of 256 and of 128 x world");
+  TORCH_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "dimensions out of range");
+  TORCH_CHECK(flags.is_cuda() && flags.scalar_type() == at::kInt && flags.is_contiguous() && flags.numel() == N / 128,
+              "flags: int32 [N / 128]");
+  TORCH_CHECK(epoch >= 1, "epoch counts calls from 1");
+  const int64_t S = N / world;
+  for (int64_t p : shard_ptrs) TORCH_CHECK(p % 16 == 0, "shard pointers must be 16-byte aligned");
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor y = at::empty({M, N}, x.options());
+  constexpr int BN = 256;
+  const int dev = x.device().index();
+  GemmParams p = base_params(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), BN, 1, wait_ns, 0, dev);
+  p.out = y.data_ptr();
+  p.ldo = y.stride(0);
+  auto kernel = gemm_gather_kernel<BN>;
+  constexpr int smem = gather_smem<BN>();
+  static bool attr[64] = {false};
+  if (!attr[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr[dev] = true;
+  }
+  // Every resident pair runs (a pair without tiles still gathers), so the split of the rows into
+  // items, and with it the counters' step per call, depends only on the device and the shape.
+  const int pairs = resident_pairs(dev, reinterpret_cast<const void*>(kernel), smem);
+  const int nkb = static_cast<int>((K + kBK - 1) / kBK);
+  const int blocks = static_cast<int>(N / 128);
+  const int parts = std::max(1, std::min(nkb, (2 * pairs + blocks - 1) / blocks));
+  GatherArgs ga;
+  std::memset(&ga, 0, sizeof(ga));
+  for (int64_t k = 0; k < world; ++k)
+    ga.shard[k] = make_tmap_bf16_3d(reinterpret_cast<const void*>(shard_ptrs[k]), 1, S, K, K, S * K, kBK, 128);
+  ga.g = make_tmap_bf16_3d(g.data_ptr(), 1, N, K, K, N * K, kBK, 128);
+  ga.flags = reinterpret_cast<unsigned*>(flags.data_ptr());
+  ga.target = static_cast<unsigned>(static_cast<uint64_t>(epoch) * static_cast<uint64_t>(parts));
+  ga.rank = static_cast<int>(rank);
+  ga.world = static_cast<int>(world);
+  ga.shard_rows = static_cast<int>(S);
+  ga.parts = parts;
+  const CUtensorMap ma = M > 0 ? operand_map(x, kBK, kBM) : ga.g;  // without rows the pairs only gather
+  const CUtensorMap mo = M > 0 ? output_map(y) : ga.g;
+  kernel<<<2 * pairs, kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(ma, mo, ga, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return y;
 }
 
 // Reads and clears the dense GEMM kernels' status word of `device` (0 = every wait completed).

@@ -249,3 +249,35 @@ def test_stacked_router_rows_match_torch_stack():
         counts = {engine.arrivals.get(s.fqn, 0) for s in engine.slots if s.trainable}
         assert len(counts) == 1 and counts.pop() >= 2
         engine.close()
+
+
+def _sharded_worker(rank, world, init, out):
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
+    try:
+        from mimir_b200.parallel.sharded_linear import ShardedLinear
+        torch.manual_seed(0)
+        w = torch.randn(8, 6)
+        layer = ShardedLinear(w, device="cpu")
+        x = torch.randn(5, 6, generator=torch.Generator().manual_seed(rank), requires_grad=True)
+        y = layer(x)
+        y.square().sum().backward()
+        torch.save({"y": y.detach(), "x": x.detach(), "dx": x.grad, "dshard": layer.shard.grad,
+                    "full": layer.full_weight()}, f"{out}.{rank}.pt")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_linear_two_gloo_ranks(tmp_path):
+    """Row-sharded projection on CPU ranks: forward, input gradient, summed weight gradient."""
+    world = 2
+    init = f"file://{tmp_path / 'init'}"
+    mp.spawn(_sharded_worker, args=(world, init, str(tmp_path / "s")), nprocs=world, join=True)
+    torch.manual_seed(0)
+    w = torch.randn(8, 6)
+    rs = [torch.load(f"{tmp_path / 's'}.{r}.pt") for r in range(world)]
+    grad = sum((2 * r["y"]).t() @ r["x"] for r in rs)
+    for rank, r in enumerate(rs):
+        assert torch.allclose(r["y"], r["x"] @ w.t(), atol=1e-6)
+        assert torch.allclose(r["dx"], (2 * r["y"]) @ w, atol=1e-5)
+        assert torch.allclose(r["dshard"], grad[rank * 4:(rank + 1) * 4], atol=1e-5)
+        assert torch.equal(r["full"], w)
