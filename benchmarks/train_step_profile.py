@@ -28,6 +28,7 @@ def main():
     ap.add_argument("--optimizer", choices=["adam_atan2", "muon"], default="adam_atan2")
     ap.add_argument("--rows", type=int, default=25)
     ap.add_argument("--overlap-report", action="store_true")
+    ap.add_argument("--shapes", action="store_true", help="also group the table by input shapes")
     args = ap.parse_args()
     import bench
     bench.CONFIG["name"] = args.config
@@ -60,11 +61,16 @@ def main():
         step()
     torch.cuda.synchronize()
     from torch.profiler import ProfilerActivity, profile
-    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=args.shapes) as prof:
         step()
         torch.cuda.synchronize()
     table = prof.key_averages()
-    print(table.table(sort_by="self_cuda_time_total", row_limit=args.rows))
+    print(table.table(sort_by="self_cuda_time_total", row_limit=args.rows, max_name_column_width=110))
+    # the same kernels with the op that launched them (shapes show which tensors they touched)
+    if args.shapes:
+        shaped = prof.key_averages(group_by_input_shape=True)
+        print(shaped.table(sort_by="self_cuda_time_total", row_limit=args.rows, max_name_column_width=60,
+                           max_shapes_column_width=80))
     total = sum(getattr(e, "self_device_time_total", getattr(e, "self_cuda_time_total", 0)) for e in table)
     print(f"total self CUDA time of the step: {total / 1e3:.1f} ms")
     if args.overlap_report:

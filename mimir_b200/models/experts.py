@@ -59,10 +59,9 @@ class TopKRouter(nn.Module):
         return out
 
     def scores(self, x, logit_bias=None):
+        from mimir_b200.ops.router import router_logits
         from mimir_b200.ops.stacked import stacked  # one gradient kernel for all rows under the replicated engine
-        weight = stacked(self.rows).float()
-        bias = stacked(self.biases).reshape(-1).float()
-        s = F.linear(x.float(), weight, bias) + self.logit_bias.float()
+        s = router_logits(x, stacked(self.rows), stacked(self.biases).reshape(-1)) + self.logit_bias.float()
         if logit_bias is not None:
             s = s + logit_bias.float()
         return s

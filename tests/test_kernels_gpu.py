@@ -403,3 +403,26 @@ def test_scaled_embedding_matches_torch(dtype):
     w.grad = None
     ops.scaled_embedding(ids, w, 2.5).backward(dy)
     assert torch.equal(first, w.grad), "the backward is deterministic"
+
+
+@pytest.mark.parametrize("d", [2048, 3072])
+def test_scaled_embedding_backward_skewed_ids(d):
+    """Zipf-like ids: one id on thousands of positions, runs of exactly 32 and 33 rows, singletons
+    (short runs summed by one warp, long runs by one CTA of eight warps), against fp32 index_add;
+    bit-identical on a second run."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    V = 4096
+    parts = [torch.full((3000,), 7), torch.full((32,), 11), torch.full((33,), 12), torch.full((200,), 13),
+             torch.randint(100, V, (1500,), generator=torch.Generator().manual_seed(1))]
+    ids = torch.cat(parts)[torch.randperm(4765, generator=torch.Generator().manual_seed(2))].cuda()
+    T = ids.numel()
+    w = (torch.randn(V, d, device="cuda", generator=g) * 0.1).to(torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(T, d, device="cuda", generator=g).to(torch.bfloat16)
+    ops.scaled_embedding(ids, w, 0.5).backward(dy)
+    ref = torch.zeros(V, d, device="cuda").index_add_(0, ids.long(), 0.5 * dy.float())
+    scale = ref.abs().max().item()
+    _close(w.grad.float() / scale, ref / scale, 1e-2, 0.0, "skewed embedding backward")
+    first = w.grad.clone()
+    w.grad = None
+    ops.scaled_embedding(ids, w, 0.5).backward(dy)
+    assert torch.equal(first, w.grad)

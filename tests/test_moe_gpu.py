@@ -241,3 +241,32 @@ def test_grouped_path_under_activation_checkpointing_returns_every_buffer():
         assert not ep._busy  # nothing held after the backward
         sizes.append(len(ep._pool))
     assert sizes[1] == sizes[2]  # the pool stops growing: buffers are reused
+
+
+@pytest.mark.parametrize("tokens,n", [(16384, 64), (1000, 32), (7, 128)])
+def test_router_logits_tensor_core_path_matches_fp32(tokens, n):
+    """bf16 hidden states and router rows: the tcgen05 fp32-output path against the fp32 F.linear
+    the reference runs (forward, input, row and bias gradients)."""
+    import torch.nn.functional as F
+
+    from mimir_b200.ops.router import router_logits, tensor_core_path
+    g = torch.Generator(device="cuda").manual_seed(tokens + n)
+    x = torch.randn(tokens, 2048, device="cuda", generator=g).to(torch.bfloat16).requires_grad_()
+    w = (torch.randn(n, 2048, device="cuda", generator=g) * 0.02).to(torch.bfloat16).requires_grad_()
+    b = (torch.randn(n, device="cuda", generator=g) * 0.1).to(torch.bfloat16).requires_grad_()
+    assert tensor_core_path(x, w)
+    s = router_logits(x, w, b)
+    ref_leaves = [t.detach().float().requires_grad_() for t in (x, w, b)]
+    ref = F.linear(*ref_leaves)
+    assert s.dtype == torch.float32
+    scale = ref.abs().max().item()
+    assert (s - ref).abs().max().item() <= 1e-4 * scale
+    ds = torch.randn(tokens, n, device="cuda", generator=g)
+    s.backward(ds)
+    ref.backward(ds)
+    for got, want, name in ((x.grad, ref_leaves[0].grad, "x"), (w.grad, ref_leaves[1].grad, "w"),
+                            (b.grad, ref_leaves[2].grad, "b")):
+        err = ((got.float() - want).abs().max() / want.abs().max()).item()
+        assert err <= 8e-3, (name, err)
+    from mimir_b200.ops import gemm as G
+    assert G.status(0) == 0
