@@ -64,6 +64,7 @@ std::vector<at::Tensor> ipc_alloc(int64_t nbytes, int64_t device);
 int64_t ipc_open(at::Tensor handle_bytes, int64_t device);
 void ipc_close(int64_t ptr, int64_t device);
 bool peer_access_possible(int64_t device, int64_t peer);
+void zero_bytes(at::Tensor t);
 void moe_dispatch(at::Tensor x, at::Tensor rows, at::Tensor dst, std::vector<int64_t> recv, int64_t k,
                   int64_t capacity);
 at::Tensor moe_combine(std::vector<int64_t> y, at::Tensor rows, at::Tensor dst, c10::optional<at::Tensor> w,
@@ -131,6 +132,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
   m.def("peer_access_possible", &peer_access_possible);
+  m.def("zero_bytes", &zero_bytes);
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_combine", &moe_combine);
   m.def("moe_combine_bwd", &moe_combine_bwd);

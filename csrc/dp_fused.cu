@@ -495,6 +495,15 @@ void ipc_close(int64_t ptr, int64_t device) {
   C10_CUDA_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)));
 }
 
+// Zeroes a contiguous device tensor with one driver memset on the current stream (the gradient
+// buffer between steps: a plain store stream at the copy engine's rate, one call for any size).
+void zero_bytes(at::Tensor t) {
+  TORCH_CHECK(t.is_cuda() && t.is_contiguous(), "zero_bytes: contiguous CUDA tensor");
+  if (t.numel() == 0) return;
+  const c10::cuda::CUDAGuard guard(t.device());
+  C10_CUDA_CHECK(cudaMemsetAsync(t.data_ptr(), 0, t.nbytes(), at::cuda::getCurrentCUDAStream()));
+}
+
 bool peer_access_possible(int64_t device, int64_t peer) {
   int ok = 0;
   C10_CUDA_CHECK(cudaDeviceCanAccessPeer(&ok, static_cast<int>(device), static_cast<int>(peer)));

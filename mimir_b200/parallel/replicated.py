@@ -115,6 +115,7 @@ class ReplicatedEngine:
         # optimizer, a parameter without one (e.g. outside the truncated-BPTT window) is not
         # updated at all (no decay, no moment update, no step count).
         self.touched: set[str] = set()
+        self._grads_zero = False  # known to be all zero (set by zero_grad, cleared by an arrival)
         self.arrivals: dict[str, int] = {}
         for s in self.slots:
             if s.trainable:
@@ -242,9 +243,17 @@ class ReplicatedEngine:
 
     # ------------------------------------------------------------------ update overlapped with the backward
     def _arrived(self, fqn: str) -> None:
+        self._grads_zero = False
         self.touched.add(fqn)
-        self.arrivals[fqn] = self.arrivals.get(fqn, 0) + 1
+        n = self.arrivals.get(fqn, 0)
+        self.arrivals[fqn] = n + 1
         b = self._bucket_of[fqn]
+        if self.expected is not None:  # slots of the bucket whose count equals the expectation
+            e = self.expected.get(fqn, 0)
+            if n == e:
+                self._done[b] -= 1
+            elif n + 1 == e:
+                self._done[b] += 1
         self._arrival_seq += 1
         self._last_arrival[b] = self._arrival_seq
         if self._armed is None:
@@ -257,7 +266,9 @@ class ReplicatedEngine:
             self._next += 1
 
     def _bucket_final(self, b: int) -> bool:
-        return all(self.arrivals.get(s.fqn, 0) == self.expected.get(s.fqn, 0) for s in self.buckets[b])
+        # every slot's arrival count equals the learned one (kept per arrival: O(1) here, where a
+        # scan of the bucket per arrival cost O(slots^2) per MoE block)
+        return self._done[b] == len(self.buckets[b])
 
     def _fire(self, b: int) -> None:
         slots = [s for s in self.buckets[b] if s.fqn in self.touched]
@@ -334,6 +345,8 @@ class ReplicatedEngine:
         decision takes two collectives per learning step and none afterwards."""
         same_counts = self.arrivals == self.expected
         self.expected = dict(self.arrivals)
+        self._done_start = [sum(1 for s in bucket if self.expected.get(s.fqn, 0) == 0) for bucket in self.buckets]
+        self._done = [len(bucket) for bucket in self.buckets]  # now every count equals the expectation
         if self.overlap_ready is not None or not self.overlap_enabled:
             return
         self._learn_steps += 1
@@ -357,9 +370,20 @@ class ReplicatedEngine:
 
     # ------------------------------------------------------------------ step plumbing
     def zero_grad(self) -> None:
-        self.grads.zero_()
+        # Gradients reach the buffer only through arrivals (accumulation hooks and sinks), so a
+        # buffer that saw none since it was last zeroed is still zero (training zeroes it both
+        # after a step and before the next one; the second is free).
+        if not self._grads_zero:
+            if self.cuda:
+                from mimir_b200.ops._ext import ext
+                ext().zero_bytes(self.grads)
+            else:
+                self.grads.zero_()
+            self._grads_zero = True
         self.touched.clear()
         self.arrivals.clear()
+        if self.expected is not None:
+            self._done = list(self._done_start)
         self._last_arrival.clear()
         self._arrival_seq = 0
 
