@@ -281,3 +281,25 @@ def test_sharded_linear_two_gloo_ranks(tmp_path):
         assert torch.allclose(r["dx"], (2 * r["y"]) @ w, atol=1e-5)
         assert torch.allclose(r["dshard"], grad[rank * 4:(rank + 1) * 4], atol=1e-5)
         assert torch.equal(r["full"], w)
+
+
+def test_zero_grad_zeroes_once_per_arrival_window():
+    """The engine zeroes its gradient buffer when something arrived since the last zeroing and
+    skips the call otherwise (training zeroes after the step and again before the next)."""
+    model = _model()
+    engine = wrap_replicated(model, torch.device("cpu"), torch.float32)
+    opt = ReplicatedAdamATan2(engine, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, ema=0.9)
+    calls = []
+    real = engine.grads.zero_
+    engine.grads.zero_ = lambda: (calls.append(1), real())[1]
+    model(torch.randn(3, 16)).square().sum().backward()
+    assert engine.grads.abs().sum() > 0
+    opt.zero_grad()
+    assert torch.count_nonzero(engine.grads) == 0 and len(calls) == 1
+    opt.zero_grad()  # nothing arrived: skipped
+    assert len(calls) == 1
+    model(torch.randn(3, 16)).square().sum().backward()
+    opt.step()
+    opt.zero_grad()
+    assert torch.count_nonzero(engine.grads) == 0 and len(calls) == 2
+    engine.close()
