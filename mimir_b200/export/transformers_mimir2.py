@@ -212,21 +212,23 @@ class Mimir2Model(Mimir2PreTrainedModel):
         self.rope = _Rope(config.head_dim, float(config.rope_parameters.get("rope_theta", 10000.0)))
         self.post_init()
 
-    def _mask(self, b, s, past, prefix_lengths, device, dtype):
+    def _mask(self, b, s, past, prefix_lengths, device, dtype, key_valid=None):
         """Additive mask ``[b, 1, s, past + s]``: keys before the new tokens are all visible; among
         the new ones, a query sees every key up to its own position and, inside the prefix, all of
-        the prefix."""
+        the prefix.  ``key_valid`` ([b, past + s] bool) hides padding keys of a left-padded batch."""
         q = torch.arange(s, device=device)[:, None] + past
         k = torch.arange(past + s, device=device)[None, :]
         allowed = (k <= q).expand(b, s, past + s)
         if prefix_lengths is not None:
             p = prefix_lengths.to(device)[:, None, None]
             allowed = allowed | ((q[None] < p) & (k[None] < p))
+        if key_valid is not None:
+            allowed = allowed & key_valid.to(device)[:, None, :]
         mask = torch.zeros(b, 1, s, past + s, device=device, dtype=dtype)
         return mask.masked_fill(~allowed[:, None], torch.finfo(dtype).min)
 
     def forward(self, input_ids, prefix_lengths=None, past_key_values: Optional[DynamicCache] = None,
-                position_ids=None):
+                position_ids=None, key_valid=None):
         cfg = self.config
         b, s = input_ids.shape
         past = past_key_values.get_seq_length() if past_key_values is not None else 0
@@ -241,7 +243,7 @@ class Mimir2Model(Mimir2PreTrainedModel):
                     history = past_key_values.mimir_ngram_history = {}
             x = self.ngram(x, input_ids, position_ids, history)
         rope = self.rope(position_ids)
-        mask = self._mask(b, s, past, prefix_lengths if cfg.prefix_lm else None, x.device, x.dtype)
+        mask = self._mask(b, s, past, prefix_lengths if cfg.prefix_lm else None, x.device, x.dtype, key_valid)
         layers = cfg.num_layers_per_stack
         looped = cfg.recurrence_mode == "looped"
         z_h, z_l = x, self.z_L_init.to(x.dtype)
@@ -284,9 +286,18 @@ class Mimir2ForCausalLM(Mimir2PreTrainedModel, GenerationMixin):
                                                                  or past_key_values.get_seq_length() == 0):
             # A prompt is the prefix: every prompt token sees the whole prompt.
             prefix_lengths = torch.full((input_ids.shape[0],), input_ids.shape[1], dtype=torch.long)
+        positions, key_valid = None, None
+        if attention_mask is not None and not bool(attention_mask.all()):
+            # A left-padded batch (batched serving): positions count real tokens only (padding
+            # sits at position 0, so no n-gram or rotary phase reaches across it) and padding keys
+            # are hidden from every query.
+            past = past_key_values.get_seq_length() if past_key_values is not None else 0
+            am = attention_mask.to(device=input_ids.device, dtype=torch.long)[:, :past + input_ids.shape[1]]
+            positions = (am.cumsum(-1) - 1).clamp_min(0)[:, past:]
+            key_valid = am.bool()
         hidden = self.model(input_ids, prefix_lengths=prefix_lengths,
                             past_key_values=past_key_values if use_cache or past_key_values is not None else None,
-                            position_ids=None)
+                            position_ids=positions, key_valid=key_valid)
         logits = self.lm_head(hidden)
         loss = None
         if labels is not None:

@@ -14,10 +14,15 @@ Endpoints (the subset the evaluation runner and the serving pool use):
 * ``POST /v1/completions`` (``prompt``)
 
 Request fields: ``max_tokens``, ``temperature`` (0 = greedy), ``top_p``, ``stop``, ``seed``.
-Requests are served one at a time (one model, one device); the HTTP server accepts concurrent
-connections and queues them.
+The HTTP server accepts concurrent connections.  Greedy requests without a seed are batched: a
+worker thread takes what has queued up (up to ``--max-batch`` requests, waiting at most
+``--batch-wait-ms`` after the first), left-pads the prompts into one batch (the model hides
+padding keys and counts positions from each prompt's first token) and decodes them together,
+which gives each request its own greedy continuation.  Sampled or seeded requests run one at a
+time.
 
-Usage: ``python -m mimir_b200.serving.native MODEL_DIR [--port 8000] [--device cuda:0]``.
+Usage: ``python -m mimir_b200.serving.native MODEL_DIR [--port 8000] [--device cuda:0]
+[--max-batch 8] [--batch-wait-ms 5]``.
 """
 from __future__ import annotations
 
@@ -33,11 +38,22 @@ from typing import Optional
 import torch
 
 
+class _Pending:
+    """One queued greedy request and, once its batch ran, its result (or the batch's error)."""
+
+    def __init__(self, ids: list[int], body: dict):
+        self.ids, self.body = ids, body
+        self.done = threading.Event()
+        self.result = None
+        self.error: Optional[BaseException] = None
+
+
 class Engine:
     """Tokenizer + model + a lock; ``complete`` returns ``(text, prompt_tokens, completion_tokens,
     finish_reason)``."""
 
-    def __init__(self, model_dir, device: str = "cpu", dtype: Optional[torch.dtype] = None, name: Optional[str] = None):
+    def __init__(self, model_dir, device: str = "cpu", dtype: Optional[torch.dtype] = None, name: Optional[str] = None,
+                 max_batch: int = 8, batch_wait_ms: float = 5.0):
         from transformers import AutoModelForCausalLM, AutoTokenizer
 
         from mimir_b200.export.transformers_mimir2 import register
@@ -49,6 +65,14 @@ class Engine:
         self.model = AutoModelForCausalLM.from_pretrained(model_dir, local_files_only=True, **kwargs).to(self.device)
         self.model.eval()
         self.lock = threading.Lock()
+        self.max_batch = max(1, int(max_batch))
+        self.batch_wait = max(0.0, float(batch_wait_ms)) / 1000.0
+        self.pad_id = (self.tokenizer.pad_token_id if self.tokenizer.pad_token_id is not None
+                       else self.tokenizer.eos_token_id if self.tokenizer.eos_token_id is not None else 0)
+        self._queue: list[_Pending] = []
+        self._ready = threading.Condition()
+        if self.max_batch > 1:
+            threading.Thread(target=self._serve_batches, name="mimir-batcher", daemon=True).start()
 
     def prompt_ids(self, body: dict, chat: bool) -> list[int]:
         if chat:
@@ -60,31 +84,89 @@ class Engine:
             return list(prompt)
         return self.tokenizer(prompt if isinstance(prompt, str) else prompt[0])["input_ids"]
 
-    @torch.no_grad()
-    def complete(self, ids: list[int], body: dict) -> tuple[str, int, int, str]:
-        max_tokens = int(body.get("max_tokens") or body.get("max_completion_tokens") or 16)
-        temperature = float(body.get("temperature") or 0.0)
-        stops = body.get("stop") or []
-        stops = [stops] if isinstance(stops, str) else list(stops)
-        gen = dict(max_new_tokens=max_tokens, do_sample=temperature > 0, pad_token_id=self.tokenizer.pad_token_id
-                   if self.tokenizer.pad_token_id is not None else self.tokenizer.eos_token_id)
-        if temperature > 0:
-            gen.update(temperature=temperature, top_p=float(body.get("top_p") or 1.0))
+    @staticmethod
+    def _max_tokens(body: dict) -> int:
+        return int(body.get("max_tokens") or body.get("max_completion_tokens") or 16)
+
+    def _gen_args(self, max_new: int) -> dict:
+        gen = dict(max_new_tokens=max_new, pad_token_id=self.pad_id)
         if self.tokenizer.eos_token_id is not None:
             gen["eos_token_id"] = self.tokenizer.eos_token_id
+        return gen
+
+    def _finish(self, ids: list[int], new: list[int], body: dict) -> tuple[str, int, int, str]:
+        max_tokens = self._max_tokens(body)
+        eos = self.tokenizer.eos_token_id
+        if eos is not None and eos in new:  # a batch row keeps padding after its end
+            new = new[:new.index(eos) + 1]
+        new = new[:max_tokens]
+        finish = "length" if len(new) >= max_tokens else "stop"
+        text = self.tokenizer.decode(new, skip_special_tokens=True)
+        stops = body.get("stop") or []
+        for s in [stops] if isinstance(stops, str) else list(stops):
+            cut = text.find(s)
+            if s and cut >= 0:
+                text, finish = text[:cut], "stop"
+        return text, len(ids), len(new), finish
+
+    def batchable(self, body: dict) -> bool:
+        return self.max_batch > 1 and not float(body.get("temperature") or 0.0) > 0 and body.get("seed") is None
+
+    @torch.no_grad()
+    def complete(self, ids: list[int], body: dict) -> tuple[str, int, int, str]:
+        if self.batchable(body):
+            item = _Pending(ids, body)
+            with self._ready:
+                self._queue.append(item)
+                self._ready.notify()
+            item.done.wait()
+            if item.error is not None:
+                raise item.error
+            return item.result
+        temperature = float(body.get("temperature") or 0.0)
+        gen = self._gen_args(self._max_tokens(body)) | dict(do_sample=temperature > 0)
+        if temperature > 0:
+            gen.update(temperature=temperature, top_p=float(body.get("top_p") or 1.0))
         with self.lock:
             if body.get("seed") is not None:
                 torch.manual_seed(int(body["seed"]))
             x = torch.tensor([ids], device=self.device)
             out = self.model.generate(x, attention_mask=torch.ones_like(x), **gen)
-        new = out[0, len(ids):].tolist()
-        finish = "length" if len(new) >= max_tokens else "stop"
-        text = self.tokenizer.decode(new, skip_special_tokens=True)
-        for s in stops:
-            cut = text.find(s)
-            if s and cut >= 0:
-                text, finish = text[:cut], "stop"
-        return text, len(ids), len(new), finish
+        return self._finish(ids, out[0, len(ids):].tolist(), body)
+
+    # ------------------------------------------------------------------ batched greedy decoding
+    def _serve_batches(self) -> None:
+        while True:
+            with self._ready:
+                while not self._queue:
+                    self._ready.wait()
+                deadline = time.monotonic() + self.batch_wait
+                while len(self._queue) < self.max_batch and time.monotonic() < deadline:
+                    self._ready.wait(max(0.0, deadline - time.monotonic()))
+                batch = self._queue[:self.max_batch]
+                del self._queue[:len(batch)]
+            try:
+                for item, result in zip(batch, self._generate_batch(batch)):
+                    item.result = result
+            except BaseException as exc:  # the requests of a failed batch all report it
+                for item in batch:
+                    item.error = exc
+            finally:
+                for item in batch:
+                    item.done.set()
+
+    @torch.no_grad()
+    def _generate_batch(self, batch: list[_Pending]) -> list:
+        width = max(len(item.ids) for item in batch)
+        x = torch.full((len(batch), width), self.pad_id, dtype=torch.long)
+        mask = torch.zeros_like(x)
+        for i, item in enumerate(batch):
+            x[i, width - len(item.ids):] = torch.tensor(item.ids)
+            mask[i, width - len(item.ids):] = 1
+        gen = self._gen_args(max(self._max_tokens(item.body) for item in batch)) | dict(do_sample=False)
+        with self.lock:
+            out = self.model.generate(x.to(self.device), attention_mask=mask.to(self.device), **gen)
+        return [self._finish(item.ids, out[i, width:].tolist(), item.body) for i, item in enumerate(batch)]
 
 
 def _handler(engine: Engine):
@@ -146,8 +228,11 @@ def main(argv=None) -> None:
     ap.add_argument("--port", type=int, default=8000)
     ap.add_argument("--device", default="cuda:0" if torch.cuda.is_available() else "cpu")
     ap.add_argument("--dtype", choices=["float32", "bfloat16"], default=None)
+    ap.add_argument("--max-batch", type=int, default=8, help="greedy requests decoded together (1: one at a time)")
+    ap.add_argument("--batch-wait-ms", type=float, default=5.0, help="how long a batch waits for more requests")
     args = ap.parse_args(argv)
-    engine = Engine(args.model, args.device, getattr(torch, args.dtype) if args.dtype else None)
+    engine = Engine(args.model, args.device, getattr(torch, args.dtype) if args.dtype else None,
+                    max_batch=args.max_batch, batch_wait_ms=args.batch_wait_ms)
     server = make_server(engine, args.host, args.port)
     print(f"serving {engine.name} on http://{args.host}:{args.port}/v1", flush=True)
     server.serve_forever()

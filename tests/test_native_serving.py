@@ -72,3 +72,32 @@ def test_native_backend_command(tmp_path):
         command(ServerSpec(str(tmp_path), "0,1", backend="native"))
     with pytest.raises(ValueError, match="Looped"):  # the vLLM command keeps its own limits
         command(ServerSpec(str(tmp_path), "0"))
+
+
+def test_concurrent_greedy_requests_are_batched_and_match_single_requests(tmp_path):
+    from test_transformers_model import _export
+
+    from mimir_b200.serving.native import Engine
+    _export(tmp_path, {})
+    _tokenizer(tmp_path)
+    engine = Engine(tmp_path, "cpu", name="tiny", max_batch=4, batch_wait_ms=200)
+    single = Engine(tmp_path, "cpu", name="tiny", max_batch=1)
+    bodies = [{"messages": [{"role": "user", "content": c}], "max_tokens": m}
+              for c, m in (("w1 w2 w3 w4 w5 w6", 5), ("w7", 3), ("w8 w9 w10", 6))]
+    sizes = []
+    real = engine._generate_batch
+    engine._generate_batch = lambda batch: (sizes.append(len(batch)), real(batch))[1]
+    results = [None] * len(bodies)
+
+    def ask(i):
+        results[i] = engine.complete(engine.prompt_ids(bodies[i], chat=True), bodies[i])
+
+    threads = [threading.Thread(target=ask, args=(i,)) for i in range(len(bodies))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    assert sizes and max(sizes) > 1, sizes  # at least two requests shared a batch
+    for body, got in zip(bodies, results):
+        assert got == single.complete(single.prompt_ids(body, chat=True), body), (body, got)
+        assert got[2] <= body["max_tokens"]

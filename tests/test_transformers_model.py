@@ -60,3 +60,31 @@ def test_cached_generation_equals_full_recomputation(tmp_path, extra):
         logits = native(seq, prefix_lengths=[prompt.shape[1]])
         seq = torch.cat([seq, logits[:, -1].argmax(-1, keepdim=True)], dim=1)
     assert torch.equal(out, seq)
+
+
+@pytest.mark.parametrize("extra", VARIANTS, ids=["plain", "gates", "ngram", "looped"])
+def test_left_padded_batch_generates_like_single_prompts(tmp_path, extra):
+    """Prompts of different lengths, left-padded into one batch (what batched serving does), give
+    each prompt's own greedy continuation and the same first-step logits."""
+    from transformers import AutoModelForCausalLM
+    from mimir_b200.export.transformers_mimir2 import register
+    register()
+    _export(tmp_path, extra)
+    model = AutoModelForCausalLM.from_pretrained(tmp_path)
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(1, 96, (n,), generator=g) for n in (9, 4, 6)]
+    width = max(len(p) for p in prompts)
+    batch = torch.zeros(len(prompts), width, dtype=torch.long)
+    mask = torch.zeros_like(batch)
+    for i, p in enumerate(prompts):
+        batch[i, width - len(p):] = p
+        mask[i, width - len(p):] = 1
+    with torch.no_grad():
+        padded_logits = model(batch, attention_mask=mask).logits[:, -1]
+    out = model.generate(batch, attention_mask=mask, max_new_tokens=5, do_sample=False, pad_token_id=0)
+    for i, p in enumerate(prompts):
+        with torch.no_grad():
+            alone_logits = model(p[None]).logits[:, -1]
+        torch.testing.assert_close(padded_logits[i:i + 1], alone_logits, atol=1e-5, rtol=1e-5)
+        alone = model.generate(p[None], max_new_tokens=5, do_sample=False, pad_token_id=0)
+        assert torch.equal(out[i, width:], alone[0, len(p):]), (i, out[i, width:], alone[0, len(p):])
