@@ -1,0 +1,128 @@
+"""Behaviour of individual Mimir2 features on CPU: invocation gates, n-gram memory, windowed
+cosine module learning rates.
+
+* Gates with ``alpha = 0`` are the identity on their injection, so a gated model trains exactly
+  like the ungated one until alpha ramps up (the gates add no RNG draws); a gate is token-local
+  and scales its injection by a factor within ``1 +- alpha``.
+* N-gram memory is causal, restarts at packed-sequence boundaries (positions restart at 0), and
+  token-by-token decoding with its history cache equals the full forward.
+* The windowed cosine starts at the base rate, ends at ``base * min_ratio``, is clamped outside
+  the window and rejects malformed windows.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from mimir_b200.models.common import wrap_tensor
+from mimir_b200.models.mimir2 import InvocationGate
+from mimir_b200.models.ngram import NGramMemory
+from mimir_b200.optim.module_lr import windowed_cosine_lr
+
+
+def _cfg(**kw):
+    return dict(max_seq_len=64, n_layers=2, hidden_size=32, num_heads=2, expansion=4, init_type="lecun_normal",
+                norm_type="pre", norm_eps=1e-6, pos_emb_type="rope", rope_theta=10000.0, H_cycles=2, L_cycles=2,
+                half_layers=False, fwd_bwd_dtype="float32", vocab_size=64) | kw
+
+
+def _batch(T=24):
+    from mimir_b200.data.prefixlm import compute_aux_seq_tensors_scalars
+    g = torch.Generator().manual_seed(4)
+    p, c = np.array([3, 6], np.int32), np.array([5, 7], np.int32)
+    tensors, scalars = compute_aux_seq_tensors_scalars(p, c, T)
+    pos = torch.cat([torch.arange(int(a + b)) for a, b in zip(p, c)]
+                    + [torch.zeros(T - int((p + c).sum()), dtype=torch.long)])
+    b = dict(inputs=torch.randint(0, 64, (T,), generator=g), labels=torch.randint(0, 64, (T,), generator=g),
+             position_ids=pos) | {k: torch.from_numpy(v) for k, v in tensors.items()}
+    return b | {k: wrap_tensor(torch.tensor(v)) for k, v in scalars.items()}
+
+
+def test_zero_alpha_gates_train_like_the_ungated_model():
+    from mimir_b200.models import LMHead, Mimir2
+    runs = {}
+    for gated in (False, True):
+        c = _cfg(gates_enabled=gated)
+        torch.manual_seed(0)
+        model = LMHead(Mimir2(c), c)
+        _, loss, _ = model(None, _batch(), bp_steps=3)
+        loss.backward()
+        runs[gated] = (loss.detach(), {n: p.grad for n, p in model.named_parameters()})
+    assert torch.equal(runs[False][0], runs[True][0])
+    plain, gated = runs[False][1], runs[True][1]
+    for name, grad in plain.items():
+        torch.testing.assert_close(gated[name], grad, atol=0, rtol=0, msg=name)
+    for name, grad in gated.items():
+        if "invocation_gates" in name:  # d/dW carries alpha = 0 (None outside the BPTT window)
+            assert grad is None or not bool(grad.any()), name
+
+
+def test_gate_is_token_local_and_bounded():
+    torch.manual_seed(1)
+    gate = InvocationGate(16)
+    with torch.no_grad():
+        gate.weight.normal_(0, 1.0)
+        gate.bias.normal_(0, 1.0)
+    hidden, injection = torch.randn(7, 16), torch.randn(7, 16)
+    alpha = torch.tensor(0.7)
+    out = gate(hidden, injection, alpha)
+    ratio = out / injection
+    assert bool((ratio >= 1 - 0.7 - 1e-6).all() and (ratio <= 1 + 0.7 + 1e-6).all())
+    hidden2 = hidden.clone()
+    hidden2[3] += 5.0
+    out2 = gate(hidden2, injection, alpha)
+    changed = (out2 != out).any(-1)
+    assert changed.tolist() == [i == 3 for i in range(7)]
+    torch.testing.assert_close(gate(hidden, injection, torch.tensor(0.0)), injection, atol=0, rtol=0)
+
+
+def _ngram():
+    torch.manual_seed(2)
+    mem = NGramMemory(16, orders=(2, 3), buckets=97, heads=2)
+    with torch.no_grad():
+        for t in mem.tables:
+            t.normal_()
+        mem.alpha.fill_(0.5)
+    return mem
+
+
+def test_ngram_is_causal_and_restarts_at_sequence_boundaries():
+    mem = _ngram()
+    tokens = torch.randint(0, 50, (1, 12), generator=torch.Generator().manual_seed(3))
+    positions = torch.cat([torch.arange(5), torch.arange(7)])[None]  # two packed sequences
+    x = torch.zeros(1, 12, 16)
+    base = mem(x, tokens, positions)
+    for t in range(11):  # changing a later token leaves every earlier output alone
+        later = tokens.clone()
+        later[0, t + 1] = (later[0, t + 1] + 7) % 50
+        torch.testing.assert_close(mem(x, later, positions)[:, :t + 1], base[:, :t + 1], atol=0, rtol=0)
+    first = tokens.clone()
+    first[0, :5] = (first[0, :5] + 11) % 50  # the first sequence is invisible to the second
+    torch.testing.assert_close(mem(x, first, positions)[:, 5:], base[:, 5:], atol=0, rtol=0)
+
+
+def test_ngram_decode_with_history_equals_full_forward():
+    mem = _ngram()
+    tokens = torch.randint(0, 50, (2, 9), generator=torch.Generator().manual_seed(5))
+    positions = torch.arange(9).expand(2, 9)
+    x = torch.randn(2, 9, 16)
+    full = mem(x, tokens, positions)
+    history = {}
+    prompt = mem(x[:, :4], tokens[:, :4], positions[:, :4], history)
+    steps = [mem(x[:, t:t + 1], tokens[:, t:t + 1], positions[:, t:t + 1], history) for t in range(4, 9)]
+    torch.testing.assert_close(torch.cat([prompt] + steps, dim=1), full, atol=1e-6, rtol=1e-6)
+
+
+def test_windowed_cosine_endpoints_clamping_and_validation():
+    base, low = 3e-4, 0.1
+    assert windowed_cosine_lr(base, low, 10, 10, 30) == pytest.approx(base)
+    assert windowed_cosine_lr(base, low, 30, 10, 30) == pytest.approx(base * low)
+    assert windowed_cosine_lr(base, low, 20, 10, 30) == pytest.approx(base * (low + (1 - low) / 2))
+    assert windowed_cosine_lr(base, low, 15, 10, 30) == pytest.approx(
+        base * (low + (1 - low) * (1 + math.cos(math.pi / 4)) / 2))
+    assert windowed_cosine_lr(base, low, 0, 10, 30) == pytest.approx(base)
+    assert windowed_cosine_lr(base, low, 99, 10, 30) == pytest.approx(base * low)
+    for start, end, ratio in ((None, 5, low), (5, 5, low), (-1, 3, low), (0, 10, 1.5), (0, 10, -0.1)):
+        with pytest.raises(ValueError):
+            windowed_cosine_lr(base, ratio, 3, start, end)
