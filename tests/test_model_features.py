@@ -126,3 +126,45 @@ def test_windowed_cosine_endpoints_clamping_and_validation():
     for start, end, ratio in ((None, 5, low), (5, 5, low), (-1, 3, low), (0, 10, 1.5), (0, 10, -0.1)):
         with pytest.raises(ValueError):
             windowed_cosine_lr(base, ratio, 3, start, end)
+
+
+def test_sequence_routes_read_only_what_their_policy_allows():
+    """Sparse MoS routing pools each packed sequence: ``prefix_mean`` reads its prompt only,
+    ``first_token`` its first token only; other sequences never leak in."""
+    from mimir_b200.models.experts import TopKRouter
+    from mimir_b200.models.mimir2 import Mimir2
+    from mimir_b200.models.sparse_stacks import sequence_routes
+    torch.manual_seed(6)
+    router = TopKRouter(8, 3, 2, init_std=0.5)
+    info = dict(numseqs=torch.tensor(2), cu_seqlens=torch.tensor([0, 6, 11]), prefix_lens=torch.tensor([2, 4]))
+    x = torch.randn(11, 8)
+    for policy, visible in (("prefix_mean", [0, 1, 6, 7, 8, 9]), ("first_token", [0, 6])):
+        base = sequence_routes(router, x, info, policy=policy)
+        for row in range(11):
+            moved = x.clone()
+            moved[row] += 3.0
+            same = torch.equal(sequence_routes(router, moved, info, policy=policy), base)
+            assert same is (row not in visible), (policy, row)
+    with pytest.raises(ValueError, match="PrefixLM"):
+        Mimir2(_cfg(mos_num_experts=2, mos_top_k=1, mos_sparse=True, mos_sparse_routing="prefix_mean",
+                    attn_type="causal"))
+
+
+def test_metadata_routing_bias_schedule_and_training_only():
+    """Category rows of the routing-logit bias decay linearly to zero over the configured step
+    window and apply in training forwards only; warm-up ramps move alpha linearly from 0 to max."""
+    from types import SimpleNamespace
+
+    from mimir_b200.models.mimir2 import Mimir2
+    model = Mimir2(_cfg(moe_num_experts=2, moe_top_k=1, moe_metadata_bias=[[0.0, 4.0], [2.0, 0.0]],
+                        routing_bias_decay_start=10, routing_bias_decay_end=30, gates_enabled=True,
+                        gate_warmup_start_step=5, gate_warmup_steps=10, gate_alpha_max=0.8))
+    model.train()
+    category = torch.tensor([1, 0, 1])
+    for step, scale, alpha in ((0, 1.0, 0.0), (10, 1.0, 0.4), (20, 0.5, 0.8), (30, 0.0, 0.8), (99, 0.0, 0.8)):
+        model.compute_train_extra_args(SimpleNamespace(step=step))
+        expected = torch.tensor([[2.0, 0.0], [0.0, 4.0], [2.0, 0.0]]) * scale
+        torch.testing.assert_close(model._metadata_bias(category, "moe"), expected)
+        assert float(model.gate_alpha) == pytest.approx(alpha), step
+    model.eval()
+    assert model._metadata_bias(category, "moe") is None
