@@ -489,6 +489,14 @@ def save_train_checkpoint(config, train_state: TrainState, tag: str, epoch: int,
                           checkpoint_kind: str = "regular", local_batch_size: int = 0,
                           resume_info: Optional[dict] = None, batch_in_epoch_exact: bool = True) -> Optional[Path]:
     """Write ``<checkpoint_path>/<tag>`` (all ranks call this); return the published directory."""
+    from mimir_b200.utils.trace import nvtx_range
+    with nvtx_range("checkpoint_save"):
+        return _save_train_checkpoint(config, train_state, tag, epoch, batch_in_epoch, rank, checkpoint_kind,
+                                      local_batch_size, resume_info, batch_in_epoch_exact)
+
+
+def _save_train_checkpoint(config, train_state, tag, epoch, batch_in_epoch, rank, checkpoint_kind, local_batch_size,
+                           resume_info, batch_in_epoch_exact):
     from mimir_b200.ckpt.contract import publish, rng_state
     if config.checkpoint_path is None:
         return None

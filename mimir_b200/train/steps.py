@@ -25,7 +25,7 @@ from torch.nn.parallel import DistributedDataParallel
 from mimir_b200.models.common import IGNORE_LABEL_ID, wrap_tensor
 from mimir_b200.optim.clipping import clip_grad_norm_mean_units
 from mimir_b200.optim.routing_balance import has_balanced_routers, routing_balance
-from mimir_b200.utils.trace import trace_print
+from mimir_b200.utils.trace import nvtx_range, trace_print
 
 
 def forward_backward_batch(train_state, batch: dict, loss_scale: Tensor, **kwargs):
@@ -109,7 +109,7 @@ def _forward_backward_all(config, rank, train_state, batches, counts, total, ste
                 model.set_requires_all_reduce(last, recurse=True)
             else:
                 model.set_requires_gradient_sync(last, recurse=True)
-        with ctx:
+        with ctx, nvtx_range(f"microbatch_{i}"):
             metrics = _add_metrics(metrics, step_fn(train_state, batch, count / total, **kwargs))
         trace_print(config, rank, f"forward_backward_end step={train_state.step} microbatch={i}")
     return metrics
@@ -191,7 +191,8 @@ def _accumulate_and_step(config, rank: int, train_state, batches: list, use_comp
         probe = ParameterUpdateProbe(model)
     if not skipped:
         trace_print(config, rank, f"optim_step_begin step={train_state.step}")
-        train_state.optim.step()
+        with nvtx_range("optimizer_step"):
+            train_state.optim.step()
         trace_print(config, rank, f"optim_step_end step={train_state.step}")
     elif getattr(model, "replicated_engine", None) is not None:
         model.replicated_engine.reduced = None
