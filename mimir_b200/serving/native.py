@@ -12,14 +12,16 @@ Endpoints (the subset the evaluation runner and the serving pool use):
 * ``GET  /health``, ``GET /v1/models``
 * ``POST /v1/chat/completions`` (``messages``; the export's chat template; ``chat_template_kwargs``)
 * ``POST /v1/completions`` (``prompt``)
+* ``"stream": true`` on either POST: server-sent events (``chat.completion.chunk`` /
+  ``text_completion`` chunks, then ``data: [DONE]``), decoded text sent as it is generated.
 
 Request fields: ``max_tokens``, ``temperature`` (0 = greedy), ``top_p``, ``stop``, ``seed``.
 The HTTP server accepts concurrent connections.  Greedy requests without a seed are batched: a
 worker thread takes what has queued up (up to ``--max-batch`` requests, waiting at most
 ``--batch-wait-ms`` after the first), left-pads the prompts into one batch (the model hides
 padding keys and counts positions from each prompt's first token) and decodes them together,
-which gives each request its own greedy continuation.  Sampled or seeded requests run one at a
-time.
+which gives each request its own greedy continuation.  Sampled, seeded or streamed requests run
+one at a time.
 
 Usage: ``python -m mimir_b200.serving.native MODEL_DIR [--port 8000] [--device cuda:0]
 [--max-batch 8] [--batch-wait-ms 5]``.
@@ -134,6 +136,49 @@ class Engine:
             out = self.model.generate(x, attention_mask=torch.ones_like(x), **gen)
         return self._finish(ids, out[0, len(ids):].tolist(), body)
 
+    def stream(self, ids: list[int], body: dict):
+        """Yield decoded text pieces as they are generated, then ``(None, result)`` where result
+        is what :meth:`complete` returns (stop strings cut the text and end the stream early)."""
+        from transformers import TextIteratorStreamer
+        temperature = float(body.get("temperature") or 0.0)
+        gen = self._gen_args(self._max_tokens(body)) | dict(do_sample=temperature > 0)
+        if temperature > 0:
+            gen.update(temperature=temperature, top_p=float(body.get("top_p") or 1.0))
+        streamer = TextIteratorStreamer(self.tokenizer, skip_prompt=True, skip_special_tokens=True)
+        holder: dict = {}
+
+        def run():
+            try:
+                with self.lock, torch.no_grad():
+                    if body.get("seed") is not None:
+                        torch.manual_seed(int(body["seed"]))
+                    x = torch.tensor([ids], device=self.device)
+                    holder["out"] = self.model.generate(x, attention_mask=torch.ones_like(x), streamer=streamer, **gen)
+            except BaseException as exc:  # reported to the reader below
+                holder["error"] = exc
+                streamer.end()
+
+        worker = threading.Thread(target=run, daemon=True)
+        worker.start()
+        stops = body.get("stop") or []
+        stops = [stops] if isinstance(stops, str) else [x for x in stops if x]
+        sent, stopped = "", False
+        for piece in streamer:
+            if stopped:
+                continue  # drain until generation ends
+            text = sent + piece
+            cut = min((text.find(x) for x in stops if x in text), default=-1)
+            if cut >= 0:
+                piece, stopped = text[len(sent):cut], True
+            if piece:
+                sent += piece
+                yield piece, None
+        worker.join()
+        if "error" in holder:
+            raise holder["error"]
+        result = self._finish(ids, holder["out"][0, len(ids):].tolist(), body)
+        yield None, (sent, result[1], result[2], "stop" if stopped else result[3])
+
     # ------------------------------------------------------------------ batched greedy decoding
     def _serve_batches(self) -> None:
         while True:
@@ -199,9 +244,9 @@ def _handler(engine: Engine):
                 chat = self.path == "/v1/chat/completions"
                 if not chat and self.path != "/v1/completions":
                     return self._send(404, {"error": {"message": f"unknown path {self.path}"}})
-                if body.get("stream"):
-                    return self._send(400, {"error": {"message": "streaming is not supported"}})
                 ids = engine.prompt_ids(body, chat)
+                if body.get("stream"):
+                    return self._stream(engine.stream(ids, body), chat)
                 text, n_in, n_out, finish = engine.complete(ids, body)
             except (KeyError, ValueError, TypeError) as exc:
                 return self._send(400, {"error": {"message": str(exc)}})
@@ -214,6 +259,38 @@ def _handler(engine: Engine):
             else:
                 self._send(200, base | {"object": "text_completion", "choices": [
                     {"index": 0, "text": text, "finish_reason": finish}]})
+        def _stream(self, pieces, chat: bool) -> None:
+            cid, created = f"cmpl-{uuid.uuid4().hex}", int(time.time())
+            kind = "chat.completion.chunk" if chat else "text_completion"
+            self.send_response(200)
+            self.send_header("Content-Type", "text/event-stream")
+            self.send_header("Cache-Control", "no-cache")
+            self.send_header("Connection", "close")
+            self.end_headers()
+            self.close_connection = True
+
+            def event(payload) -> None:
+                data = payload if isinstance(payload, str) else json.dumps(payload)
+                self.wfile.write(f"data: {data}\n\n".encode())
+                self.wfile.flush()
+
+            def chunk(text, finish=None, usage=None):
+                choice = ({"index": 0, "delta": {"content": text} if text else {}, "finish_reason": finish} if chat
+                          else {"index": 0, "text": text or "", "finish_reason": finish})
+                out = {"id": cid, "object": kind, "created": created, "model": engine.name, "choices": [choice]}
+                return out | ({"usage": usage} if usage else {})
+
+            if chat:
+                event({"id": cid, "object": kind, "created": created, "model": engine.name,
+                       "choices": [{"index": 0, "delta": {"role": "assistant"}, "finish_reason": None}]})
+            for piece, result in pieces:
+                if piece is not None:
+                    event(chunk(piece))
+                else:
+                    _, n_in, n_out, finish = result
+                    event(chunk(None, finish, {"prompt_tokens": n_in, "completion_tokens": n_out,
+                                               "total_tokens": n_in + n_out}))
+            event("[DONE]")
     return Handler
 
 

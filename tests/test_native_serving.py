@@ -29,6 +29,16 @@ def _post(url, body):
         return json.loads(r.read())
 
 
+def _stream(url, body):
+    """POST with ``stream``: the server-sent events' payloads (JSON objects, then ``[DONE]``)."""
+    req = urllib.request.Request(url, data=json.dumps(body).encode(), headers={"Content-Type": "application/json"})
+    with urllib.request.urlopen(req, timeout=60) as r:
+        assert r.headers["Content-Type"] == "text/event-stream"
+        lines = [line.decode().strip() for line in r.read().splitlines()]
+    data = [line[len("data: "):] for line in lines if line.startswith("data: ")]
+    return [d if d == "[DONE]" else json.loads(d) for d in data]
+
+
 def test_native_server_answers_like_generate(tmp_path):
     from test_transformers_model import _export
 
@@ -56,8 +66,25 @@ def test_native_server_answers_like_generate(tmp_path):
         assert chat["choices"][0]["message"]["content"] == expected
         text = _post(base + "/v1/completions", {"prompt": "w5 w6", "max_tokens": 3})
         assert text["object"] == "text_completion" and isinstance(text["choices"][0]["text"], str)
-        with pytest.raises(urllib.error.HTTPError):
-            _post(base + "/v1/completions", {"prompt": "w5", "stream": True})
+        streamed = _stream(base + "/v1/chat/completions", {"model": "tiny", "max_tokens": 4, "temperature": 0,
+                                                           "stream": True,
+                                                           "messages": [{"role": "user", "content": "w1 w2 w3"}]})
+        assert streamed[-1] == "[DONE]" and streamed[0]["choices"][0]["delta"] == {"role": "assistant"}
+        chunks = streamed[1:-1]
+        assert all(c["object"] == "chat.completion.chunk" for c in chunks)
+        assert "".join(c["choices"][0]["delta"].get("content", "") for c in chunks) == expected
+        assert chunks[-1]["choices"][0]["finish_reason"] == chat["choices"][0]["finish_reason"]
+        assert chunks[-1]["usage"] == chat["usage"]
+        plain = _stream(base + "/v1/completions", {"prompt": "w5 w6", "max_tokens": 3, "stream": True})
+        assert "".join(c["choices"][0]["text"] for c in plain[:-1]) == text["choices"][0]["text"]
+        full = text["choices"][0]["text"]
+        if len(full.split()) > 1:  # a stop string cuts the stream where it cuts the plain answer
+            stop = full.split()[1]
+            cut = _post(base + "/v1/completions", {"prompt": "w5 w6", "max_tokens": 3, "stop": [stop]})
+            streamed_cut = _stream(base + "/v1/completions", {"prompt": "w5 w6", "max_tokens": 3, "stop": [stop],
+                                                              "stream": True})
+            assert "".join(c["choices"][0]["text"] for c in streamed_cut[:-1]) == cut["choices"][0]["text"]
+            assert streamed_cut[-2]["choices"][0]["finish_reason"] == "stop"
     finally:
         server.shutdown()
         server.server_close()
