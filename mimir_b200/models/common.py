@@ -3,7 +3,6 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
-import torch
 import torch.nn.functional as F
 from torch import Tensor
 

@@ -20,7 +20,6 @@ import copy
 import re
 
 import torch
-import torch.nn.functional as F
 from torch import nn
 
 from mimir_b200 import ops

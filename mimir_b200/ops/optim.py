@@ -14,8 +14,6 @@ parameter of a group (fp32 or bf16 params/moments; fp32 EMA).
 """
 from __future__ import annotations
 
-import torch
-
 from mimir_b200.ops._ext import ext
 
 

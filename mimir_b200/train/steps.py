@@ -14,7 +14,6 @@ compatibility and uses ``torch.compile`` only when explicitly enabled).
 from __future__ import annotations
 
 from contextlib import nullcontext
-from typing import Optional
 
 import torch
 import torch.distributed as dist

@@ -1,5 +1,4 @@
 """Numerics of the sm_100a kernels against plain PyTorch fp32 references."""
-import math
 
 import pytest
 import torch

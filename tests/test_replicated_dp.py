@@ -6,10 +6,6 @@ identical data the summed gradient is exactly 2x and AdamATan2 is scale invarian
 last bit of the vectorised CPU atan2 may differ with the shard layout) and check
 that its DCP checkpoints resume exactly and load into a non-replicated model.
 """
-import copy
-import json
-import os
-import tempfile
 
 import pytest
 import torch
