@@ -191,6 +191,27 @@ class ShardedLinear(nn.Module):
             raise TypeError("the CUDA sharded projection computes in bf16")
         return _GatheredLinearFn.apply(x, self.shard, self)
 
+    # ------------------------------------------------------------------ checkpoints
+    def _save_to_state_dict(self, destination, prefix, keep_vars):
+        """Checkpoints hold the whole matrix as ``weight`` (every rank calls ``state_dict``: it
+        all-gathers), so they load at any world size."""
+        destination[prefix + "weight"] = self.full_weight()
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                              error_msgs):
+        key = prefix + "weight"
+        if key not in state_dict:
+            missing_keys.append(key)
+            return
+        full = state_dict[key]
+        if tuple(full.shape) != (self.out_features, self.in_features):
+            error_msgs.append(f"{key}: shape {tuple(full.shape)} != {(self.out_features, self.in_features)}")
+            return
+        S = self.out_features // self.world
+        with torch.no_grad():
+            self.shard.copy_(full[self.rank * S:(self.rank + 1) * S].to(self.shard.dtype))
+        self.publish()
+
     def full_weight(self) -> Tensor:
         """The whole matrix (an all-gather; for checks and export)."""
         out = torch.empty(self.out_features, self.in_features, dtype=self.shard.dtype, device=self.device)

@@ -321,3 +321,27 @@ def test_bf16_gradient_accumulation_drift_is_bounded():
     drift = (engine.grads.float() - exact).abs().max() / exact.abs().max()
     assert drift <= 3 * 2.0 ** -8, float(drift)
     engine.close()
+
+
+def _sharded_ckpt_worker(rank, world, init, out):
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
+    try:
+        from mimir_b200.parallel.sharded_linear import ShardedLinear
+        torch.manual_seed(0)
+        w = torch.randn(8, 6)
+        layer = ShardedLinear(w, device="cpu")
+        state = layer.state_dict()
+        assert list(state) == ["weight"] and torch.equal(state["weight"], w)
+        other = ShardedLinear(torch.zeros(8, 6), device="cpu")
+        other.load_state_dict({"weight": w * 2})
+        torch.save(other.shard.detach().clone(), f"{out}.{rank}.pt")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_linear_checkpoints_hold_the_whole_matrix(tmp_path):
+    mp.spawn(_sharded_ckpt_worker, args=(2, f"file://{tmp_path / 'init'}", str(tmp_path / "c")), nprocs=2, join=True)
+    torch.manual_seed(0)
+    w = torch.randn(8, 6)
+    for rank in range(2):
+        assert torch.equal(torch.load(f"{tmp_path / 'c'}.{rank}.pt"), 2 * w[rank * 4:(rank + 1) * 4])
