@@ -145,7 +145,8 @@ def parser() -> argparse.ArgumentParser:
     sv.add_argument("--port", type=int, default=8000)
     sv.add_argument("--gpus", required=True)
     sv.add_argument("--eager", action="store_true")
-    sv.add_argument("--backend", choices=("vllm", "native"), default="vllm")
+    sv.add_argument("--backend", choices=("auto", "vllm", "native"), default="auto",
+                    help="auto: vLLM when it registers Mimir2, else the native server")
     sv.set_defaults(fn=_serve)
     ev = sub.add_parser("eval")
     ev.add_argument("suite", type=Path)

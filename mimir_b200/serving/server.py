@@ -8,6 +8,9 @@ Reference behaviour: ``src/mimir/serving/server.py:12-75``.
   ``backend="native"`` launches :mod:`mimir_b200.serving.native` instead (this framework's
   Transformers model behind an OpenAI-compatible endpoint, one GPU): it serves every exported
   configuration, looped recurrence included, with the prompt as the prefix-LM prefix.
+  ``backend="auto"`` (the default) takes vLLM when the installed vLLM registers the Mimir2
+  architecture (the reference's patched fork does; stock vLLM does not) and the native server
+  otherwise.
 * ``ServerPool`` keys servers by SHA-256 of the export receipt, the chat template and the
   spec, so a server is reused only for an identical model/template/launch; it owns each
   server's process group and tears it down (TERM, then KILL after 30 s).
@@ -35,7 +38,7 @@ class ServerSpec:
     eager: bool = False
     max_model_len: Optional[int] = None
     template: Optional[str] = None
-    backend: str = "vllm"  # or "native"
+    backend: str = "auto"  # "vllm", "native", or "auto": vLLM when it knows Mimir2
 
     def key(self) -> str:
         receipt = (Path(self.model) / "export_receipt.json").read_bytes()
@@ -43,18 +46,30 @@ class ServerSpec:
         return hashlib.sha256(receipt + template + json.dumps(asdict(self), sort_keys=True).encode()).hexdigest()
 
 
+def vllm_knows_mimir2() -> bool:
+    """True when the installed vLLM registers ``Mimir2ForCausalLM``."""
+    try:
+        from vllm import ModelRegistry
+        return "Mimir2ForCausalLM" in ModelRegistry.get_supported_archs()
+    except Exception:  # vLLM missing or unusable here
+        return False
+
+
 def command(spec: ServerSpec) -> list[str]:
     cfg = json.loads((Path(spec.model) / "config.json").read_text())
     if cfg.get("model_type") != "mimir2":
         raise ValueError("Only Mimir2 can be served")
-    if spec.backend == "native":
+    backend = spec.backend
+    if backend == "auto":
+        backend = "vllm" if vllm_knows_mimir2() else "native"
+    if backend == "native":
         if not spec.gpus or len(spec.gpus.split(",")) != 1 or not spec.gpus.isdigit():
             raise ValueError("The native server runs on exactly one explicit GPU index")
         # CUDA_VISIBLE_DEVICES (set by the launcher) makes the chosen GPU cuda:0.
         return [sys.executable, "-m", "mimir_b200.serving.native", spec.model, "--host", "127.0.0.1",
                 "--port", str(spec.port), "--device", "cuda:0", "--dtype", "bfloat16"]
-    if spec.backend != "vllm":
-        raise ValueError(f"unknown serving backend {spec.backend!r}")
+    if backend != "vllm":
+        raise ValueError(f"unknown serving backend {backend!r}")
     if cfg.get("recurrence_mode", "hierarchical") != "hierarchical":
         raise ValueError("Looped recurrence is not supported by the inference integrations")
     if cfg.get("h_residual_persistence") or cfg.get("h_branch_l_mixing"):
@@ -74,7 +89,7 @@ def command(spec: ServerSpec) -> list[str]:
     return args
 
 
-def serve(model, port: int, gpus: str, *, eager: bool = False, backend: str = "vllm") -> None:
+def serve(model, port: int, gpus: str, *, eager: bool = False, backend: str = "auto") -> None:
     spec = ServerSpec(str(model), gpus, port, eager, backend=backend)
     subprocess.run(command(spec), env=os.environ | {"CUDA_VISIBLE_DEVICES": gpus}, check=True)
 

@@ -98,7 +98,17 @@ def test_native_backend_command(tmp_path):
     with pytest.raises(ValueError, match="exactly one"):
         command(ServerSpec(str(tmp_path), "0,1", backend="native"))
     with pytest.raises(ValueError, match="Looped"):  # the vLLM command keeps its own limits
-        command(ServerSpec(str(tmp_path), "0"))
+        command(ServerSpec(str(tmp_path), "0", backend="vllm"))
+    import mimir_b200.serving.server as server
+    original = server.vllm_knows_mimir2
+    try:  # auto: native unless vLLM registers the architecture
+        server.vllm_knows_mimir2 = lambda: False
+        assert command(ServerSpec(str(tmp_path), "2"))[1:3] == ["-m", "mimir_b200.serving.native"]
+        server.vllm_knows_mimir2 = lambda: True
+        with pytest.raises(ValueError, match="Looped"):
+            command(ServerSpec(str(tmp_path), "2"))
+    finally:
+        server.vllm_knows_mimir2 = original
 
 
 def test_concurrent_greedy_requests_are_batched_and_match_single_requests(tmp_path):

@@ -254,15 +254,15 @@ def test_server_compatibility_includes_template_contents(tmp_path):
     (tmp_path / "config.json").write_text(json.dumps({"model_type": "mimir2", "mos_sparse": True}))
     template = tmp_path / "chat.jinja"
     template.write_text("first")
-    spec = ServerSpec(str(tmp_path), "0", template=str(template))
+    spec = ServerSpec(str(tmp_path), "0", template=str(template), backend="vllm")
     before = spec.key()
     template.write_text("second")
     assert spec.key() != before
     with pytest.raises(ValueError, match="eager"):
         command(spec)
-    assert "--enforce-eager" in command(ServerSpec(str(tmp_path), "0", eager=True))
+    assert "--enforce-eager" in command(ServerSpec(str(tmp_path), "0", eager=True, backend="vllm"))
     with pytest.raises(ValueError, match="GPU indices"):
-        command(ServerSpec(str(tmp_path), "a", eager=True))
+        command(ServerSpec(str(tmp_path), "a", eager=True, backend="vllm"))
 
 
 def test_server_pool_reuses_and_owns_processes(tmp_path):
