@@ -168,3 +168,42 @@ def test_metadata_routing_bias_schedule_and_training_only():
         assert float(model.gate_alpha) == pytest.approx(alpha), step
     model.eval()
     assert model._metadata_bias(category, "moe") is None
+
+
+@pytest.mark.parametrize("changes,message", [
+    (dict(moe_aux_loss_free=True), "MoE balancing requires multiple MoE experts"),
+    (dict(H_override={"n_layers": 0}), "Zero-layer H requires looped recurrence"),
+    (dict(h_residual_persistence=True), "H stream options require hierarchical recurrence"),
+    (dict(h_branch_l_mixing=True, residual_branches=2, residual_levels="H"), "Branch-specific L mixing requires MoS"),
+    (dict(recurrence_mode="looped", gates_enabled=True), "Looped recurrence requires shared MoS state"),
+    (dict(moe_num_experts=2, moe_metadata_bias=[[0.0]]), "Metadata bias rows must contain one finite logit"),
+    (dict(routing_bias_decay_start=5, routing_bias_decay_end=5), "Routing bias decay end must follow start"),
+    (dict(moe_num_experts=2, specialist_training=True), "Specialist training requires a frozen reference expert"),
+    (dict(moe_num_experts=2, moe_dispatch="grouped"), "need moe_sparse with several experts"),
+    (dict(moe_num_experts=2, moe_top_k=3), "Expert top_k must not exceed num_experts"),
+    (dict(residual_branches=2, norm_type="post"), "Multiple residual branches currently require pre-norm"),
+    (dict(expert_freeze_base=True), "expert_freeze_base requires an expert mixture"),
+    (dict(gate_initialize_from_v1=True), "gate_initialize_from_v1 requires gates_enabled=true"),
+])
+def test_invalid_feature_combinations_are_rejected(changes, message):
+    from mimir_b200.models.mimir2 import Mimir2
+    with pytest.raises(ValueError, match=message):
+        Mimir2(_cfg(**changes))
+
+
+def test_frozen_base_expert_takes_no_gradient():
+    """A frozen reference expert (``expert_freeze_base``) and its router row receive no parameter
+    gradient while the other experts and the backbone train."""
+    from mimir_b200.models import LMHead, Mimir2
+    c = _cfg(moe_num_experts=3, moe_top_k=2, expert_freeze_base=True)
+    torch.manual_seed(0)
+    model = LMHead(Mimir2(c), c)
+    _, loss, _ = model(None, _batch(), bp_steps=3)
+    loss.backward()
+    grads = {n: p.grad for n, p in model.named_parameters()}
+    frozen = [n for n, p in model.named_parameters() if not p.requires_grad]
+    assert frozen and all(grads[n] is None for n in frozen)
+    assert any(".experts.0." in n for n in frozen) and any("rows.0" in n for n in frozen)
+    trained = [n for n in grads if n not in frozen and grads[n] is not None]
+    assert any(".experts.1." in n for n in trained)
+    assert any("embed" in n for n in trained)
