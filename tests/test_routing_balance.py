@@ -66,3 +66,27 @@ def test_bias_stays_fp32_under_precision_changes():
     assert r.selection_bias.dtype == torch.float32
     assert r.rows[0].dtype == torch.bfloat16
     assert torch.equal(r.selection_bias, torch.full((4,), 0.125))
+
+
+def test_top1_router_gradient_comes_only_from_the_straight_through_surrogate():
+    """With one expert per token the mixing weight is exactly 1: the router learns only through
+    the straight-through surrogate (on by default) and gets a zero gradient without it."""
+    x = torch.randn(9, 8)
+    for straight_through in (True, False):
+        torch.manual_seed(0)
+        r = TopKRouter(8, 4, 1, top1_straight_through=straight_through, init_std=0.5)
+        w = r(x)
+        assert torch.equal(w.detach().sum(-1), torch.ones(9))
+        (w * torch.randn(9, 4, generator=torch.Generator().manual_seed(1))).sum().backward()
+        moved = any(bool(p.grad.any()) for p in r.rows if p.grad is not None)
+        assert moved is straight_through
+
+
+def test_selection_bias_is_checkpointed():
+    r = _router()
+    r.selection_bias.copy_(torch.tensor([0.5, -0.25, 0.0, 1.0]))
+    state = r.state_dict()
+    assert torch.equal(state["selection_bias"], r.selection_bias)
+    fresh = _router()
+    fresh.load_state_dict(state)
+    assert torch.equal(fresh.selection_bias, r.selection_bias)
