@@ -207,3 +207,28 @@ def test_frozen_base_expert_takes_no_gradient():
     trained = [n for n in grads if n not in frozen and grads[n] is not None]
     assert any(".experts.1." in n for n in trained)
     assert any("embed" in n for n in trained)
+
+
+def test_residual_branches_add_no_sublayer_calls():
+    """Residual branches mix the streams around each sublayer; the attention and MLP sublayers run
+    as often as in the single-stream model."""
+    from mimir_b200.models import LMHead, Mimir2
+    from mimir_b200.models.transformer import Attention
+    from mimir_b200.models.layers import SwiGLU
+
+    def calls(**kw):
+        c = _cfg(**kw)
+        torch.manual_seed(0)
+        model = LMHead(Mimir2(c), c)
+        seen = {"attn": 0, "mlp": 0}
+        for m in model.modules():
+            if isinstance(m, (Attention, SwiGLU)):
+                key = "attn" if isinstance(m, Attention) else "mlp"
+                m.register_forward_hook(lambda *_, key=key: seen.__setitem__(key, seen[key] + 1))
+        model(None, _batch(), bp_steps=3)
+        return seen
+
+    single = calls()
+    assert single["attn"] > 0 and single["mlp"] > 0
+    assert calls(residual_branches=2) == single
+    assert calls(residual_branches=3, residual_levels="H") == single
