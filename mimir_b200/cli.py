@@ -98,7 +98,30 @@ def _doctor(_args, _rest):
         out["mimir_b200._host"] = "built"
     except ImportError:
         out["mimir_b200._host"] = "missing"
+    out["gpus"] = _nvml_gpus()
     print(json.dumps(out, indent=2))
+
+
+def _nvml_gpus():
+    """GPUs as NVML reports them (read-only queries; no CUDA context): name, memory, compute
+    capability and whether it is the sm_100 part the kernels are built for."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+    except Exception as exc:  # no driver here (a CPU box) or no NVML bindings
+        return f"unavailable ({type(exc).__name__})"
+    try:
+        gpus = []
+        for i in range(pynvml.nvmlDeviceGetCount()):
+            h = pynvml.nvmlDeviceGetHandleByIndex(i)
+            name = pynvml.nvmlDeviceGetName(h)
+            major, minor = pynvml.nvmlDeviceGetCudaComputeCapability(h)
+            gpus.append({"index": i, "name": name.decode() if isinstance(name, bytes) else name,
+                         "memory_mib": pynvml.nvmlDeviceGetMemoryInfo(h).total // (1 << 20),
+                         "compute_capability": f"{major}.{minor}", "kernels_supported": (major, minor) == (10, 0)})
+        return gpus
+    finally:
+        pynvml.nvmlShutdown()
 
 
 def _campaign(args, _rest) -> None:

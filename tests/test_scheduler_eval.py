@@ -304,3 +304,24 @@ def test_cli_doctor_and_schedule(tmp_path, capsys):
     assert [r["id"] for r in rows] == ["a", "b"] and rows[0]["held"] == 1
     with pytest.raises(SystemExit):
         main(["export", "x"])
+
+
+def test_doctor_lists_gpus_through_nvml(monkeypatch):
+    """``mimir doctor`` reads GPUs through NVML only (a fake here): name, memory, capability."""
+    import types
+
+    from mimir_b200.cli import _nvml_gpus
+
+    class Mem:
+        total = 183359 << 20
+
+    fake = types.SimpleNamespace(
+        nvmlInit=lambda: None, nvmlShutdown=lambda: None, nvmlDeviceGetCount=lambda: 2,
+        nvmlDeviceGetHandleByIndex=lambda i: i, nvmlDeviceGetName=lambda h: b"NVIDIA B200",
+        nvmlDeviceGetCudaComputeCapability=lambda h: (10, 0) if h == 0 else (9, 0),
+        nvmlDeviceGetMemoryInfo=lambda h: Mem())
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    gpus = _nvml_gpus()
+    assert gpus[0] == {"index": 0, "name": "NVIDIA B200", "memory_mib": 183359, "compute_capability": "10.0",
+                       "kernels_supported": True}
+    assert gpus[1]["kernels_supported"] is False
