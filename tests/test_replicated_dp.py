@@ -345,3 +345,33 @@ def test_sharded_linear_checkpoints_hold_the_whole_matrix(tmp_path):
     w = torch.randn(8, 6)
     for rank in range(2):
         assert torch.equal(torch.load(f"{tmp_path / 'c'}.{rank}.pt"), 2 * w[rank * 4:(rank + 1) * 4])
+
+
+@pytest.mark.parametrize("N,K,world,rank,pairs", [(5120, 2048, 8, 3, 74), (11264, 2048, 8, 0, 74), (2048, 5632, 2, 1, 74),
+                                                  (1024, 136, 4, 2, 7), (65536, 2048, 8, 7, 74), (256, 64, 1, 0, 3)])
+def test_allgather_gemm_work_split_covers_every_block_once(N, K, world, rank, pairs):
+    """The index arithmetic of ``gemm_gather_kernel`` (``csrc/gemm.cu``), restated on the host:
+    the gatherers' items cover every (128-row block, k-block) of the weight exactly once, each
+    row block's counter grows by ``parts`` per call, and the tile order visits every output tile
+    once starting at this rank's own columns."""
+    nkb, blocks = (K + 63) // 64, N // 128
+    parts = max(1, min(nkb, (2 * pairs + blocks - 1) // blocks))
+    shard_rows, per_rank = N // world, N // world // 128
+    items = world * per_rank * parts
+    seen, counters = {}, [0] * blocks
+    for cid in range(pairs):
+        for item in range(cid, items, pairs):
+            owner = (rank + 1 + (item // parts) // per_rank) % world
+            grow = owner * shard_rows + ((item // parts) % per_rank) * 128
+            lo, hi = ((item % parts) * nkb) // parts, ((item % parts + 1) * nkb) // parts
+            assert hi > lo
+            for kb in range(lo, hi):
+                assert (grow, kb) not in seen
+                seen[(grow, kb)] = cid
+            counters[grow // 128] += 1
+    assert len(seen) == blocks * nkb and counters == [parts] * blocks
+    tiles_m, tiles_n = 3, N // 256
+    order = [((t % tiles_m), (t // tiles_m + (rank * shard_rows) // 256) % tiles_n) for t in range(tiles_m * tiles_n)]
+    assert len(set(order)) == tiles_m * tiles_n
+    first_rows = order[0][1] * 256
+    assert first_rows <= rank * shard_rows < first_rows + 256  # the first column holds this rank's first row
