@@ -107,7 +107,9 @@ def main():
         nvlink = N * K * 2 * (world - 1) / world
         roof = max(flops / (tflops * 1e12), nvlink / (NVLINK_GBS * 1e9)) * 1e3
         out.update(roofline_ms=round(roof, 4), fused_frac_of_roofline=round(roof / out["fused_ms"], 3),
-                   fused_vs_nccl=round(out["nccl_ms"] / out["fused_ms"], 3))
+                   fused_vs_nccl=round(out["nccl_ms"] / out["fused_ms"], 3),
+                   fused_tflops=round(flops / out["fused_ms"] / 1e9, 1),
+                   nvlink_gbs_min_per_direction=round(nvlink / out["fused_ms"] / 1e6, 1))
         rows.append(out)
         layer.close()
     torch.cuda.synchronize()
