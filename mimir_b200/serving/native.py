@@ -16,12 +16,13 @@ Endpoints (the subset the evaluation runner and the serving pool use):
   ``text_completion`` chunks, then ``data: [DONE]``), decoded text sent as it is generated.
 
 Request fields: ``max_tokens``, ``temperature`` (0 = greedy), ``top_p``, ``stop``, ``seed``.
-The HTTP server accepts concurrent connections.  Greedy requests without a seed are batched: a
-worker thread takes what has queued up (up to ``--max-batch`` requests, waiting at most
-``--batch-wait-ms`` after the first), left-pads the prompts into one batch (the model hides
-padding keys and counts positions from each prompt's first token) and decodes them together,
-which gives each request its own greedy continuation.  Sampled, seeded or streamed requests run
-one at a time.
+The HTTP server accepts concurrent connections.  Requests without a seed are batched: a worker
+thread takes what has queued up with the same decoding rule (greedy, or one temperature/top-p;
+up to ``--max-batch`` requests, waiting at most ``--batch-wait-ms`` after the first), left-pads
+the prompts into one batch (the model hides padding keys and counts positions from each prompt's
+first token) and decodes them together, which gives each greedy request its own greedy
+continuation and each sampled request independent samples.  Seeded or streamed requests run one
+at a time.
 
 Usage: ``python -m mimir_b200.serving.native MODEL_DIR [--port 8000] [--device cuda:0]
 [--max-batch 8] [--batch-wait-ms 5]``.
@@ -112,7 +113,13 @@ class Engine:
         return text, len(ids), len(new), finish
 
     def batchable(self, body: dict) -> bool:
-        return self.max_batch > 1 and not float(body.get("temperature") or 0.0) > 0 and body.get("seed") is None
+        return self.max_batch > 1 and body.get("seed") is None
+
+    @staticmethod
+    def _sampling(body: dict) -> tuple:
+        """Requests share a batch only with the same decoding rule (greedy, or one temperature/top-p)."""
+        temperature = float(body.get("temperature") or 0.0)
+        return (temperature, float(body.get("top_p") or 1.0)) if temperature > 0 else (0.0, 1.0)
 
     @torch.no_grad()
     def complete(self, ids: list[int], body: dict) -> tuple[str, int, int, str]:
@@ -185,11 +192,17 @@ class Engine:
             with self._ready:
                 while not self._queue:
                     self._ready.wait()
+                rule = self._sampling(self._queue[0].body)
+
+                def same():
+                    return [item for item in self._queue if self._sampling(item.body) == rule][:self.max_batch]
+
                 deadline = time.monotonic() + self.batch_wait
-                while len(self._queue) < self.max_batch and time.monotonic() < deadline:
+                while len(same()) < self.max_batch and time.monotonic() < deadline:
                     self._ready.wait(max(0.0, deadline - time.monotonic()))
-                batch = self._queue[:self.max_batch]
-                del self._queue[:len(batch)]
+                batch = same()
+                taken = {id(item) for item in batch}
+                self._queue = [item for item in self._queue if id(item) not in taken]
             try:
                 for item, result in zip(batch, self._generate_batch(batch)):
                     item.result = result
@@ -208,7 +221,10 @@ class Engine:
         for i, item in enumerate(batch):
             x[i, width - len(item.ids):] = torch.tensor(item.ids)
             mask[i, width - len(item.ids):] = 1
-        gen = self._gen_args(max(self._max_tokens(item.body) for item in batch)) | dict(do_sample=False)
+        temperature, top_p = self._sampling(batch[0].body)
+        gen = self._gen_args(max(self._max_tokens(item.body) for item in batch)) | dict(do_sample=temperature > 0)
+        if temperature > 0:
+            gen.update(temperature=temperature, top_p=top_p)
         with self.lock:
             out = self.model.generate(x.to(self.device), attention_mask=mask.to(self.device), **gen)
         return [self._finish(item.ids, out[i, width:].tolist(), item.body) for i, item in enumerate(batch)]

@@ -138,3 +138,33 @@ def test_concurrent_greedy_requests_are_batched_and_match_single_requests(tmp_pa
     for body, got in zip(bodies, results):
         assert got == single.complete(single.prompt_ids(body, chat=True), body), (body, got)
         assert got[2] <= body["max_tokens"]
+
+
+def test_batches_never_mix_decoding_rules(tmp_path):
+    from test_transformers_model import _export
+
+    from mimir_b200.serving.native import Engine
+    _export(tmp_path, {})
+    _tokenizer(tmp_path)
+    engine = Engine(tmp_path, "cpu", name="tiny", max_batch=4, batch_wait_ms=200)
+    single = Engine(tmp_path, "cpu", name="tiny", max_batch=1)
+    rules = []
+    real = engine._generate_batch
+    engine._generate_batch = lambda batch: (rules.append({engine._sampling(i.body) for i in batch}), real(batch))[1]
+    bodies = [{"prompt": f"w{i} w{i + 1}", "max_tokens": 4, "temperature": t}
+              for i, t in enumerate((0, 0.8, 0, 0.8, 0))]
+    results = [None] * len(bodies)
+
+    def ask(i):
+        results[i] = engine.complete(engine.prompt_ids(bodies[i], chat=False), bodies[i])
+
+    threads = [threading.Thread(target=ask, args=(i,)) for i in range(len(bodies))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    assert rules and all(len(r) == 1 for r in rules) and len(rules) < len(bodies), rules
+    for body, got in zip(bodies, results):
+        assert got is not None and got[2] <= body["max_tokens"]
+        if body["temperature"] == 0:
+            assert got == single.complete(single.prompt_ids(body, chat=False), body)
