@@ -232,3 +232,21 @@ def test_residual_branches_add_no_sublayer_calls():
     assert single["attn"] > 0 and single["mlp"] > 0
     assert calls(residual_branches=2) == single
     assert calls(residual_branches=3, residual_levels="H") == single
+
+
+@pytest.mark.parametrize("levels,branched", [("both", {"L", "H"}), ("H", {"H"}), ("L", {"L"})])
+def test_residual_branch_levels_and_alpha_ramp(levels, branched):
+    """``residual_levels`` picks which stacks get branched residual streams, and their mixing
+    alpha ramps linearly from 0 to ``residual_alpha_max`` over the warm-up window."""
+    from types import SimpleNamespace
+
+    from mimir_b200.models.branches import BranchedTransformer
+    from mimir_b200.models.mimir2 import Mimir2
+    model = Mimir2(_cfg(residual_branches=2, residual_levels=levels, residual_alpha_max=0.6,
+                        residual_warmup_start_step=4, residual_warmup_steps=8))
+    found = {name for name in ("L", "H") if isinstance(getattr(model, f"{name}_level").core, BranchedTransformer)}
+    assert found == branched
+    for step, alpha in ((0, 0.0), (4, 0.0), (8, 0.3), (12, 0.6), (50, 0.6)):
+        model.compute_train_extra_args(SimpleNamespace(step=step))
+        values = [float(m.residual_alpha) for m in model.modules() if isinstance(m, BranchedTransformer)]
+        assert values and all(v == pytest.approx(alpha) for v in values), (step, values)
