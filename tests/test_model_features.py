@@ -250,3 +250,26 @@ def test_residual_branch_levels_and_alpha_ramp(levels, branched):
         model.compute_train_extra_args(SimpleNamespace(step=step))
         values = [float(m.residual_alpha) for m in model.modules() if isinstance(m, BranchedTransformer)]
         assert values and all(v == pytest.approx(alpha) for v in values), (step, values)
+
+
+def test_model_yaml_defaults_equal_the_schema_defaults():
+    """Every feature key of ``conf/model/mimir2.yaml`` carries the schema's default value, so a run
+    without overrides is the plain backbone whichever way it is configured."""
+    from pathlib import Path
+
+    import yaml
+
+    import mimir_b200
+    from mimir_b200.models.mimir2 import Mimir2Config
+    conf = yaml.safe_load((Path(mimir_b200.__file__).parent / "conf" / "model" / "mimir2.yaml").read_text())
+    fields = Mimir2Config.model_fields
+    checked = 0
+    for key, value in conf.items():
+        if key in fields and not fields[key].is_required():
+            default = fields[key].get_default(call_default_factory=True)
+            if key in ("H_cycles", "L_cycles", "half_layers", "bp_min_steps", "bp_max_steps", "bp_warmup_ratio",
+                       "recurrence_mode", "H_override"):
+                continue  # architecture of the preset, not an opt-in feature
+            assert value == default, (key, value, default)
+            checked += 1
+    assert checked > 20
